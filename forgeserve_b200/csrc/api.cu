@@ -1,0 +1,200 @@
+// The C ABI (include/forgeserve_b200.h): argument checks, dispatch, error strings, launch counting.
+#include <atomic>
+#include <string>
+
+#include "../../include/forgeserve_b200.h"
+#include "common.cuh"
+#include "gemm.h"
+#include "kernels.h"
+
+namespace fs {
+
+static thread_local std::string t_last_error;
+static std::atomic<int64_t> g_launches{0};
+
+void set_last_error(const std::string& msg) { t_last_error = msg; }
+int fail(const std::string& msg) {
+  set_last_error(msg);
+  return -1;
+}
+int check_launch(const char* what) {
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return fail(std::string(what) + ": " + cudaGetErrorString(e));
+  g_launches.fetch_add(1, std::memory_order_relaxed);
+  return 0;
+}
+
+static KVCache to_internal(const fs_kv_cache* c) {
+  KVCache k;
+  k.k = c->k;
+  k.v = c->v;
+  k.table = c->table;
+  k.table_stride = c->table_stride;
+  k.table_cols = c->table_cols;
+  k.block_size = c->block_size;
+  k.block_stride = c->block_stride;
+  k.head_stride = c->head_stride;
+  k.num_blocks = c->num_blocks;
+  return k;
+}
+
+static int check_kv(const fs_kv_cache* c) {
+  if (!c) return fail("kv cache descriptor is NULL");
+  if (!c->k || !c->v || !c->table) return fail("kv cache: NULL pointer");
+  if (c->block_size <= 0 || c->num_blocks <= 0 || c->table_cols <= 0) return fail("kv cache: empty cache");
+  return 0;
+}
+
+static bool dtype_ok(int dtype) { return dtype == F32 || dtype == BF16; }
+
+unsigned* error_word() {
+  static unsigned* words[64] = {nullptr};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) {
+    fail("error_word: no current CUDA device");
+    return nullptr;
+  }
+  if (!words[dev]) {
+    unsigned* p = nullptr;
+    if (cudaMalloc(&p, sizeof(unsigned)) != cudaSuccess || cudaMemset(p, 0, sizeof(unsigned)) != cudaSuccess) {
+      fail("error_word: cudaMalloc failed");
+      return nullptr;
+    }
+    words[dev] = p;
+  }
+  return words[dev];
+}
+
+}  // namespace fs
+
+using namespace fs;
+
+extern "C" {
+
+int fs_version(void) { return 100; }
+
+const char* fs_last_error(void) { return t_last_error.c_str(); }
+
+int fs_device_error(int clear, unsigned* out_bits) {
+  unsigned bits = 0;
+  unsigned* word = error_word();
+  if (!word) return -1;
+  cudaError_t e = cudaDeviceSynchronize();
+  if (e != cudaSuccess) return fail(std::string("fs_device_error: ") + cudaGetErrorString(e));
+  e = cudaMemcpy(&bits, word, sizeof(bits), cudaMemcpyDeviceToHost);
+  if (e != cudaSuccess) return fail(std::string("fs_device_error: ") + cudaGetErrorString(e));
+  if (clear) {
+    e = cudaMemset(word, 0, sizeof(unsigned));
+    if (e != cudaSuccess) return fail(std::string("fs_device_error: ") + cudaGetErrorString(e));
+  }
+  if (out_bits) *out_bits = bits;
+  return 0;
+}
+
+int64_t fs_launch_count(void) { return g_launches.load(std::memory_order_relaxed); }
+
+int fs_rmsnorm(const void* x, int64_t x_stride, const void* w, void* y, int64_t y_stride, int64_t rows, int64_t dim,
+               float eps, int dtype, void* stream) {
+  if (!x || !w || !y) return rows <= 0 ? 0 : fail("fs_rmsnorm: NULL pointer");
+  if (x_stride < dim || y_stride < dim) return fail("fs_rmsnorm: row stride smaller than dim");
+  return rmsnorm(dtype, x, x_stride, w, y, y_stride, rows, dim, eps, static_cast<cudaStream_t>(stream));
+}
+
+static int gemm_common(bool allow_tc, const void* A, int64_t lda, const void* B, int64_t ldb, void* C, int64_t ldc,
+                       const void* R, int64_t ldr, int64_t M, int64_t N, int64_t K, int64_t n_out, int epi, int dtype,
+                       void* stream) {
+  if (M <= 0 || n_out <= 0) return 0;
+  if (!A || !B || !C) return fail("fs_gemm: NULL pointer");
+  if (!dtype_ok(dtype)) return fail("fs_gemm: unsupported dtype");
+  if (K <= 0 || N <= 0) return fail("fs_gemm: K and N must be positive");
+  if (lda < K || ldb < K) return fail("fs_gemm: row stride smaller than K");
+  if (epi == EPI_RESIDUAL && !R) return fail("fs_gemm: residual epilogue needs R");
+  if (epi == EPI_SWIGLU) {
+    if (N != 2 * n_out) return fail("fs_gemm: swiglu weight [W_gate; W_up] must have 2 * n_out rows");
+  } else if (epi == EPI_STORE || epi == EPI_RESIDUAL) {
+    if (n_out != N) return fail("fs_gemm: n_out must equal N");
+  } else {
+    return fail("fs_gemm: unknown epilogue");
+  }
+  if (ldc < n_out || (epi == EPI_RESIDUAL && ldr < n_out)) return fail("fs_gemm: output row stride too small");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (allow_tc && dtype == BF16 && tcg::supported(A, lda, B, ldb, K))
+    return tcg::gemm_tc(A, lda, B, ldb, C, ldc, R, ldr, M, N, K, n_out, epi, st);
+  return gemm_simt(dtype, A, lda, B, ldb, C, ldc, R, ldr, M, N, K, n_out, epi, st);
+}
+
+int fs_gemm(const void* A, int64_t lda, const void* B, int64_t ldb, void* C, int64_t ldc, const void* R, int64_t ldr,
+            int64_t M, int64_t N, int64_t K, int64_t n_out, int epilogue, int dtype, void* stream) {
+  return gemm_common(true, A, lda, B, ldb, C, ldc, R, ldr, M, N, K, n_out, epilogue, dtype, stream);
+}
+
+int fs_gemm_simt(const void* A, int64_t lda, const void* B, int64_t ldb, void* C, int64_t ldc, const void* R,
+                 int64_t ldr, int64_t M, int64_t N, int64_t K, int64_t n_out, int epilogue, int dtype, void* stream) {
+  return gemm_common(false, A, lda, B, ldb, C, ldc, R, ldr, M, N, K, n_out, epilogue, dtype, stream);
+}
+
+int fs_rope_kv_write(void* qkv, int64_t ld, const float* cos_t, const float* sin_t, int64_t rope_rows,
+                     const int64_t* positions, const fs_kv_cache* kv, int64_t B, int64_t T, int64_t nh, int64_t nkv,
+                     int64_t hd, int64_t slot_base, int slot_from_pos, int apply_rope, int dtype, void* stream) {
+  if (B * T <= 0) return 0;
+  if (check_kv(kv)) return -1;
+  if (!qkv || !positions || (apply_rope && (!cos_t || !sin_t))) return fail("fs_rope_kv_write: NULL pointer");
+  if (ld < (nh + 2 * nkv) * hd) return fail("fs_rope_kv_write: qkv row stride too small");
+  return rope_kv_write(dtype, qkv, ld, cos_t, sin_t, rope_rows, positions, to_internal(kv), B, T, nh, nkv, hd, slot_base,
+                       slot_from_pos, apply_rope, static_cast<cudaStream_t>(stream));
+}
+
+int fs_kv_store(const void* k, const void* v, const int64_t* positions, const fs_kv_cache* kv, int64_t B, int64_t T,
+                int64_t nkv, int64_t hd, int dtype, void* stream) {
+  if (B * T <= 0) return 0;
+  if (check_kv(kv)) return -1;
+  if (!k || !v || !positions) return fail("fs_kv_store: NULL pointer");
+  return kv_store(dtype, k, v, positions, to_internal(kv), B, T, nkv, hd, static_cast<cudaStream_t>(stream));
+}
+
+int fs_paged_gather(const void* pool, const int64_t* table, int64_t B, int64_t nb, int64_t num_blocks, int64_t nkv,
+                    int64_t block_size, int64_t hd, void* out, int dtype, void* stream) {
+  if (B * nb <= 0) return 0;
+  if (!pool || !table || !out) return fail("fs_paged_gather: NULL pointer");
+  return paged_gather(dtype, pool, table, B, nb, num_blocks, nkv, block_size, hd, out, static_cast<cudaStream_t>(stream));
+}
+
+static int attention_common(int force_generic, const void* q, int64_t ldq, const fs_kv_cache* kv, int64_t n_slots,
+                            const int64_t* positions, void* out, int64_t ldo, int64_t B, int64_t T, int64_t nh,
+                            int64_t nkv, int64_t hd, float scale, int dtype, void* stream) {
+  if (B * T <= 0) return 0;
+  if (check_kv(kv)) return -1;
+  if (!q || !positions || !out) return fail("fs_attention: NULL pointer");
+  if (n_slots <= 0) return fail("fs_attention: the cache view has no slots");
+  if (ldq < nh * hd || ldo < nh * hd) return fail("fs_attention: row stride too small");
+  return attention(dtype, q, ldq, to_internal(kv), n_slots, positions, out, ldo, B, T, nh, nkv, hd, scale,
+                   force_generic, static_cast<cudaStream_t>(stream));
+}
+
+int fs_attention(const void* q, int64_t ldq, const fs_kv_cache* kv, int64_t n_slots, const int64_t* positions,
+                 void* out, int64_t ldo, int64_t B, int64_t T, int64_t nh, int64_t nkv, int64_t hd, float scale,
+                 int dtype, void* stream) {
+  return attention_common(0, q, ldq, kv, n_slots, positions, out, ldo, B, T, nh, nkv, hd, scale, dtype, stream);
+}
+
+int fs_attention_generic(const void* q, int64_t ldq, const fs_kv_cache* kv, int64_t n_slots, const int64_t* positions,
+                         void* out, int64_t ldo, int64_t B, int64_t T, int64_t nh, int64_t nkv, int64_t hd,
+                         float scale, int dtype, void* stream) {
+  return attention_common(1, q, ldq, kv, n_slots, positions, out, ldo, B, T, nh, nkv, hd, scale, dtype, stream);
+}
+
+int fs_embed(const int64_t* ids, int64_t n, const void* table, int64_t vocab, int64_t dim, void* out, int dtype,
+             void* stream) {
+  if (n <= 0) return 0;
+  if (!ids || !table || !out) return fail("fs_embed: NULL pointer");
+  return embed(dtype, ids, n, table, vocab, dim, out, static_cast<cudaStream_t>(stream));
+}
+
+int fs_argmax(const void* x, int64_t rows, int64_t n, int64_t row_stride, int64_t* out, int dtype, void* stream) {
+  if (rows <= 0) return 0;
+  if (!x || !out) return fail("fs_argmax: NULL pointer");
+  if (row_stride < n) return fail("fs_argmax: row stride smaller than n");
+  return argmax(dtype, x, rows, n, row_stride, out, static_cast<cudaStream_t>(stream));
+}
+
+}  // extern "C"

@@ -1,0 +1,378 @@
+// Dense bf16 projection GEMM on the 5th-generation tensor cores (tcgen05 + TMEM), sm_100a.
+//
+//   C[M, n_out] = epilogue( A[M, K] @ B[N, K]^T )          A = activations, B = nn.Linear weight (out, in)
+//
+// This is the kernel behind every projection of a decoder layer (forgeserve/model.py:64-66 q/k/v,
+// :77 o, :93 gate/up/down) and the output head (forgeserve/pipeline.py:112 lm_head). Epilogues fuse
+// what follows each projection in the reference module:
+//   EPI_STORE     C = bf16(acc)
+//   EPI_RESIDUAL  C = bf16(R + bf16(acc))                    Block.forward residual add (model.py:105-106)
+//   EPI_SWIGLU    C = bf16(bf16(silu(bf16(g))) * bf16(u))    SwiGLU (model.py:93); B = [W_gate; W_up]
+//                 (2 * n_out rows): an output tile of 128 columns j0.. reads gate rows j0.. and up rows n_out+j0..
+//
+// Design (one CTA per SM, persistent over output tiles):
+//   warp 0      TMA producer: A tile 128x64 and two B half-tiles 128x64 per k-block (rows n0.. and n1..:
+//               n1 = n0 + 128 for plain tiles, the matching up rows for SwiGLU), 128-byte swizzle, 4-stage ring
+//   warp 1      MMA issuer: one thread issues tcgen05.mma (M=128, N=256, K=16) into a TMEM accumulator
+//   warp 2      TMEM allocator (2 accumulators x 256 fp32 columns = all 512 columns)
+//   warps 4-7   epilogue: tcgen05.ld 32 lanes x 32 columns, fused epilogue, vector stores to global memory
+// The two TMEM accumulators let the epilogue of one tile overlap the main loop of the next.
+// No TMA multicast is used anywhere (the kernel also runs in multi-GPU jobs).
+#include <cudaTypedefs.h>
+
+#include "common.cuh"
+#include "gemm.h"
+
+namespace fs {
+namespace tcg {
+
+constexpr int BM = 128, BN = 256, BK = 64, STAGES = 4;
+constexpr int A_BYTES = BM * BK * 2;  // 16 KiB
+constexpr int B_BYTES = BN * BK * 2;  // 32 KiB (two 128-row halves)
+constexpr int BH_BYTES = B_BYTES / 2;
+constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+constexpr int NUM_ACC = 2;
+constexpr int TMEM_COLS = NUM_ACC * BN;  // 512
+constexpr int THREADS = 256;
+constexpr int BAR_BYTES = 256;
+constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 + BAR_BYTES;
+constexpr uint32_t IDESC = idesc_bf16_f32(BM, BN);
+
+struct Params {
+  __nv_bfloat16* C;
+  const __nv_bfloat16* R;
+  int64_t ldc, ldr;
+  int M, n_out;
+  int num_m_blocks, num_tiles, k_blocks;
+  unsigned* err;
+};
+
+__device__ __forceinline__ void tile_coords(int tile, int num_m_blocks, int& m_blk, int& n_blk) {
+  // M-fastest order: the CTAs resident at one time share a few B (weight) tiles and stream all of A,
+  // which for the prefill shapes (M <= 8192, K <= 14336) stays resident in the 126 MB L2.
+  m_blk = tile % num_m_blocks;
+  n_blk = tile / num_m_blocks;
+}
+
+__device__ __forceinline__ float bf16_lo(uint32_t v) { return __uint_as_float(v << 16); }
+__device__ __forceinline__ float bf16_hi(uint32_t v) { return __uint_as_float(v & 0xFFFF0000u); }
+__device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
+  __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&h);
+}
+__device__ __forceinline__ float silu_f(float x) { return x / (1.0f + expf(-x)); }
+
+// Store 32 consecutive outputs of one row (values already final fp32, rounded to bf16 here).
+__device__ __forceinline__ void store_row32(__nv_bfloat16* crow, int col0, int n_out, bool vec_ok,
+                                            const float (&v)[32]) {
+  if (vec_ok && col0 + 32 <= n_out) {
+    uint4* dst = reinterpret_cast<uint4*>(crow + col0);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      uint4 w;
+      w.x = pack_bf16(v[8 * i + 0], v[8 * i + 1]);
+      w.y = pack_bf16(v[8 * i + 2], v[8 * i + 3]);
+      w.z = pack_bf16(v[8 * i + 4], v[8 * i + 5]);
+      w.w = pack_bf16(v[8 * i + 6], v[8 * i + 7]);
+      dst[i] = w;
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < 32; ++i)
+      if (col0 + i < n_out) crow[col0 + i] = __float2bfloat16_rn(v[i]);
+  }
+}
+
+__device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, unsigned* err) {
+  // Every lane waits (bounded); the warp proceeds only if all lanes saw the phase complete, so that the
+  // following .sync.aligned tcgen05 instructions are executed by the whole warp or by none of it.
+  bool ok = mbar_wait(bar, parity, err);
+  return __all_sync(0xffffffffu, ok);
+}
+
+template <int EPI>
+__global__ void __launch_bounds__(THREADS, 1)
+    gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, Params p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* tiles = smem;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES);
+  uint64_t* full = bars;
+  uint64_t* empty = bars + STAGES;
+  uint64_t* tfull = bars + 2 * STAGES;
+  uint64_t* tempty = bars + 2 * STAGES + NUM_ACC;
+  uint64_t* mma_done = bars + 2 * STAGES + 2 * NUM_ACC;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < NUM_ACC; ++a) {
+      mbar_init(&tfull[a], 1);
+      mbar_init(&tempty[a], 128);
+    }
+    mbar_init(mma_done, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    prefetch_tmap(&tmA);
+    prefetch_tmap(&tmB);
+  }
+  if (warp == 2) {
+    tmem_alloc(tmem_slot, TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      int s = 0;
+      uint32_t ph = 0;
+      bool issued[STAGES];
+      uint32_t last_ph[STAGES];
+#pragma unroll
+      for (int i = 0; i < STAGES; ++i) issued[i] = false, last_ph[i] = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < p.num_tiles && ok; tile += gridDim.x) {
+        int m_blk, n_blk;
+        tile_coords(tile, p.num_m_blocks, m_blk, n_blk);
+        const int b_row0 = EPI == EPI_SWIGLU ? n_blk * (BN / 2) : n_blk * BN;
+        const int b_row1 = EPI == EPI_SWIGLU ? p.n_out + n_blk * (BN / 2) : n_blk * BN + BN / 2;
+        for (int kb = 0; kb < p.k_blocks; ++kb) {
+          if (!mbar_wait(&empty[s], ph ^ 1u, p.err) || *abort_flag) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&full[s], STAGE_BYTES);
+          tma_load_2d(tiles + s * STAGE_BYTES, &tmA, &full[s], kb * BK, m_blk * BM);
+          tma_load_2d(tiles + s * STAGE_BYTES + A_BYTES, &tmB, &full[s], kb * BK, b_row0);
+          tma_load_2d(tiles + s * STAGE_BYTES + A_BYTES + BH_BYTES, &tmB, &full[s], kb * BK, b_row1);
+          issued[s] = true;
+          last_ph[s] = ph;
+          if (++s == STAGES) s = 0, ph ^= 1u;
+        }
+      }
+      if (!ok) {
+        *abort_flag = 1;
+        // Let every copy this thread started land before the CTA can exit (bounded).
+        for (int i = 0; i < STAGES; ++i)
+          if (issued[i]) mbar_wait(&full[i], last_ph[i], p.err);
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      int s = 0, acc = 0;
+      uint32_t ph = 0, acc_ph = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < p.num_tiles && ok; tile += gridDim.x) {
+        if (!mbar_wait(&tempty[acc], acc_ph ^ 1u, p.err) || *abort_flag) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
+        for (int kb = 0; kb < p.k_blocks; ++kb) {
+          if (!mbar_wait(&full[s], ph, p.err) || *abort_flag) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_addr = smem_u32(tiles + s * STAGE_BYTES);
+          const uint64_t adesc = sw128_kmajor_desc(a_addr);
+          const uint64_t bdesc = sw128_kmajor_desc(a_addr + A_BYTES);
+#pragma unroll
+          for (int k = 0; k < BK / 16; ++k) {
+            // +32 bytes along K inside the 128-byte swizzle row = +2 in the descriptor's address field
+            tc_mma_f16(d_tmem, adesc + 2u * k, bdesc + 2u * k, IDESC, (kb | k) != 0);
+          }
+          tc_commit(&empty[s]);  // the smem stage is free once these MMAs have read it
+          if (++s == STAGES) s = 0, ph ^= 1u;
+        }
+        if (!ok) break;
+        tc_commit(&tfull[acc]);  // accumulator complete
+        if (++acc == NUM_ACC) acc = 0, acc_ph ^= 1u;
+      }
+      if (!ok) *abort_flag = 1;
+      tc_commit(mma_done);  // arrives once every MMA issued above has completed
+    }
+  } else if (warp >= 4) {
+    // ------------------------------------------------------------------ epilogue (TMEM -> global)
+    const int q = warp - 4;  // this warp may read TMEM lanes 32q .. 32q+31
+    const bool vec_ok = ((p.ldc & 7) == 0) && ((reinterpret_cast<uintptr_t>(p.C) & 15) == 0) &&
+                        (EPI != EPI_RESIDUAL || (((p.ldr & 7) == 0) && ((reinterpret_cast<uintptr_t>(p.R) & 15) == 0)));
+    int acc = 0;
+    uint32_t acc_ph = 0;
+    for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x) {
+      if (!warp_wait(&tfull[acc], acc_ph, p.err)) break;
+      tc_fence_after();
+      int m_blk, n_blk;
+      tile_coords(tile, p.num_m_blocks, m_blk, n_blk);
+      const int row = m_blk * BM + q * 32 + lane;
+      const bool row_ok = row < p.M;
+      __nv_bfloat16* crow = p.C + static_cast<int64_t>(row) * p.ldc;
+      const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(acc * BN);
+      if constexpr (EPI == EPI_SWIGLU) {
+#pragma unroll 1
+        for (int c = 0; c < BN / 64; ++c) {
+          uint32_t g[32], u[32];
+          tmem_ld_32x32b_x32(taddr + c * 32, g);
+          tmem_ld_32x32b_x32(taddr + BN / 2 + c * 32, u);
+          tc_wait_ld();
+          float v[32];
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            const float gb = rnd<__nv_bfloat16>(__uint_as_float(g[i]));
+            const float ub = rnd<__nv_bfloat16>(__uint_as_float(u[i]));
+            v[i] = rnd<__nv_bfloat16>(silu_f(gb)) * ub;
+          }
+          if (row_ok) store_row32(crow, n_blk * (BN / 2) + c * 32, p.n_out, vec_ok, v);
+        }
+      } else {
+#pragma unroll 1
+        for (int c = 0; c < BN / 32; ++c) {
+          uint32_t r[32];
+          tmem_ld_32x32b_x32(taddr + c * 32, r);
+          tc_wait_ld();
+          const int col0 = n_blk * BN + c * 32;
+          float v[32];
+#pragma unroll
+          for (int i = 0; i < 32; ++i) v[i] = rnd<__nv_bfloat16>(__uint_as_float(r[i]));
+          if constexpr (EPI == EPI_RESIDUAL) {
+            if (row_ok) {
+              const __nv_bfloat16* rrow = p.R + static_cast<int64_t>(row) * p.ldr;
+              if (vec_ok && col0 + 32 <= p.n_out) {
+                const uint4* src = reinterpret_cast<const uint4*>(rrow + col0);
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                  const uint4 w = src[i];
+                  v[8 * i + 0] += bf16_lo(w.x), v[8 * i + 1] += bf16_hi(w.x);
+                  v[8 * i + 2] += bf16_lo(w.y), v[8 * i + 3] += bf16_hi(w.y);
+                  v[8 * i + 4] += bf16_lo(w.z), v[8 * i + 5] += bf16_hi(w.z);
+                  v[8 * i + 6] += bf16_lo(w.w), v[8 * i + 7] += bf16_hi(w.w);
+                }
+              } else {
+#pragma unroll
+                for (int i = 0; i < 32; ++i)
+                  if (col0 + i < p.n_out) v[i] += __bfloat162float(rrow[col0 + i]);
+              }
+            }
+          }
+          if (row_ok) store_row32(crow, col0, p.n_out, vec_ok, v);
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(&tempty[acc]);
+      if (++acc == NUM_ACC) acc = 0, acc_ph ^= 1u;
+    }
+  }
+
+  __syncthreads();
+  if (warp == 2) {
+    // All MMAs must have completed before the accumulators are released (they have, unless a wait ran out).
+    mbar_wait(mma_done, 0, p.err);
+    tc_fence_after();
+    tmem_dealloc(tmem_base, TMEM_COLS);
+  }
+}
+
+// ------------------------------------------------------------------------------------------------ host
+static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  if (!fn) {
+    cudaDriverEntryPointQueryResult q;
+    void* ptr = nullptr;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+  }
+  return fn;
+}
+
+// K-major bf16 matrix [rows, K] with row stride ld (elements) -> tensor map with box (box_rows x 64).
+static int make_kmajor_map(CUtensorMap* map, const void* ptr, int64_t rows, int64_t K, int64_t ld, int box_rows) {
+  auto fn = encode_fn();
+  if (!fn) return fail("cuTensorMapEncodeTiled is unavailable from the CUDA driver");
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(K), static_cast<cuuint64_t>(rows)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(ld) * 2};
+  cuuint32_t box[2] = {static_cast<cuuint32_t>(BK), static_cast<cuuint32_t>(box_rows)};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(ptr), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail("cuTensorMapEncodeTiled failed with CUresult " + std::to_string(int(r)));
+  return 0;
+}
+
+static int sm_count() {
+  static int n[64] = {0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) dev = 0;
+  if (!n[dev]) cudaDeviceGetAttribute(&n[dev], cudaDevAttrMultiProcessorCount, dev);
+  return n[dev] > 0 ? n[dev] : 148;
+}
+
+bool supported(const void* A, int64_t lda, const void* B, int64_t ldb, int64_t K) {
+  // TMA: base 16-byte aligned, row strides a multiple of 16 bytes.
+  return ((reinterpret_cast<uintptr_t>(A) & 15) == 0) && ((reinterpret_cast<uintptr_t>(B) & 15) == 0) &&
+         (lda % 8 == 0) && (ldb % 8 == 0) && K >= 8 && K % 8 == 0;
+}
+
+template <int EPI>
+static int launch_t(const CUtensorMap& ma, const CUtensorMap& mb, const Params& p, int grid, cudaStream_t st) {
+  static bool attr_set[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev >= 0 && dev < 64 && !attr_set[dev]) {
+    if (cudaFuncSetAttribute(gemm_tc_kernel<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES) !=
+        cudaSuccess)
+      return check_launch("gemm_tc set smem");
+    attr_set[dev] = true;
+  }
+  gemm_tc_kernel<EPI><<<grid, THREADS, SMEM_BYTES, st>>>(ma, mb, p);
+  return check_launch("gemm_tc_kernel");
+}
+
+int gemm_tc(const void* A, int64_t lda, const void* B, int64_t ldb, void* C, int64_t ldc, const void* R,
+            int64_t ldr, int64_t M, int64_t N, int64_t K, int64_t n_out, int epi, cudaStream_t stream) {
+  if (M <= 0 || N <= 0 || n_out <= 0) return 0;
+  if (M > INT32_MAX / 2 || N > INT32_MAX / 2 || K > INT32_MAX / 2) return fail("gemm: dimension too large");
+  CUtensorMap ma, mb;
+  if (make_kmajor_map(&ma, A, M, K, lda, BM)) return -1;
+  if (make_kmajor_map(&mb, B, N, K, ldb, BN / 2)) return -1;
+  Params p;
+  p.C = static_cast<__nv_bfloat16*>(C);
+  p.R = static_cast<const __nv_bfloat16*>(R);
+  p.ldc = ldc;
+  p.ldr = ldr;
+  p.M = static_cast<int>(M);
+  p.n_out = static_cast<int>(n_out);
+  p.num_m_blocks = static_cast<int>((M + BM - 1) / BM);
+  const int n_tile = epi == EPI_SWIGLU ? BN / 2 : BN;  // output columns per tile
+  const int num_n_blocks = static_cast<int>((n_out + n_tile - 1) / n_tile);
+  p.num_tiles = p.num_m_blocks * num_n_blocks;
+  p.k_blocks = static_cast<int>((K + BK - 1) / BK);
+  p.err = error_word();
+  if (!p.err) return -1;
+  const int grid = p.num_tiles < sm_count() ? p.num_tiles : sm_count();
+  switch (epi) {
+    case EPI_STORE: return launch_t<EPI_STORE>(ma, mb, p, grid, stream);
+    case EPI_RESIDUAL: return launch_t<EPI_RESIDUAL>(ma, mb, p, grid, stream);
+    case EPI_SWIGLU: return launch_t<EPI_SWIGLU>(ma, mb, p, grid, stream);
+    default: return fail("gemm: unknown epilogue");
+  }
+}
+
+}  // namespace tcg
+}  // namespace fs

@@ -1,0 +1,116 @@
+/* forgeserve_b200 — C ABI of the B200 (sm_100a) kernels behind the pipeline-parallel forward path.
+ *
+ * The reference (omkarbhad/forgeserve) is pure PyTorch: each entry point below replaces the ATen calls of
+ * one step of a decoder stage, cited as file:line of the reference project. All pointers are device
+ * pointers unless stated; `stream` is a cudaStream_t passed as void*. Every entry point only enqueues work
+ * on `stream` and returns 0 on success, or a negative status with a message readable through
+ * fs_last_error() (thread-local). Kernels never trap: bad token ids, cache slots or positions found on the
+ * device, and waits that run out of time, set bits of a device error word read by fs_device_error().
+ *
+ * dtype: FS_F32 (true fp32 arithmetic, the 1e-4 parity mode) or FS_BF16 (tensor-core mode).
+ * Matrices are row-major with an explicit row stride in elements.
+ */
+#ifndef FORGESERVE_B200_H
+#define FORGESERVE_B200_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum { FS_F32 = 0, FS_BF16 = 1 };
+enum { FS_EPI_STORE = 0, FS_EPI_RESIDUAL = 1, FS_EPI_SWIGLU = 2 };
+enum { FS_ERR_WAIT_TIMEOUT = 1, FS_ERR_BAD_TOKEN = 2, FS_ERR_BAD_SLOT = 4, FS_ERR_BAD_POSITION = 8 };
+
+/* Library version (major*10000 + minor*100 + patch). */
+int fs_version(void);
+
+/* Message of the last failed call on this host thread ("" if none). */
+const char* fs_last_error(void);
+
+/* Reads (and, if clear != 0, resets) the device error word of the current device. Synchronises the device. */
+int fs_device_error(int clear, unsigned* out_bits);
+
+/* Number of kernel launches made by this library in this process (all devices). */
+int64_t fs_launch_count(void);
+
+/* RMSNorm over rows: y = T(T(x * rsqrt(mean(x^2) + eps)) * w), fp32 statistics.
+ * Replaces RMSNorm.forward, forgeserve/model.py:29-31. y may alias x. */
+int fs_rmsnorm(const void* x, int64_t x_stride, const void* w, void* y, int64_t y_stride, int64_t rows, int64_t dim,
+               float eps, int dtype, void* stream);
+
+/* Projection GEMM: C[M, n_out] = epi(A[M, K] @ B[N, K]^T), B in nn.Linear (out, in) layout.
+ *   FS_EPI_STORE:    n_out = N.
+ *   FS_EPI_RESIDUAL: C = R + C (R may alias C), the residual adds of Block.forward (model.py:105-106).
+ *   FS_EPI_SWIGLU:   C = silu(gate) * up, SwiGLU.forward (model.py:93); B = [W_gate; W_up], N = 2 * n_out.
+ * Replaces nn.Linear calls at model.py:64-66, :77, :93 and pipeline.py:112 (lm_head).
+ * bf16 runs on the tcgen05/TMEM tensor-core kernel when A/B are 16-byte aligned with row strides a multiple of
+ * 8 elements; fp32 (and other bf16 layouts) run on CUDA cores with fp32 accumulation. */
+int fs_gemm(const void* A, int64_t lda, const void* B, int64_t ldb, void* C, int64_t ldc, const void* R, int64_t ldr,
+            int64_t M, int64_t N, int64_t K, int64_t n_out, int epilogue, int dtype, void* stream);
+
+/* Same as fs_gemm but never uses the tensor-core kernel (CUDA-core path), for cross-checking. */
+int fs_gemm_simt(const void* A, int64_t lda, const void* B, int64_t ldb, void* C, int64_t ldc, const void* R,
+                 int64_t ldr, int64_t M, int64_t N, int64_t K, int64_t n_out, int epilogue, int dtype, void* stream);
+
+/* KV cache of one layer. Slot s of batch row r, KV head g is at
+ *   base + table[r*table_stride + s/block_size]*block_stride + g*head_stride + (s % block_size)*head_dim.
+ * Paged pool (num_blocks, n_kv, block_size, hd) (forgeserve/paged.py:48-50): table = block table.
+ * Contiguous per-row cache (B, n_kv, capacity, hd) (forgeserve/kv.py:10-24): block_size = capacity,
+ * table = [0, 1, ..., B-1]. */
+typedef struct {
+  void* k;
+  void* v;
+  const int64_t* table;
+  int64_t table_stride;
+  int64_t table_cols;
+  int64_t block_size;
+  int64_t block_stride;
+  int64_t head_stride;
+  int64_t num_blocks;
+} fs_kv_cache;
+
+/* RoPE on the fused q/k/v projection output + store of the new keys/values into the cache.
+ * qkv: (B*T, ld) rows [q: nh*hd | k: nkv*hd | v: nkv*hd]; q is rotated in place. cos/sin: fp32 (rope_rows, hd/2)
+ * tables (model.py:34-37), rotation as model.py:40-45. Slot of token (r, j): slot_base + j if slot_from_pos == 0
+ * (contiguous cache, ContiguousKV.update kv.py:21-24), positions[r, j] otherwise (PagedLayerView.update
+ * paged.py:74-78). apply_rope = 0 stores k unrotated (used by tests). */
+int fs_rope_kv_write(void* qkv, int64_t ld, const float* cos_t, const float* sin_t, int64_t rope_rows,
+                     const int64_t* positions, const fs_kv_cache* kv, int64_t B, int64_t T, int64_t nh, int64_t nkv,
+                     int64_t hd, int64_t slot_base, int slot_from_pos, int apply_rope, int dtype, void* stream);
+
+/* Store k, v of shape (B, nkv, T, hd) at slots positions[r, j] (write half of PagedLayerView.update,
+ * paged.py:72-78). */
+int fs_kv_store(const void* k, const void* v, const int64_t* positions, const fs_kv_cache* kv, int64_t B, int64_t T,
+                int64_t nkv, int64_t hd, int dtype, void* stream);
+
+/* out (B, nkv, nb*bs, hd) = pool[table] permuted (read half of PagedLayerView.update, paged.py:80-81). */
+int fs_paged_gather(const void* pool, const int64_t* table, int64_t B, int64_t nb, int64_t num_blocks, int64_t nkv,
+                    int64_t block_size, int64_t hd, void* out, int dtype, void* stream);
+
+/* GQA attention of B*T new queries over the cache: key slot s visible iff s <= positions[r, j] and s < n_slots
+ * (model.py:69-76: cache update, repeat_interleave, mask, scaled_dot_product_attention with scale 1/sqrt(hd)).
+ * q rows (B*T, ldq) hold nh heads; out rows (B*T, ldo). bf16 with hd 64/128 runs on tensor cores. */
+int fs_attention(const void* q, int64_t ldq, const fs_kv_cache* kv, int64_t n_slots, const int64_t* positions,
+                 void* out, int64_t ldo, int64_t B, int64_t T, int64_t nh, int64_t nkv, int64_t hd, float scale,
+                 int dtype, void* stream);
+
+/* Same as fs_attention on the CUDA-core kernel only (cross-checking). */
+int fs_attention_generic(const void* q, int64_t ldq, const fs_kv_cache* kv, int64_t n_slots, const int64_t* positions,
+                         void* out, int64_t ldo, int64_t B, int64_t T, int64_t nh, int64_t nkv, int64_t hd,
+                         float scale, int dtype, void* stream);
+
+/* Token embedding gather out[i] = table[ids[i]] (nn.Embedding at pipeline.py:106 / model.py:134-135). */
+int fs_embed(const int64_t* ids, int64_t n, const void* table, int64_t vocab, int64_t dim, void* out, int dtype,
+             void* stream);
+
+/* Greedy sampling: out[i] = argmax(x[i, :n]) with the lowest index on ties (sampling.py:18-19,
+ * pipeline.py:133). */
+int fs_argmax(const void* x, int64_t rows, int64_t n, int64_t row_stride, int64_t* out, int dtype, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* FORGESERVE_B200_H */
