@@ -1,0 +1,380 @@
+"""Pipeline-parallel prefill throughput of an 8B-shaped bf16 decoder on 1-8 B200s (one pipeline stage per GPU).
+
+Workload: LLaMA-3-8B shape — 32 layers, d_model 4096, 32 query / 8 KV heads (head_dim 128),
+ffn 14336, vocab 128256, RoPE theta 5e5 — seeded N(0, 0.02) weights, uniform random token ids; one step is one
+`pipeline_forward` of 16 micro-batches x (4 x 2048) tokens through p = N stages, logits for every position on the
+last stage, exactly as the reference's pipeline_forward computes them.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+    torchrun --nproc-per-node N bench.py --gpus N ...     (one rank per GPU, NCCL)
+
+Prints one JSON line on rank 0. `value` is device-timed (CUDA events, max over ranks) with the token ids already
+on the GPU; `e2e` is the same through the public API with the token ids copied from pinned host memory and the
+last-position logits copied back every step. `--impl reference` times the CPU oracle (a restatement of the
+reference's algorithm) on the host cores on a bounded sample of the same workload.
+"""
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+import torch
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "PP prefill tokens/s, 8B-shape bf16"
+CFG = dict(vocab_size=128256, d_model=4096, n_layers=32, n_heads=32, n_kv_heads=8, ffn_dim=14336, max_seq_len=8192,
+           rope_theta=500000.0)
+MICROBATCHES, MB_ROWS, SEQ = 16, 4, 2048
+WORKLOAD = ("C3: 8B-shape prefill (32 layers, d4096, 32/8 heads, ffn 14336, vocab 128256, theta 5e5), "
+            "16 micro-batches x (4 x 2048 tokens), one pipeline stage per GPU")
+
+
+def peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return d["bf16_tflops_sustained"], "measured (bf16_tflops_sustained, MEASURED_PEAKS.json)"
+    return 1400.0, "fallback (1.4 PFLOP/s sustained)"
+
+
+class ClockSampler:
+    """nvidia-smi samples every 200 ms while running (reads clocks only; changes nothing)."""
+
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+             "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+             "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpus):
+        self.gpus = set(gpus)
+        self.proc = None
+        self.lines = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
+                                          "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except (OSError, FileNotFoundError):
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *a):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.lines:
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9 or not f[0].isdigit() or int(f[0]) not in self.gpus:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = float(f[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        under = [s for s in sm if mx and s > 0.3 * mx] or sm
+        return {"sm_mhz": statistics.median(under) if under else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# --------------------------------------------------------------------------------------------------- ours
+def run_ours(args):
+    import torch.distributed as dist
+
+    from forgeserve_b200 import ModelConfig, PipelineStage, PipelineState, bubble_fraction, ops, pipeline_forward
+    from forgeserve_b200 import _lib
+    from forgeserve_b200.weights import init_stage_
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=600))
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    def allreduce(x, op):
+        t = torch.tensor([float(x)], device=dev, dtype=torch.float64)
+        if world > 1:
+            dist.all_reduce(t, op=op)
+        return float(t)
+
+    cfg = ModelConfig(**CFG)
+    stage = PipelineStage(cfg, rank, world, device=dev, dtype=torch.bfloat16).eval()
+    init_stage_(stage, seed=1234, std=0.02)
+    batch = MICROBATCHES * MB_ROWS
+    g = torch.Generator(device="cpu").manual_seed(7)
+    idx_host = torch.randint(0, cfg.vocab_size, (batch, SEQ), generator=g).pin_memory()
+    idx_dev = idx_host.to(dev)
+    tokens_per_step = batch * SEQ
+
+    def step(idx):
+        state = PipelineState(stage, batch, MICROBATCHES)
+        return pipeline_forward(stage, state, idx if stage.is_first else None, SEQ)
+
+    for _ in range(args.warmup):
+        step(idx_dev)
+    barrier()
+
+    # ---- device-timed region (token ids already on the GPU)
+    stream = torch.cuda.current_stream(dev)
+    stage.trace = []
+    ops.gemm_events = []
+    launches0 = _lib.launch_count()
+    sampler = ClockSampler([local] if world == 1 else range(world))
+    with sampler:
+        barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(args.steps):
+            out = step(idx_dev)
+            del out
+        e1.record(stream)
+        torch.cuda.synchronize()
+    launches = _lib.launch_count() - launches0
+    ms_total = e0.elapsed_time(e1)
+    ms_max = allreduce(ms_total, dist.ReduceOp.MAX if world > 1 else None)
+    busy_ms = sum(a.elapsed_time(b) for _, a, b in stage.trace)
+    busy_sum = allreduce(busy_ms, dist.ReduceOp.SUM if world > 1 else None)
+    gemm_flops = sum(f for _, _, f in ops.gemm_events)
+    gemm_ms = sum(a.elapsed_time(b) for a, b, _ in ops.gemm_events)
+    gemm_n = len(ops.gemm_events)
+    gemm_flops = allreduce(gemm_flops, dist.ReduceOp.SUM if world > 1 else None)
+    gemm_ms = allreduce(gemm_ms, dist.ReduceOp.SUM if world > 1 else None)
+    gemm_n = allreduce(gemm_n, dist.ReduceOp.SUM if world > 1 else None)
+    launches = allreduce(launches, dist.ReduceOp.SUM if world > 1 else None)
+    stage.trace = None
+    ops.gemm_events = None
+
+    # ---- end to end through the public API: host token ids in, last-position logits out
+    barrier()
+    out_host = torch.empty(batch, cfg.vocab_size, dtype=torch.bfloat16).pin_memory() if stage.is_last else None
+    e2 = torch.cuda.Event(enable_timing=True)
+    e3 = torch.cuda.Event(enable_timing=True)
+    e2.record(stream)
+    for _ in range(args.steps):
+        idx = idx_host.to(dev, non_blocking=True) if stage.is_first else None
+        logits = step(idx)
+        if stage.is_last:
+            out_host.copy_(logits[:, -1], non_blocking=True)
+        del logits
+    e3.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = allreduce(e2.elapsed_time(e3), dist.ReduceOp.MAX if world > 1 else None)
+
+    clocks = sampler.summary()
+    result = None
+    if rank == 0:
+        value = tokens_per_step * args.steps / (ms_max / 1e3)
+        peak, peak_src = peaks()
+        achieved = gemm_flops / (gemm_ms / 1e3) / 1e12 if gemm_ms > 0 else None
+        flops_per_token = 2 * (cfg.d_model * (cfg.n_heads + 2 * cfg.n_kv_heads) * cfg.head_dim +
+                               cfg.n_heads * cfg.head_dim * cfg.d_model + 3 * cfg.d_model * cfg.ffn_dim) * cfg.n_layers \
+            + 2 * cfg.d_model * cfg.vocab_size
+        attn_flops = 2 * MB_ROWS * cfg.n_heads * SEQ * SEQ * cfg.head_dim * cfg.n_layers * MICROBATCHES  # causal
+        step_flops = flops_per_token * tokens_per_step + attn_flops
+        result = {
+            "metric": METRIC, "value": round(value, 1), "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(ms_max / args.steps, 3), "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic: uniform token ids, seeded N(0, 0.02) weights (no checkpoint or dataset)",
+            "config": {"workload": WORKLOAD, "global_batch": batch, "seq_len": SEQ, "microbatches": MICROBATCHES,
+                       "stages": world, "parallelism": f"pp{world}",
+                       "l2": "no flush needed: every step streams 16 GB of weights (> 126 MB L2)"},
+            "bubble": {"measured": round(1.0 - busy_sum / (world * ms_max), 4),
+                       "analytic": round(bubble_fraction(world, MICROBATCHES), 4)},
+            "model_tflops": round(step_flops * args.steps / (ms_max / 1e3) / 1e12, 1),
+            "roofline": {"bound": "tensor", "kernel": "gemm_tc_kernel (every projection GEMM of the timed region)",
+                         "achieved": round(achieved, 1) if achieved else None, "peak": peak, "unit": "TFLOP/s",
+                         "frac": round(achieved / peak, 4) if achieved else None, "peak_source": peak_src,
+                         "launches": int(gemm_n), "traffic": gemm_traffic()},
+            "e2e": {"value": round(tokens_per_step * args.steps / (e2e_ms / 1e3), 1), "unit": "tokens/s",
+                    "h2d_bytes_per_step": idx_host.numel() * idx_host.element_size(),
+                    "d2h_bytes_per_step": batch * cfg.vocab_size * 2},
+            "gpu_launches": int(launches),
+            "clocks": clocks,
+        }
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return result
+
+
+def gemm_traffic():
+    """DRAM bytes per launch of the profiled gate/up GEMM launch, from the committed ncu summary (or None)."""
+    p = ROOT / "profiles" / "gemm_tc_8b_gateup.txt"
+    if not p.exists():
+        return None
+    for line in p.read_text().splitlines():
+        if line.startswith("dram_bytes_per_launch:"):
+            try:
+                return int(line.split(":")[1].split()[0])
+            except (ValueError, IndexError):
+                return None
+    return None
+
+
+# ------------------------------------------------------------------------------------------- CPU baseline
+def cpu_sample(steps: int, warmup: int):
+    """The oracle (CPU restatement of the reference path, fp32, all host threads) on a bounded sample of the
+    workload: one decoder layer and the head on one 2048-token row; tokens/s for the whole 32-layer model is
+    2048 / (32 * t_layer + t_head)."""
+    from oracle import forge_oracle as O
+    cfg = O.Cfg(**CFG)
+    threads = torch.get_num_threads()
+    g = torch.Generator().manual_seed(0)
+    names = O.param_order(cfg)
+    sd = {}
+    for name, shape in names:
+        if name.startswith("layers.0.") or name in ("norm.weight",):
+            sd[name] = torch.randn(shape, generator=g) * 0.02 if len(shape) > 1 else torch.ones(shape)
+    sd["lm_head.weight"] = torch.randn(cfg.vocab_size, cfg.d_model, generator=g) * 0.02
+    cos, sin = O.rope_tables(cfg.head_dim, cfg.max_seq_len, cfg.rope_theta)
+    x = torch.randn(1, SEQ, cfg.d_model, generator=g)
+    pos = torch.arange(SEQ)[None]
+    times = []
+    for i in range(warmup + steps):
+        t0 = time.perf_counter()
+        y = O.block(sd, 0, x, cfg, cos, sin, pos, O.ContiguousCache())
+        t1 = time.perf_counter()
+        O.head(sd, y, cfg)
+        t2 = time.perf_counter()
+        if i >= warmup:
+            times.append((t1 - t0, t2 - t1))
+    t_layer = statistics.median(t for t, _ in times)
+    t_head = statistics.median(h for _, h in times)
+    per_row = cfg.n_layers * t_layer + t_head
+    return {"value": round(SEQ / per_row, 2), "unit": "tokens/s", "cores": threads, "kind": "port",
+            "sample": f"oracle fp32: 1 of 32 layers + final norm/head on 1 x {SEQ} tokens per step, "
+                      f"extrapolated to the 32-layer model (t_layer {t_layer:.3f} s, t_head {t_head:.3f} s)"}
+
+
+def run_reference(args):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return None
+    t0 = time.perf_counter()
+    cb = cpu_sample(args.steps, args.warmup)
+    wall = time.perf_counter() - t0
+    return {"metric": METRIC, "value": cb["value"], "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(SEQ / cb["value"] * 1e3, 3), "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "f32", "impl": "reference",
+            "data": "synthetic: random fp32 weights (std 0.02) and activations",
+            "config": {"workload": WORKLOAD, "global_batch": MICROBATCHES * MB_ROWS, "seq_len": SEQ,
+                       "microbatches": MICROBATCHES, "stages": world, "parallelism": "cpu"},
+            "cpu_baseline": cb,
+            "e2e": {"value": cb["value"], "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+            "wall_s": round(wall, 1)}
+
+
+def profile_case(name: str, reps: int):
+    """A few launches of one kernel on a small case (inputs larger than L2, a few GB at most) for ncu captures."""
+    from forgeserve_b200 import _lib as L
+    from forgeserve_b200 import ops
+    dev = torch.device("cuda", 0)
+    g = torch.Generator(device=dev).manual_seed(0)
+
+    def rnd(*shape, scale=1.0):
+        return (torch.randn(*shape, device=dev, generator=g) * scale).bfloat16()
+
+    M, d, F, nh, nkv, hd, V = MB_ROWS * SEQ, CFG["d_model"], CFG["ffn_dim"], CFG["n_heads"], CFG["n_kv_heads"], 128, \
+        CFG["vocab_size"]
+    if name == "gemm_gateup":          # one micro-batch's gate/up projection: M 8192, N 2 x 14336, K 4096
+        a, w = rnd(M, d), rnd(2 * F, d, scale=0.02)
+        fn = lambda: ops.linear(a, w, L.FS_EPI_SWIGLU)
+    elif name == "gemm_qkv":
+        a, w = rnd(M, d), rnd((nh + 2 * nkv) * hd, d, scale=0.02)
+        fn = lambda: ops.linear(a, w)
+    elif name == "gemm_down":
+        a, w, x = rnd(M, F), rnd(d, F, scale=0.02), rnd(M, d)
+        fn = lambda: ops.linear(a, w, L.FS_EPI_RESIDUAL, residual=x, out=x)
+    elif name == "gemm_head":
+        a, w = rnd(M, d), rnd(V, d, scale=0.02)
+        out = torch.empty(M, V, device=dev, dtype=torch.bfloat16)
+        fn = lambda: ops.linear(a, w, out=out)
+    elif name == "attention":          # one micro-batch's causal prefill attention: 4 x 2048 queries, 32/8 heads
+        kc, vc = rnd(MB_ROWS, nkv, SEQ, hd), rnd(MB_ROWS, nkv, SEQ, hd)
+        q = rnd(M, (nh + 2 * nkv) * hd)
+        pos = torch.arange(SEQ, device=dev)[None].expand(MB_ROWS, SEQ).contiguous()
+        out = torch.empty(M, nh * hd, device=dev, dtype=torch.bfloat16)
+        table = torch.arange(MB_ROWS, device=dev)
+        desc = ops.contiguous_desc(kc, vc, table)
+        fn = lambda: ops.attention(q[:, : nh * hd], desc, SEQ, pos, out, MB_ROWS, SEQ, nh, nkv, hd)
+    elif name == "rope_kv":
+        kc, vc = rnd(MB_ROWS, nkv, SEQ, hd), rnd(MB_ROWS, nkv, SEQ, hd)
+        q = rnd(M, (nh + 2 * nkv) * hd)
+        pos = torch.arange(SEQ, device=dev)[None].expand(MB_ROWS, SEQ).contiguous()
+        from forgeserve_b200.model import precompute_rope
+        cos, sin = (t.to(dev) for t in precompute_rope(hd, CFG["max_seq_len"], CFG["rope_theta"]))
+        desc = ops.contiguous_desc(kc, vc, torch.arange(MB_ROWS, device=dev))
+        fn = lambda: ops.rope_kv_write(q, cos, sin, pos, desc, MB_ROWS, SEQ, nh, nkv, hd, 0, False)
+    elif name == "rmsnorm":
+        x, w = rnd(M, d), rnd(d)
+        fn = lambda: ops.rmsnorm(x, w, 1e-5)
+    else:
+        raise SystemExit(f"unknown profile case {name}")
+    for _ in range(reps):
+        fn()
+    torch.cuda.synchronize()
+    print(json.dumps({"profile_case": name, "reps": reps, "device_error": L.device_error()}))
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--profile-case", default=None, help="run a few launches of one kernel (for ncu) and exit")
+    ap.add_argument("--reps", type=int, default=3)
+    args = ap.parse_args()
+    if args.profile_case:
+        profile_case(args.profile_case, args.reps)
+        return
+    if args.warmup < 3 and args.impl == "ours":
+        print("warning: fewer than 3 warm-up steps", file=sys.stderr)
+    if args.impl == "reference":
+        res = run_reference(args)
+    else:
+        res = run_ours(args)
+        if res is not None and args.gpus == 1 and not args.no_cpu_baseline:
+            torch.cuda.empty_cache()
+            res["cpu_baseline"] = cpu_sample(steps=2, warmup=1)
+    if res is not None:
+        print(json.dumps(res), flush=True)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,158 @@
+"""Continuous batching over a paged KV cache (forgeserve/engine.py:23-139), on the GPU.
+
+Scheduling is the reference's, step for step: a step prefills the head of the queue (whole prompt, batch 1)
+when a slot and its blocks are free, otherwise decodes one token for every running request; blocks are taken
+on demand; when the pool runs dry the most recently started request is preempted (its blocks freed, its
+output kept, re-prefilled later from prompt + output); requests finish on max_new_tokens, eos or max_seq_len.
+
+What runs differently: the pool lives on the model's device in the model's dtype; the model computes the head
+for the last position only; greedy rows are sampled together by one argmax kernel and read back with one copy,
+and temperature rows draw from the engine's seeded CPU generator in row order (the order of the reference's
+per-row `sample` calls, so the generator stream is consumed identically).
+"""
+
+from collections import deque
+from dataclasses import dataclass, field
+from typing import Deque, Dict, List, Optional
+
+import torch
+import torch.nn.functional as F
+
+from . import ops
+from .paged import PagedKVPool
+
+
+@dataclass
+class Request:
+    id: int
+    prompt: List[int]
+    max_new_tokens: int
+    eos_id: Optional[int] = None
+    temperature: float = 0.0
+    output: List[int] = field(default_factory=list)
+    blocks: List[int] = field(default_factory=list)    # block table while the request holds cache blocks
+    cached: int = 0                                     # tokens whose keys/values are in the cache
+    finished: bool = False
+
+
+class Engine:
+    def __init__(self, model, num_blocks: int, block_size: int = 16, max_batch: int = 8, seed: int = 0):
+        self.model, self.cfg = model, model.cfg
+        self.pool = PagedKVPool(self.cfg, num_blocks, block_size, tp=model.tp, dtype=model.dtype, device=model.device)
+        self.max_batch = max_batch
+        self.generator = torch.Generator().manual_seed(seed)
+        self.waiting: Deque[Request] = deque()
+        self.running: List[Request] = []
+        self.requests: Dict[int, Request] = {}
+        self.steps = self.preemptions = self.peak_running = self.peak_blocks = 0
+
+    # ---- public API ------------------------------------------------------------------------------------
+    def add_request(self, prompt: List[int], max_new_tokens: int, eos_id: Optional[int] = None,
+                    temperature: float = 0.0) -> int:
+        if not 0 < len(prompt) < self.cfg.max_seq_len:
+            raise ValueError(f"prompt length must be in 1..{self.cfg.max_seq_len - 1}")
+        if self.pool.blocks_for(len(prompt) + 1) > self.pool.allocator.num_blocks:
+            raise ValueError("prompt does not fit in the block pool")
+        req = Request(len(self.requests), list(prompt), max_new_tokens, eos_id, temperature)
+        self.requests[req.id] = req
+        self.waiting.append(req)
+        return req.id
+
+    def has_work(self) -> bool:
+        return bool(self.waiting or self.running)
+
+    def run(self) -> Dict[int, List[int]]:
+        """Step until every request is finished. Returns the generated tokens of each request."""
+        while self.has_work():
+            self.step()
+        return {rid: r.output for rid, r in self.requests.items()}
+
+    def step(self) -> None:
+        self.steps += 1
+        if self.waiting and len(self.running) < self.max_batch and self._try_prefill():
+            pass
+        elif self.running:
+            self._decode()
+        elif self.waiting:
+            raise RuntimeError("the head request cannot be scheduled: the block pool is too small")
+        used = self.pool.allocator.num_blocks - self.pool.allocator.num_free
+        self.peak_running = max(self.peak_running, len(self.running))
+        self.peak_blocks = max(self.peak_blocks, used)
+
+    # ---- scheduling ------------------------------------------------------------------------------------
+    def _try_prefill(self) -> bool:
+        req = self.waiting[0]
+        tokens = req.prompt + req.output             # after a preemption this includes earlier output
+        need = self.pool.blocks_for(len(tokens))
+        if need > self.pool.allocator.num_free:
+            return False
+        self.waiting.popleft()
+        req.blocks = self.pool.allocator.allocate(need)
+        positions = torch.arange(len(tokens))[None]
+        views = self.pool.views(torch.tensor([req.blocks]), positions)
+        logits = self.model(torch.tensor([tokens]), positions, views, last_only=True)
+        req.cached = len(tokens)
+        self._append(req, self._sample_rows(logits[:, -1], [req])[0])
+        if not req.finished:
+            self.running.append(req)
+        return True
+
+    def _grant_blocks(self) -> None:
+        """Every running request writes one token at position `cached`; give a block to those that need one,
+        preempting the most recently started request while the pool is empty (engine.py:100-120)."""
+        bs = self.pool.block_size
+        i = 0
+        while i < len(self.running):
+            req = self.running[i]
+            if req.cached % bs == 0 and req.cached // bs == len(req.blocks):
+                if self.pool.allocator.num_free == 0:
+                    if len(self.running) == 1:
+                        raise RuntimeError("the block pool is too small to hold even one sequence of this length")
+                    victim = self.running.pop()
+                    self.pool.allocator.release(victim.blocks)
+                    victim.blocks, victim.cached = [], 0
+                    self.waiting.appendleft(victim)
+                    self.preemptions += 1
+                    if victim is not req and not self.running:
+                        return
+                    continue                             # retry: a block is free now (or req itself left)
+                req.blocks += self.pool.allocator.allocate(1)
+            i += 1
+
+    def _decode(self) -> None:
+        self._grant_blocks()
+        if not self.running:
+            return
+        width = max(len(r.blocks) for r in self.running)
+        tables = torch.tensor([r.blocks + [0] * (width - len(r.blocks)) for r in self.running])
+        positions = torch.tensor([[r.cached] for r in self.running])
+        idx = torch.tensor([[r.output[-1]] for r in self.running])
+        logits = self.model(idx, positions, self.pool.views(tables, positions), last_only=True)
+        rows = list(self.running)
+        tokens = self._sample_rows(logits[:, -1], rows)
+        for req, tok in zip(rows, tokens):
+            req.cached += 1
+            self._append(req, tok)
+            if req.finished:
+                self.running.remove(req)
+
+    def _sample_rows(self, logits: torch.Tensor, reqs: List[Request]) -> List[int]:
+        """One token per row of logits (R, V): greedy rows by one argmax kernel, the others from the engine's
+        generator in row order."""
+        greedy = ops.argmax(logits).cpu().tolist()
+        out = []
+        for r, req in enumerate(reqs):
+            if req.temperature == 0:
+                out.append(int(greedy[r]))
+            else:
+                probs = F.softmax(logits[r].float() / req.temperature, dim=-1).cpu()
+                out.append(int(torch.multinomial(probs[None], 1, generator=self.generator)[0, 0]))
+        return out
+
+    def _append(self, req: Request, token: int) -> None:
+        req.output.append(token)
+        total = len(req.prompt) + len(req.output)
+        if len(req.output) >= req.max_new_tokens or token == req.eos_id or total >= self.cfg.max_seq_len:
+            req.finished = True
+            self.pool.allocator.release(req.blocks)
+            req.blocks = []

@@ -1,0 +1,233 @@
+"""Pipeline parallelism (forgeserve/pipeline.py:26-137): consecutive layer ranges per stage, one process (one
+GPU) per stage, GPipe micro-batches flowing stage to stage.
+
+Kept from the reference: the stage split, which stage holds the embedding and the head, the micro-batch rows
+(torch.tensor_split of the batch), one KV cache per (micro-batch, local layer), positions
+state.length + arange(t) for every row, logits for every position on the last stage, and the generation loop
+(last stage samples, tokens broadcast from it).
+
+B200 specifics: a stage's layers run as sm_100a kernels on its GPU; activations move by NCCL send/recv over
+NVLink (see transport.py) with every receive posted up front, so micro-batch i+1's compute is enqueued while
+micro-batch i is in flight; the last stage writes each micro-batch's logits into one preallocated output
+instead of concatenating at the end; optional CUDA events per micro-batch measure the real bubble.
+"""
+
+from typing import Dict, List, Optional, Tuple
+
+import torch
+import torch.nn as nn
+
+from . import ops
+from .config import ModelConfig
+from .kv import ContiguousKV
+from .model import Block, RMSNorm, RopeTables, layer_forward_
+from .parallel import SINGLE
+from .sampling import sample
+from .transport import default_transport
+
+
+def stage_layers(n_layers: int, size: int) -> List[Tuple[int, int]]:
+    """Consecutive layer ranges [lo, hi), as even as possible (earlier stages take the extra layers)."""
+    if size > n_layers:
+        raise ValueError("more pipeline stages than layers")
+    base, extra = divmod(n_layers, size)
+    bounds = [0]
+    for r in range(size):
+        bounds.append(bounds[-1] + base + (r < extra))
+    return list(zip(bounds[:-1], bounds[1:]))
+
+
+def bubble_fraction(stages: int, microbatches: int) -> float:
+    """Share of stage time spent waiting while the pipeline fills and drains: (p - 1) / (m + p - 1)."""
+    return (stages - 1) / (microbatches + stages - 1)
+
+
+def microbatch_sizes(batch: int, microbatches: int) -> List[int]:
+    """Row counts of torch.arange(batch).tensor_split(microbatches): the first batch % m parts get one extra."""
+    base, extra = divmod(batch, microbatches)
+    return [base + (i < extra) for i in range(microbatches)]
+
+
+class PipelineStage(nn.Module):
+    """Stage `rank` of `size`: layers stage_layers(cfg.n_layers, size)[rank], the embedding on the first stage, the
+    final norm and an untied copy of the output head on the last (pipeline.py:44-58).
+
+    `device` / `dtype` build the stage in place (default: the current CUDA device if there is one, fp32).
+    `transport` defaults to the torch.distributed default group (or the thread's hub in run_in_threads)."""
+
+    def __init__(self, cfg: ModelConfig, rank: int, size: int, device=None, dtype=None, transport=None):
+        super().__init__()
+        self.cfg, self.rank, self.size = cfg, rank, size
+        self.lo, self.hi = stage_layers(cfg.n_layers, size)[rank]
+        self.is_first, self.is_last = rank == 0, rank == size - 1
+        if device is None:
+            device = torch.device("cuda", torch.cuda.current_device()) if torch.cuda.is_available() else "cpu"
+        f = dict(device=device, dtype=dtype)
+        self.layers = nn.ModuleList(Block(cfg, SINGLE, **f) for _ in range(self.hi - self.lo))
+        if self.is_first:
+            self.tok_emb = nn.Embedding(cfg.vocab_size, cfg.d_model, **f)
+        if self.is_last:
+            self.norm = RMSNorm(cfg.d_model, cfg.norm_eps, **f)
+            self.lm_head = nn.Linear(cfg.d_model, cfg.vocab_size, bias=False, **f)
+        self._rope = RopeTables(cfg)
+        self.register_buffer("rope_cos", self._rope.cos.to(device), persistent=False)
+        self.register_buffer("rope_sin", self._rope.sin.to(device), persistent=False)
+        self.transport = transport if transport is not None else default_transport()
+        self.trace: Optional[List] = None   # set to a list to record (mb, start, end) CUDA events per micro-batch
+
+    @property
+    def device(self) -> torch.device:
+        return self.rope_cos.device
+
+    @property
+    def dtype(self) -> torch.dtype:
+        return next(self.parameters()).dtype
+
+    def load_from_full(self, full: Dict[str, torch.Tensor]) -> None:
+        """Take this stage's weights out of a full model's state dict, renumbering layers.i -> layers.(i - lo)."""
+        own = {}
+        for name, w in full.items():
+            if name.startswith("layers."):
+                i = int(name.split(".")[1])
+                if self.lo <= i < self.hi:
+                    own[name.replace(f"layers.{i}.", f"layers.{i - self.lo}.", 1)] = w
+            elif (name == "tok_emb.weight" and self.is_first) or (name in ("norm.weight", "lm_head.weight")
+                                                                  and self.is_last):
+                own[name] = w
+        self.load_state_dict(own)
+
+    def _rope_tables(self):
+        return self._rope.on(self.device)
+
+    def run_layers_(self, x: torch.Tensor, positions: torch.Tensor, caches: List) -> torch.Tensor:
+        """The stage's layers on x (b, t, d) in place; positions (b, t) int64 on the stage's device."""
+        cos, sin = self._rope_tables()
+        for layer, kv in zip(self.layers, caches):
+            layer_forward_(layer, x, positions, kv, cos, sin)
+        return x
+
+    @torch.no_grad()
+    def run_layers(self, x, positions, caches: List[ContiguousKV]):
+        ops.require_cuda(x)
+        pos = torch.as_tensor(positions).to(device=x.device, dtype=torch.int64).contiguous()
+        return self.run_layers_(x.contiguous().clone(), pos, caches)
+
+    def embed(self, idx: torch.Tensor) -> torch.Tensor:
+        return ops.embed(idx, self.tok_emb.weight)
+
+    def head(self, x: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+        return ops.linear(ops.rmsnorm(x, self.norm.weight, self.norm.eps), self.lm_head.weight, out=out)
+
+
+class PipelineState:
+    """One KV cache per local layer for each micro-batch (each micro-batch is a fixed set of batch rows)."""
+
+    def __init__(self, stage: PipelineStage, batch: int, microbatches: int):
+        self.sizes = microbatch_sizes(batch, microbatches)
+        self.caches = [[ContiguousKV(stage.cfg.max_seq_len) for _ in stage.layers] for _ in self.sizes]
+        self._length = 0
+
+    @property
+    def length(self) -> int:
+        return self.caches[0][0].length if self.caches[0] else self._length
+
+
+_POS_CACHE: Dict[Tuple, torch.Tensor] = {}
+
+
+def _positions(start: int, t: int, rows: int, device) -> torch.Tensor:
+    key = (str(device), start, t, rows)
+    p = _POS_CACHE.get(key)
+    if p is None:
+        if len(_POS_CACHE) > 256:
+            _POS_CACHE.clear()
+        p = (start + torch.arange(t, dtype=torch.int64))[None, :].expand(rows, t).contiguous().to(device)
+        _POS_CACHE[key] = p
+    return p
+
+
+@torch.no_grad()
+def pipeline_forward(stage: PipelineStage, state: PipelineState, idx: Optional[torch.Tensor], t: int,
+                     last_only: bool = False):
+    """Push t new tokens per row through the pipeline. `idx` (B, t) is needed on stage 0 only.
+
+    Returns the logits (B, t, vocab) on the last stage (on its device) and None elsewhere.
+    last_only=True computes the head for the last position only and returns (B, 1, vocab)."""
+    cfg = stage.cfg
+    start = state.length
+    if start + t > cfg.max_seq_len:
+        raise IndexError(f"positions up to {start + t - 1} exceed the rotary table of max_seq_len {cfg.max_seq_len}")
+    dev = stage.device
+    tr = stage.transport
+    batch = sum(state.sizes)
+    d = cfg.d_model
+    act_dtype = stage.dtype
+    recvs = {}
+    if not stage.is_first and all(state.sizes):
+        for mb, size in enumerate(state.sizes):
+            buf = torch.empty(size, t, d, dtype=act_dtype, device=dev)
+            recvs[mb] = (tr.irecv(buf, stage.rank - 1), buf)
+    if stage.is_first:
+        idx = torch.as_tensor(idx)
+        if idx.shape != (batch, t):
+            raise ValueError(f"idx must have shape ({batch}, {t})")
+        if idx.device.type == "cpu" and idx.numel() and (int(idx.min()) < 0 or int(idx.max()) >= cfg.vocab_size):
+            raise IndexError("token id out of range for the embedding")
+        idx = idx.to(device=dev, dtype=torch.int64, non_blocking=True)
+    out = None
+    if stage.is_last:
+        out = torch.empty(batch, 1 if last_only else t, cfg.vocab_size, dtype=act_dtype, device=dev)
+    stream = torch.cuda.current_stream(dev) if stage.trace is not None else None
+    if any(size == 0 for size in state.sizes):
+        # The reference fails on a zero-row micro-batch (its attention reshapes an empty tensor,
+        # forgeserve/model.py:77); refuse up front, on every stage, instead of part-way through.
+        raise RuntimeError(f"more micro-batches ({len(state.sizes)}) than batch rows ({batch})")
+    sends, row = [], 0
+    for mb, size in enumerate(state.sizes):
+        if stage.is_first:
+            x = stage.embed(idx[row : row + size])
+        else:
+            work, x = recvs.pop(mb)
+            work.wait()
+        if stage.trace is not None:
+            e0 = torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+        stage.run_layers_(x, _positions(start, t, size, dev), state.caches[mb])
+        if stage.is_last:
+            stage.head(x[:, -1:] if last_only else x, out=out[row : row + size])
+        else:
+            sends.append(tr.isend(x, stage.rank + 1))
+        if stage.trace is not None:
+            e1 = torch.cuda.Event(enable_timing=True)
+            e1.record(stream)
+            stage.trace.append((mb, e0, e1))
+        row += size
+    for work in sends:
+        work.wait()
+    if not state.caches[0]:
+        state._length = start + t
+    return out
+
+
+@torch.no_grad()
+def pipeline_generate(stage: PipelineStage, prompt: torch.Tensor, max_new_tokens: int, microbatches: int = 1,
+                      temperature: float = 0.0, generator=None) -> torch.Tensor:
+    """Generate with the pipeline. Every stage calls this with the same `prompt` (B, T) and gets the same result
+    (on the prompt's device). The last stage samples; the tokens are broadcast from it (pipeline.py:121-137)."""
+    b, t = prompt.shape
+    max_new_tokens = min(max_new_tokens, stage.cfg.max_seq_len - t)
+    state = PipelineState(stage, b, microbatches)
+    dev = stage.device
+    toks = torch.empty(b, t + max(max_new_tokens, 0), dtype=torch.int64, device=dev)
+    toks[:, :t].copy_(prompt.to(dev))
+    idx, new = toks[:, :t], t
+    for i in range(max_new_tokens):
+        logits = pipeline_forward(stage, state, idx if stage.is_first else None, new, last_only=True)
+        if stage.is_last:
+            nxt = sample(logits[:, -1], temperature, generator).to(torch.int64)
+        else:
+            nxt = torch.empty(b, dtype=torch.int64, device=dev)
+        stage.transport.broadcast(nxt, src=stage.size - 1)
+        toks[:, t + i].copy_(nxt)
+        idx, new = toks[:, t + i : t + i + 1], 1
+    return toks.to(prompt.device)

@@ -1,0 +1,84 @@
+"""Seeded weights in the reference's state-dict format, generated per tensor.
+
+Every tensor is drawn from its own generator, seeded from (seed, tensor name), so a pipeline stage can build
+exactly its own layers — on its GPU, without materialising the full model — and still hold the same values
+as a single-process model built from the same seed. Names are the reference's state-dict keys
+(forgeserve/model.py:109-138; `lm_head.weight` equals `tok_emb.weight`, as ForgeModel ties them).
+"""
+
+import hashlib
+from typing import Dict, Iterable, Optional
+
+import torch
+
+from .config import ModelConfig
+
+
+def layer_shapes(cfg: ModelConfig, i: int) -> Dict[str, tuple]:
+    d, hd = cfg.d_model, cfg.head_dim
+    p = f"layers.{i}."
+    return {
+        p + "attn_norm.weight": (d,),
+        p + "attn.wq.weight": (cfg.n_heads * hd, d),
+        p + "attn.wk.weight": (cfg.n_kv_heads * hd, d),
+        p + "attn.wv.weight": (cfg.n_kv_heads * hd, d),
+        p + "attn.wo.weight": (d, cfg.n_heads * hd),
+        p + "mlp_norm.weight": (d,),
+        p + "mlp.w_gate.weight": (cfg.ffn_dim, d),
+        p + "mlp.w_up.weight": (cfg.ffn_dim, d),
+        p + "mlp.w_down.weight": (d, cfg.ffn_dim),
+    }
+
+
+def model_shapes(cfg: ModelConfig) -> Dict[str, tuple]:
+    shapes = {"tok_emb.weight": (cfg.vocab_size, cfg.d_model)}
+    for i in range(cfg.n_layers):
+        shapes.update(layer_shapes(cfg, i))
+    shapes["norm.weight"] = (cfg.d_model,)
+    shapes["lm_head.weight"] = (cfg.vocab_size, cfg.d_model)
+    return shapes
+
+
+def _tensor_seed(seed: int, name: str) -> int:
+    h = hashlib.sha256(f"{seed}:{name}".encode()).digest()
+    return int.from_bytes(h[:8], "little") & ((1 << 63) - 1)
+
+
+def seeded_tensor(name: str, shape: tuple, seed: int, std: float, device="cpu", dtype=torch.float32) -> torch.Tensor:
+    """Norm weights are ones (the reference's RMSNorm init); matrices are N(0, std^2)."""
+    if name.endswith("norm.weight"):
+        return torch.ones(shape, device=device, dtype=dtype)
+    if name == "lm_head.weight":
+        name = "tok_emb.weight"
+    g = torch.Generator(device=device).manual_seed(_tensor_seed(seed, name))
+    t = torch.empty(shape, device=device, dtype=torch.float32)
+    t.normal_(0.0, std, generator=g)
+    return t.to(dtype)
+
+
+def seeded_state_dict(cfg: ModelConfig, seed: int = 0, std: float = 0.02, names: Optional[Iterable[str]] = None,
+                      device="cpu", dtype=torch.float32) -> Dict[str, torch.Tensor]:
+    shapes = model_shapes(cfg)
+    keys = list(shapes) if names is None else list(names)
+    return {k: seeded_tensor(k, shapes[k], seed, std, device, dtype) for k in keys}
+
+
+@torch.no_grad()
+def init_stage_(stage, seed: int = 0, std: float = 0.02) -> None:
+    """Fill a PipelineStage with the seeded weights of its own layers (global layer numbering), on its device."""
+    shapes = model_shapes(stage.cfg)
+    for name, p in stage.named_parameters():
+        if name.startswith("layers."):
+            i = int(name.split(".")[1])
+            gname = name.replace(f"layers.{i}.", f"layers.{i + stage.lo}.", 1)
+        else:
+            gname = name
+        p.copy_(seeded_tensor(gname, shapes[gname], seed, std, device=p.device, dtype=p.dtype))
+
+
+@torch.no_grad()
+def init_model_(model, seed: int = 0, std: float = 0.02) -> None:
+    """Fill a ForgeModel with the same seeded weights (tied head = embedding)."""
+    shapes = model_shapes(model.cfg)
+    for name, p in model.named_parameters():
+        p.copy_(seeded_tensor(name, shapes[name], seed, std, device=p.device, dtype=p.dtype))

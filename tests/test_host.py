@@ -1,0 +1,143 @@
+"""Host-side logic of forgeserve_b200 that needs no GPU: configuration, stage split, micro-batch rows, block
+allocation, stage construction and weight loading, the fused-weight views, the export list."""
+
+import pytest
+import torch
+
+import forgeserve_b200 as fs
+from forgeserve_b200 import BlockAllocator, ModelConfig, OutOfBlocks, PipelineStage, bubble_fraction, stage_layers
+from forgeserve_b200.kv import ContiguousKV
+from forgeserve_b200.pipeline import microbatch_sizes
+from oracle import forge_oracle as O
+
+
+def small_cfg(**kw):
+    base = dict(vocab_size=64, d_model=64, n_layers=3, n_heads=8, n_kv_heads=4, max_seq_len=64)
+    base.update(kw)
+    return ModelConfig(**base)
+
+
+def test_export_list_matches_the_reference():
+    want = ["PipelineStage", "PipelineState", "bubble_fraction", "pipeline_forward", "pipeline_generate", "stage_layers",
+            "speculative_generate", "verify_draft", "Engine", "Request", "BlockAllocator", "OutOfBlocks", "PagedKVPool",
+            "ModelConfig", "ForgeModel", "TPContext", "SINGLE", "ContiguousKV", "new_contiguous_cache", "generate",
+            "sample"]
+    assert sorted(fs.__all__) == sorted(want)
+    for name in want:
+        assert hasattr(fs, name)
+
+
+def test_config_validation_and_defaults():
+    with pytest.raises(ValueError):
+        ModelConfig(d_model=100, n_heads=3)
+    with pytest.raises(ValueError):
+        ModelConfig(n_heads=8, n_kv_heads=3)
+    with pytest.raises(ValueError):
+        ModelConfig(d_model=24, n_heads=8, n_kv_heads=4)        # head_dim 3 is odd
+    with pytest.raises(ValueError):
+        small_cfg().check_tensor_parallel(3)
+    small_cfg().check_tensor_parallel(4)
+    for d in (64, 104, 136, 2048, 4096, 8192):
+        assert ModelConfig(d_model=d, n_heads=4, n_kv_heads=2).ffn_dim == O.Cfg(256, d, 1, 4, 2).ffn_dim
+    assert ModelConfig().to_dict()["ffn_dim"] == 384
+
+
+def test_stage_layers_and_bubble():
+    assert stage_layers(3, 3) == [(0, 1), (1, 2), (2, 3)]
+    assert stage_layers(7, 3) == [(0, 3), (3, 5), (5, 7)]
+    with pytest.raises(ValueError):
+        stage_layers(2, 3)
+    for n in range(1, 40):
+        for p in range(1, min(n, 9) + 1):
+            assert stage_layers(n, p) == O.stage_layers(n, p)
+    assert bubble_fraction(1, 5) == 0
+    assert bubble_fraction(4, 1) == 0.75
+    assert bubble_fraction(4, 13) == pytest.approx(3 / 16)
+    assert bubble_fraction(8, 16) == pytest.approx(7 / 23)
+
+
+def test_microbatch_rows_follow_tensor_split():
+    for b in range(0, 20):
+        for m in range(1, 10):
+            assert microbatch_sizes(b, m) == [len(c) for c in torch.arange(b).tensor_split(m)]
+
+
+def test_allocator_order_and_errors():
+    a = BlockAllocator(4)
+    got = a.allocate(3)
+    assert got == [0, 1, 2] and a.num_free == 1
+    with pytest.raises(OutOfBlocks):
+        a.allocate(2)
+    a.release(got)
+    assert a.num_free == 4
+    assert a.allocate(2) == [2, 1]            # last released first, as the reference's stack
+
+
+def test_stage_construction_and_load_from_full():
+    cfg = small_cfg(n_layers=5)
+    full = O.test_model_weights(O.Cfg(**{k: v for k, v in cfg.to_dict().items()}), seed=3)
+    total = sum(v.numel() for k, v in full.items() if k.startswith("layers."))
+    seen = 0
+    for rank, size in [(0, 2), (1, 2)]:
+        st = PipelineStage(cfg, rank, size, device="cpu")
+        st.load_from_full(full)
+        assert (st.lo, st.hi) == stage_layers(5, 2)[rank]
+        assert st.is_first == (rank == 0) and st.is_last == (rank == 1)
+        assert hasattr(st, "tok_emb") == st.is_first and hasattr(st, "lm_head") == st.is_last
+        for j, layer in enumerate(st.layers):
+            torch.testing.assert_close(layer.attn.wk.weight, full[f"layers.{st.lo + j}.attn.wk.weight"])
+        seen += sum(p.numel() for p in st.layers.parameters())
+    assert seen == total                       # every layer lives on exactly one stage
+
+
+def test_fused_projection_weights_are_views_of_the_parameters():
+    cfg = small_cfg()
+    st = PipelineStage(cfg, 0, 1, device="cpu")
+    full = O.test_model_weights(O.Cfg(**cfg.to_dict()), seed=4)
+    st.load_from_full(full)
+    blk = st.layers[1]
+    wqkv = blk.attn.wqkv()
+    torch.testing.assert_close(wqkv, torch.cat([full["layers.1.attn.wq.weight"], full["layers.1.attn.wk.weight"],
+                                                full["layers.1.attn.wv.weight"]]))
+    assert blk.attn.wq.weight.data_ptr() == wqkv.data_ptr()
+    assert blk.attn.wqkv() is wqkv                       # cached while the parameters still alias it
+    # loading new weights writes through the views into the fused tensor
+    full2 = O.test_model_weights(O.Cfg(**cfg.to_dict()), seed=5)
+    st.load_from_full(full2)
+    torch.testing.assert_close(blk.attn.wqkv()[: cfg.d_model], full2["layers.1.attn.wq.weight"])
+    wgu = blk.mlp.w_gate_up()
+    torch.testing.assert_close(wgu[cfg.ffn_dim:], full2["layers.1.mlp.w_up.weight"])
+    # the state dict keeps the reference's keys and shapes
+    sd = st.state_dict()
+    assert sd["layers.1.attn.wk.weight"].shape == (cfg.n_kv_heads * cfg.head_dim, cfg.d_model)
+    assert "layers.1.attn._wqkv" not in sd
+    # .to() replaces the parameters; the fused tensor is rebuilt from them
+    st = st.to(torch.bfloat16)
+    assert blk.attn.wqkv().dtype == torch.bfloat16
+
+
+def test_contiguous_cache_grows_and_truncates():
+    kv = ContiguousKV(max_len=10)
+    k = torch.randn(2, 3, 4, 5)
+    kall, _ = kv.update(k, k)
+    assert kall.shape == (2, 3, 4, 5) and kv.length == 4
+    kall, _ = kv.update(k[:, :, :1], k[:, :, :1])
+    assert kv.length == 5 and kv.capacity <= 10
+    torch.testing.assert_close(kall[:, :, :4], k)
+    kv.truncate(2)
+    assert kv.length == 2 and kv.k.shape[2] == 2
+
+
+def test_kernels_refuse_cpu_tensors():
+    from forgeserve_b200 import ops
+    with pytest.raises(RuntimeError, match="CUDA"):
+        ops.rmsnorm(torch.randn(2, 8), torch.ones(8), 1e-5)
+    with pytest.raises(RuntimeError, match="CUDA"):
+        fs.ForgeModel(small_cfg())(torch.zeros(1, 3, dtype=torch.long))
+
+
+def test_out_of_scope_names_refuse():
+    with pytest.raises(NotImplementedError):
+        fs.speculative_generate(None, None, None, 1)
+    with pytest.raises(NotImplementedError):
+        fs.ForgeModel(small_cfg(), fs.TPContext(0, 2))

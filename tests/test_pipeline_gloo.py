@@ -1,0 +1,113 @@
+"""The multi-process pipeline path on CPU: forgeserve_b200's own pipeline_forward / pipeline_generate schedule,
+stage split, micro-batch rows, transports and run_distributed, over gloo with world_size 2 and 3.
+
+The decoder math inside each stage is the oracle's (injected by subclassing the stage in this test file),
+because the product's kernels need a GPU; what is under test is everything around them. The logits are
+compared with the reference's own pipeline output (tests/golden/small.pt)."""
+
+from pathlib import Path
+
+import pytest
+import torch
+
+from oracle import forge_oracle as O
+
+GOLDEN = Path(__file__).resolve().parent / "golden"
+
+
+def _oracle_stage_class():
+    from forgeserve_b200 import PipelineStage
+
+    class OracleStage(PipelineStage):
+        """A PipelineStage whose compute is the CPU oracle (test-only)."""
+
+        def _ocfg(self):
+            return O.Cfg(**self.cfg.to_dict())
+
+        def embed(self, idx):
+            return self.tok_emb.weight.detach()[idx.cpu()].clone()
+
+        def run_layers_(self, x, positions, caches):
+            cfg = self._ocfg()
+            cos, sin = O.rope_tables(cfg.head_dim, cfg.max_seq_len, cfg.rope_theta)
+            for j, (layer, kv) in enumerate(zip(self.layers, caches)):
+                sd = {f"layers.0.{k}": v.detach() for k, v in layer.state_dict().items()}
+                x.copy_(O.block(sd, 0, x, cfg, cos, sin, positions, kv))
+            return x
+
+        def head(self, x, out=None):
+            y = O.head({"norm.weight": self.norm.weight.detach(), "lm_head.weight": self.lm_head.weight.detach()}, x,
+                       self._ocfg())
+            if out is None:
+                return y
+            out.copy_(y)
+            return out
+
+    return OracleStage
+
+
+def forward_worker(rank, size, cfg_dict, full_sd, idx, more, microbatches):
+    from forgeserve_b200 import ModelConfig, PipelineState, pipeline_forward
+    cfg = ModelConfig(**cfg_dict)
+    stage = _oracle_stage_class()(cfg, rank, size, device="cpu")
+    stage.load_from_full(full_sd)
+    state = PipelineState(stage, idx.shape[0], microbatches)
+    logits = pipeline_forward(stage, state, idx if rank == 0 else None, idx.shape[1])
+    logits2 = pipeline_forward(stage, state, more if rank == 0 else None, more.shape[1])
+    layer_params = sum(p.numel() for p in stage.layers.parameters())
+    return logits, logits2, layer_params
+
+
+def generate_worker(rank, size, cfg_dict, full_sd, prompt, microbatches, n):
+    import forgeserve_b200.pipeline as P
+    from forgeserve_b200 import ModelConfig
+    P.sample = lambda logits, temperature=0.0, generator=None: logits.argmax(-1)   # CPU greedy, test-only
+    cfg = ModelConfig(**cfg_dict)
+    stage = _oracle_stage_class()(cfg, rank, size, device="cpu")
+    stage.load_from_full(full_sd)
+    return P.pipeline_generate(stage, prompt, n, microbatches)
+
+
+def empty_microbatch_worker(rank, size, cfg_dict, full_sd, idx):
+    from forgeserve_b200 import ModelConfig, PipelineState, pipeline_forward
+    cfg = ModelConfig(**cfg_dict)
+    stage = _oracle_stage_class()(cfg, rank, size, device="cpu")
+    stage.load_from_full(full_sd)
+    state = PipelineState(stage, idx.shape[0], idx.shape[0] + 2)
+    return pipeline_forward(stage, state, idx if rank == 0 else None, idx.shape[1])
+
+
+@pytest.fixture(scope="module")
+def golden():
+    g = torch.load(GOLDEN / "small.pt", weights_only=False)
+    sd = O.test_model_weights(O.Cfg(**g["cfg"]), *g["weights"][1:])
+    return g, sd
+
+
+@pytest.mark.parametrize("size,microbatches", [(2, 1), (3, 2), (3, 4)])
+def test_pipeline_schedule_over_gloo_matches_reference(golden, size, microbatches):
+    from forgeserve_b200.tensor_parallel import run_distributed
+    g, sd = golden
+    res = run_distributed(forward_worker, size, g["cfg"], sd, g["idx"], g["more"], microbatches, backend="gloo")
+    logits, logits2, _ = res[-1]
+    want, want2 = g["pipeline"][(size, microbatches)]
+    torch.testing.assert_close(logits, want, atol=1e-4, rtol=1e-4)
+    torch.testing.assert_close(logits2, want2, atol=1e-4, rtol=1e-4)    # continued through the stage caches
+    assert all(r[0] is None and r[1] is None for r in res[:-1])
+    total = sum(v.numel() for k, v in sd.items() if k.startswith("layers."))
+    assert sum(r[2] for r in res) == total
+
+
+def test_pipeline_generation_over_gloo_matches_reference(golden):
+    from forgeserve_b200.tensor_parallel import run_distributed
+    g, sd = golden
+    res = run_distributed(generate_worker, 2, g["cfg"], sd, g["prompt"], 2, 10, backend="gloo")
+    for out in res:
+        assert torch.equal(out, g["generate"])
+
+
+def test_more_microbatches_than_rows_is_refused_on_every_rank(golden):
+    from forgeserve_b200.tensor_parallel import run_distributed
+    g, sd = golden
+    with pytest.raises(RuntimeError, match="micro-batches"):
+        run_distributed(empty_microbatch_worker, 2, g["cfg"], sd, g["idx"][:2], backend="gloo", timeout=60)
