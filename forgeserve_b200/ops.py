@@ -170,11 +170,15 @@ def argmax(x: torch.Tensor) -> torch.Tensor:
 def contiguous_desc(k: torch.Tensor, v: torch.Tensor, table: torch.Tensor) -> L.KVCacheDesc:
     """Descriptor of a per-row cache k, v of shape (B, nkv, capacity, hd) (contiguous); table = arange(B)."""
     B, nkv, cap, hd = k.shape
-    return L.KVCacheDesc(k.data_ptr(), v.data_ptr(), table.data_ptr(), 1, 1, cap, nkv * cap * hd, cap * hd, B)
+    desc = L.KVCacheDesc(k.data_ptr(), v.data_ptr(), table.data_ptr(), 1, 1, cap, nkv * cap * hd, cap * hd, B)
+    desc.keep = (k, v, table)          # the descriptor holds raw pointers: keep the tensors alive with it
+    return desc
 
 
 def paged_desc(k: torch.Tensor, v: torch.Tensor, table: torch.Tensor) -> L.KVCacheDesc:
     """Descriptor of a paged pool k, v of shape (num_blocks, nkv, block_size, hd); table (B, nb) int64."""
     nblk, nkv, bs, hd = k.shape
-    return L.KVCacheDesc(k.data_ptr(), v.data_ptr(), table.data_ptr(), table.stride(0), table.shape[1], bs,
+    desc = L.KVCacheDesc(k.data_ptr(), v.data_ptr(), table.data_ptr(), table.stride(0), table.shape[1], bs,
                          nkv * bs * hd, bs * hd, nblk)
+    desc.keep = (k, v, table)
+    return desc
