@@ -139,6 +139,72 @@ __global__ void rope_kv_kernel(T* __restrict__ qkv, int64_t ld, const float* __r
   }
 }
 
+// Vectorised bf16 variant for head_dim % 16 == 0: each work item moves 8 elements (16 bytes) of x1 and the
+// matching 8 of x2 (rotation) or 8 values of v (copy); same arithmetic and rounding as rope_kv_kernel.
+__global__ void __launch_bounds__(256)
+    rope_kv_vec_kernel(__nv_bfloat16* __restrict__ qkv, int64_t ld, const float* __restrict__ cos_t,
+                       const float* __restrict__ sin_t, int rope_rows, const int64_t* __restrict__ positions,
+                       KVCache kv, int T_new, int nh, int nkv, int hd, int64_t slot_base, int slot_from_pos,
+                       unsigned* err) {
+  using bf = __nv_bfloat16;
+  const int64_t tok = blockIdx.x;
+  const int r = static_cast<int>(tok / T_new), j = static_cast<int>(tok % T_new);
+  const int64_t pos = positions[tok];
+  if (pos < 0 || pos >= rope_rows) {
+    if (threadIdx.x == 0) flag_error(err, ERR_BAD_POSITION);
+    return;
+  }
+  const int half = hd / 2, cph = half / 8;   // 8-element chunks per half head
+  bf* row = qkv + tok * ld;
+  const int64_t slot = slot_from_pos ? pos : slot_base + j;
+  const int64_t blk_idx = slot / kv.block_size;
+  bool slot_ok = slot >= 0 && blk_idx < kv.table_cols;
+  const int64_t blk = slot_ok ? kv.table[static_cast<int64_t>(r) * kv.table_stride + blk_idx] : -1;
+  slot_ok = slot_ok && blk >= 0 && blk < kv.num_blocks;
+  if (!slot_ok && threadIdx.x == 0) flag_error(err, ERR_BAD_SLOT);
+  const int64_t slot_off = slot_ok ? blk * kv.block_stride + (slot % kv.block_size) * hd : 0;
+  const float* cr = cos_t + pos * half;
+  const float* sr = sin_t + pos * half;
+  const int rot = (nh + nkv) * cph, vchunks = nkv * hd / 8;
+  for (int i = threadIdx.x; i < rot + vchunks; i += blockDim.x) {
+    if (i < rot) {
+      const int h = i / cph, d0 = (i % cph) * 8;
+      bf* base = row + h * hd;
+      const uint4 u1 = *reinterpret_cast<const uint4*>(base + d0);
+      const uint4 u2 = *reinterpret_cast<const uint4*>(base + half + d0);
+      const float4 c0 = *reinterpret_cast<const float4*>(cr + d0), c1 = *reinterpret_cast<const float4*>(cr + d0 + 4);
+      const float4 s0 = *reinterpret_cast<const float4*>(sr + d0), s1 = *reinterpret_cast<const float4*>(sr + d0 + 4);
+      const float cc[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
+      const float ss[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
+      const bf* e1 = reinterpret_cast<const bf*>(&u1);
+      const bf* e2 = reinterpret_cast<const bf*>(&u2);
+      uint4 o1, o2;
+      bf* f1 = reinterpret_cast<bf*>(&o1);
+      bf* f2 = reinterpret_cast<bf*>(&o2);
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        const float c = rnd<bf>(cc[k]), sn = rnd<bf>(ss[k]);
+        const float x1 = to_f(e1[k]), x2 = to_f(e2[k]);
+        f1[k] = from_f<bf>(rnd<bf>(x1 * c) - rnd<bf>(x2 * sn));
+        f2[k] = from_f<bf>(rnd<bf>(x2 * c) + rnd<bf>(x1 * sn));
+      }
+      if (h < nh) {
+        *reinterpret_cast<uint4*>(base + d0) = o1;
+        *reinterpret_cast<uint4*>(base + half + d0) = o2;
+      } else if (slot_ok) {
+        bf* dst = static_cast<bf*>(kv.k) + slot_off + static_cast<int64_t>(h - nh) * kv.head_stride;
+        *reinterpret_cast<uint4*>(dst + d0) = o1;
+        *reinterpret_cast<uint4*>(dst + half + d0) = o2;
+      }
+    } else if (slot_ok) {
+      const int c = i - rot;
+      const int g = (c * 8) / hd, d0 = (c * 8) % hd;
+      const uint4 val = *reinterpret_cast<const uint4*>(row + (nh + nkv) * hd + c * 8);
+      *reinterpret_cast<uint4*>(static_cast<bf*>(kv.v) + slot_off + static_cast<int64_t>(g) * kv.head_stride + d0) = val;
+    }
+  }
+}
+
 // ------------------------------------------------------------------- KV store from (B, h, T, d) tensors
 // The write half of PagedLayerView.update (forgeserve/paged.py:72-78): new k/v of shape (B, nkv, T, hd),
 // token (r, j) goes to slot positions[r, j].
@@ -279,6 +345,17 @@ int rope_kv_write(int dtype, void* qkv, int64_t ld, const float* cos_t, const fl
   if (hd % 2) return fail("rope: head_dim must be even");
   if (tokens > INT32_MAX) return fail("rope: too many tokens");
   const int th = 128;
+  const bool vec = dtype == BF16 && apply_rope && hd % 16 == 0 && ld % 8 == 0 && kv.block_stride % 8 == 0 &&
+                   kv.head_stride % 8 == 0 &&
+                   ((reinterpret_cast<uintptr_t>(qkv) | reinterpret_cast<uintptr_t>(kv.k) |
+                     reinterpret_cast<uintptr_t>(kv.v)) & 15) == 0;
+  if (vec) {
+    rope_kv_vec_kernel<<<static_cast<unsigned>(tokens), 256, 0, st>>>(
+        static_cast<__nv_bfloat16*>(qkv), ld, cos_t, sin_t, static_cast<int>(rope_rows), positions, kv,
+        static_cast<int>(T_new), static_cast<int>(nh), static_cast<int>(nkv), static_cast<int>(hd), slot_base,
+        slot_from_pos, error_word());
+    return check_launch("rope_kv_vec_kernel");
+  }
   if (dtype == F32)
     rope_kv_kernel<float><<<static_cast<unsigned>(tokens), th, 0, st>>>(
         static_cast<float*>(qkv), ld, cos_t, sin_t, static_cast<int>(rope_rows), positions, kv, static_cast<int>(T_new),

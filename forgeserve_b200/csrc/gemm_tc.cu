@@ -314,13 +314,24 @@ static int make_kmajor_map(CUtensorMap* map, const void* ptr, int64_t rows, int6
   return 0;
 }
 
+static int g_sm_budget[64] = {0};   // persistent-grid cap per device (0 = every SM)
+
 static int sm_count() {
   static int n[64] = {0};
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev < 0 || dev >= 64) dev = 0;
   if (!n[dev]) cudaDeviceGetAttribute(&n[dev], cudaDevAttrMultiProcessorCount, dev);
-  return n[dev] > 0 ? n[dev] : 148;
+  const int all = n[dev] > 0 ? n[dev] : 148;
+  return g_sm_budget[dev] > 0 && g_sm_budget[dev] < all ? g_sm_budget[dev] : all;
+}
+
+int set_persistent_sms(int n) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return fail("no current CUDA device");
+  if (n < 0) return fail("persistent SM budget must be >= 0");
+  g_sm_budget[dev] = n;
+  return 0;
 }
 
 bool supported(const void* A, int64_t lda, const void* B, int64_t ldb, int64_t K) {

@@ -58,6 +58,11 @@ def _rows(t: torch.Tensor):
     return rows, max(row_stride, n)
 
 
+def set_persistent_sms(n: int) -> None:
+    """Cap the persistent GEMM grid of the current CUDA device to n SMs (0 = all)."""
+    L.check(L.load().fs_set_persistent_sms(int(n)), "fs_set_persistent_sms")
+
+
 def rmsnorm(x: torch.Tensor, w: torch.Tensor, eps: float, out: Optional[torch.Tensor] = None) -> torch.Tensor:
     """RMSNorm over the last dim (forgeserve/model.py:29-31)."""
     require_cuda(x, w)

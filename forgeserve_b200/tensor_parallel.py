@@ -13,6 +13,7 @@ activations through a LocalHub (transport.py): a way to run a multi-stage pipeli
 
 import datetime
 import os
+import pickle
 import socket
 import threading
 import traceback
@@ -45,7 +46,9 @@ def _worker(rank: int, size: int, port: int, backend: str, pg_timeout: float, fn
         kwargs["device_id"] = torch.device("cuda", torch.cuda.current_device())
     try:
         dist.init_process_group(backend, **kwargs)
-        queue.put((rank, fn(rank, size, *args), None))
+        # pickled to bytes here: a tensor put on the queue as-is is shared through a file descriptor that the
+        # parent can only fetch while this process is still alive
+        queue.put((rank, pickle.dumps(fn(rank, size, *args)), None))
     except BaseException:
         queue.put((rank, None, traceback.format_exc()))
     finally:
@@ -74,7 +77,7 @@ def run_distributed(fn: Callable, size: int, *args, timeout: float = 180.0, back
             if err is not None:
                 error = f"rank {rank} failed:\n{err}"
                 break
-            results[rank] = res
+            results[rank] = pickle.loads(res)
     except Exception as e:       # timeout: some rank is stuck, usually waiting for a peer
         error = f"no result within {timeout}s ({type(e).__name__})"
     finally:

@@ -11,6 +11,7 @@ handed over by reference through queues, and every stage thread uses the same CU
 which the threads enqueue work is the order in which it runs.
 """
 
+import os
 import queue
 import threading
 from typing import Dict, Optional, Tuple
@@ -37,29 +38,65 @@ class _HostStagedRecv:
         return True
 
 
+# One process group per pair of neighbouring ranks, shared by every DistTransport of the process. With one
+# communicator (and NCCL stream) per pair, a stage's receives from rank-1 and its sends to rank+1 never queue
+# behind each other; on a single group NCCL serialises all point-to-point ops of a rank on one stream.
+_PAIR_GROUPS: Dict[int, list] = {}
+
+# NCCL kernels stay resident on the SMs they run on while a receive waits for its data. Pipeline stages keep a
+# few SMs out of the persistent GEMM grid for them, and cap NCCL's point-to-point channels to match.
+COMM_SMS = int(os.environ.get("FORGESERVE_COMM_SMS", "4"))
+
+
+def _pair_groups():
+    world = dist.get_world_size()
+    if world not in _PAIR_GROUPS:
+        os.environ.setdefault("NCCL_MAX_P2P_NCHANNELS", str(max(COMM_SMS, 1)))
+        # every rank creates every pair group, in the same order (new_group is collective over the world)
+        _PAIR_GROUPS[world] = [dist.new_group([i, i + 1]) for i in range(world - 1)]
+    return _PAIR_GROUPS[world]
+
+
 class DistTransport:
     def __init__(self, group=None):
         self.group = group
+        self.pairs = None
+        if group is None and dist.is_available() and dist.is_initialized() and dist.get_world_size() > 1:
+            self.pairs = _pair_groups()
+            if dist.get_backend() == "nccl" and torch.cuda.is_available():
+                from . import ops
+                sms = torch.cuda.get_device_properties(torch.cuda.current_device()).multi_processor_count
+                ops.set_persistent_sms(max(sms - COMM_SMS, 1))
 
-    @property
-    def host_staged(self) -> bool:
-        return dist.get_backend(self.group) == "gloo"
+    def _group_with(self, peer: int):
+        if self.pairs is None:
+            return self.group
+        me = dist.get_rank()
+        lo = min(me, peer)
+        if abs(me - peer) != 1:
+            return self.group
+        return self.pairs[lo]
+
+    def _host_staged(self, group) -> bool:
+        return dist.get_backend(group) == "gloo"
 
     def isend(self, t: torch.Tensor, dst: int):
-        if t.is_cuda and self.host_staged:
+        g = self._group_with(dst)
+        if t.is_cuda and self._host_staged(g):
             host = t.to("cpu")
-            work = dist.isend(host, dst=dst, group=self.group)
+            work = dist.isend(host, dst=dst, group=g)
             return _KeepAlive(work, host)
-        return _KeepAlive(dist.isend(t, dst=dst, group=self.group), t)
+        return _KeepAlive(dist.isend(t, dst=dst, group=g), t)
 
     def irecv(self, buf: torch.Tensor, src: int):
-        if buf.is_cuda and self.host_staged:
+        g = self._group_with(src)
+        if buf.is_cuda and self._host_staged(g):
             host = torch.empty(buf.shape, dtype=buf.dtype)
-            return _HostStagedRecv(dist.irecv(host, src=src, group=self.group), host, buf)
-        return dist.irecv(buf, src=src, group=self.group)
+            return _HostStagedRecv(dist.irecv(host, src=src, group=g), host, buf)
+        return dist.irecv(buf, src=src, group=g)
 
     def broadcast(self, t: torch.Tensor, src: int) -> None:
-        if t.is_cuda and self.host_staged:
+        if t.is_cuda and self._host_staged(self.group):
             host = t.to("cpu")
             dist.broadcast(host, src=src, group=self.group)
             t.copy_(host)

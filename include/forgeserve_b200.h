@@ -35,6 +35,11 @@ int fs_device_error(int clear, unsigned* out_bits);
 /* Number of kernel launches made by this library in this process (all devices). */
 int64_t fs_launch_count(void);
 
+/* Caps the number of SMs the persistent tensor-core GEMM spreads over on the current device (0 = all).
+ * A pipeline stage that overlaps NCCL send/recv with compute leaves a few SMs to the NCCL kernels this way, so
+ * that no GEMM CTA waits behind a resident communication kernel. No counterpart in the reference (CPU/gloo). */
+int fs_set_persistent_sms(int n);
+
 /* RMSNorm over rows: y = T(T(x * rsqrt(mean(x^2) + eps)) * w), fp32 statistics.
  * Replaces RMSNorm.forward, forgeserve/model.py:29-31. y may alias x. */
 int fs_rmsnorm(const void* x, int64_t x_stride, const void* w, void* y, int64_t y_stride, int64_t rows, int64_t dim,
