@@ -169,6 +169,13 @@ def run_ours(args):
     gemm_flops = sum(f for _, _, f in ops.gemm_events)
     gemm_ms = sum(a.elapsed_time(b) for a, b, _ in ops.gemm_events)
     gemm_n = len(ops.gemm_events)
+    per_rank = {"rank": rank, "gemm_tflops": round(gemm_flops / max(gemm_ms, 1e-9) / 1e9, 1),
+                "busy_ms": round(busy_ms, 1), "elapsed_ms": round(ms_total, 1)}
+    if world > 1:
+        gathered = [None] * world
+        dist.all_gather_object(gathered, per_rank)
+    else:
+        gathered = [per_rank]
     gemm_flops = allreduce(gemm_flops, dist.ReduceOp.SUM if world > 1 else None)
     gemm_ms = allreduce(gemm_ms, dist.ReduceOp.SUM if world > 1 else None)
     gemm_n = allreduce(gemm_n, dist.ReduceOp.SUM if world > 1 else None)
@@ -221,6 +228,7 @@ def run_ours(args):
             "e2e": {"value": round(tokens_per_step * args.steps / (e2e_ms / 1e3), 1), "unit": "tokens/s",
                     "h2d_bytes_per_step": idx_host.numel() * idx_host.element_size(),
                     "d2h_bytes_per_step": batch * cfg.vocab_size * 2},
+            "per_rank": gathered,
             "gpu_launches": int(launches),
             "clocks": clocks,
         }

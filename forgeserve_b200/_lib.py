@@ -13,6 +13,7 @@ LIB_PATH = Path(__file__).resolve().with_name("libforgeserve_b200.so")
 FS_F32, FS_BF16 = 0, 1
 FS_EPI_STORE, FS_EPI_RESIDUAL, FS_EPI_SWIGLU = 0, 1, 2
 FS_ERR_WAIT_TIMEOUT, FS_ERR_BAD_TOKEN, FS_ERR_BAD_SLOT, FS_ERR_BAD_POSITION = 1, 2, 4, 8
+FS_ATTN_AUTO, FS_ATTN_CUDA_CORE, FS_ATTN_MMA_SYNC, FS_ATTN_TCGEN05 = 0, 1, 2, 3
 
 c_i64, c_int, c_float, c_vp = ctypes.c_int64, ctypes.c_int, ctypes.c_float, ctypes.c_void_p
 
@@ -51,8 +52,8 @@ SIGNATURES = {
     "fs_paged_gather": (c_int, [c_vp, c_vp, c_i64, c_i64, c_i64, c_i64, c_i64, c_i64, c_vp, c_int, c_vp]),
     "fs_attention": (c_int, [c_vp, c_i64, ctypes.POINTER(KVCacheDesc), c_i64, c_vp, c_vp, c_i64, c_i64, c_i64, c_i64,
                              c_i64, c_i64, c_float, c_int, c_vp]),
-    "fs_attention_generic": (c_int, [c_vp, c_i64, ctypes.POINTER(KVCacheDesc), c_i64, c_vp, c_vp, c_i64, c_i64, c_i64,
-                                     c_i64, c_i64, c_i64, c_float, c_int, c_vp]),
+    "fs_attention_impl": (c_int, [c_vp, c_i64, ctypes.POINTER(KVCacheDesc), c_i64, c_vp, c_vp, c_i64, c_i64, c_i64,
+                                  c_i64, c_i64, c_i64, c_float, c_int, c_int, c_vp]),
     "fs_embed": (c_int, [c_vp, c_i64, c_vp, c_i64, c_i64, c_vp, c_int, c_vp]),
     "fs_argmax": (c_int, [c_vp, c_i64, c_i64, c_i64, c_vp, c_int, c_vp]),
 }

@@ -161,7 +161,7 @@ int fs_paged_gather(const void* pool, const int64_t* table, int64_t B, int64_t n
   return paged_gather(dtype, pool, table, B, nb, num_blocks, nkv, block_size, hd, out, static_cast<cudaStream_t>(stream));
 }
 
-static int attention_common(int force_generic, const void* q, int64_t ldq, const fs_kv_cache* kv, int64_t n_slots,
+static int attention_common(int impl, const void* q, int64_t ldq, const fs_kv_cache* kv, int64_t n_slots,
                             const int64_t* positions, void* out, int64_t ldo, int64_t B, int64_t T, int64_t nh,
                             int64_t nkv, int64_t hd, float scale, int dtype, void* stream) {
   if (B * T <= 0) return 0;
@@ -169,8 +169,9 @@ static int attention_common(int force_generic, const void* q, int64_t ldq, const
   if (!q || !positions || !out) return fail("fs_attention: NULL pointer");
   if (n_slots <= 0) return fail("fs_attention: the cache view has no slots");
   if (ldq < nh * hd || ldo < nh * hd) return fail("fs_attention: row stride too small");
-  return attention(dtype, q, ldq, to_internal(kv), n_slots, positions, out, ldo, B, T, nh, nkv, hd, scale,
-                   force_generic, static_cast<cudaStream_t>(stream));
+  if (impl < 0 || impl > 3) return fail("fs_attention: unknown kernel selector");
+  return attention(dtype, q, ldq, to_internal(kv), n_slots, positions, out, ldo, B, T, nh, nkv, hd, scale, impl,
+                   static_cast<cudaStream_t>(stream));
 }
 
 int fs_attention(const void* q, int64_t ldq, const fs_kv_cache* kv, int64_t n_slots, const int64_t* positions,
@@ -179,10 +180,10 @@ int fs_attention(const void* q, int64_t ldq, const fs_kv_cache* kv, int64_t n_sl
   return attention_common(0, q, ldq, kv, n_slots, positions, out, ldo, B, T, nh, nkv, hd, scale, dtype, stream);
 }
 
-int fs_attention_generic(const void* q, int64_t ldq, const fs_kv_cache* kv, int64_t n_slots, const int64_t* positions,
-                         void* out, int64_t ldo, int64_t B, int64_t T, int64_t nh, int64_t nkv, int64_t hd,
-                         float scale, int dtype, void* stream) {
-  return attention_common(1, q, ldq, kv, n_slots, positions, out, ldo, B, T, nh, nkv, hd, scale, dtype, stream);
+int fs_attention_impl(const void* q, int64_t ldq, const fs_kv_cache* kv, int64_t n_slots, const int64_t* positions,
+                      void* out, int64_t ldo, int64_t B, int64_t T, int64_t nh, int64_t nkv, int64_t hd, float scale,
+                      int impl, int dtype, void* stream) {
+  return attention_common(impl, q, ldq, kv, n_slots, positions, out, ldo, B, T, nh, nkv, hd, scale, dtype, stream);
 }
 
 int fs_embed(const int64_t* ids, int64_t n, const void* table, int64_t vocab, int64_t dim, void* out, int dtype,

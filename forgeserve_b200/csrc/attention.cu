@@ -10,9 +10,11 @@
 // Kernels:
 //   attn_generic_kernel  CUDA cores, fp32 or bf16, any even hd <= 256, online softmax over chunks of keys.
 //                        Used for the fp32 parity mode and for shapes the tensor-core kernel does not cover.
-//   attn_fa_kernel<HD>   bf16, hd in {64, 128}: 64 queries x 64 keys tiles, QK^T and PV on tensor cores
-//                        (mma.m16n8k16, fp32 accumulate), K/V rows fetched with cp.async through the block
-//                        table into double-buffered, XOR-swizzled shared memory, online softmax in registers.
+//   attn_fa_kernel<HD>   bf16, hd in {64, 128}: 64 queries x 64 keys tiles, QK^T and PV on the legacy mma.sync
+//                        tensor-core path (m16n8k16, fp32 accumulate), K/V rows fetched with cp.async through the
+//                        block table into double-buffered, XOR-swizzled shared memory. Used for short query blocks
+//                        (decode steps of several tokens) and block sizes the tcgen05 kernel cannot take.
+//   attention_tc.cu      the tcgen05/TMEM/TMA kernel used for prefill (T >= 64).
 #include "common.cuh"
 #include "kernels.h"
 
@@ -394,7 +396,7 @@ int launch_fa(const void* q, int64_t ldq, const KVCache& kv, int64_t n_slots, co
 
 int attention(int dtype, const void* q, int64_t ldq, const KVCache& kv, int64_t n_slots, const int64_t* positions,
               void* out, int64_t ldo, int64_t B, int64_t T, int64_t nh, int64_t nkv, int64_t hd, float scale,
-              int force_generic, cudaStream_t st) {
+              int impl, cudaStream_t st) {
   if (B <= 0 || T <= 0 || nh <= 0) return 0;
   if (nkv <= 0 || nh % nkv) return fail("attention: n_heads must be a multiple of n_kv_heads");
   if (hd <= 0 || hd > 256 || hd % 2) return fail("attention: head_dim must be even and <= 256");
@@ -402,9 +404,15 @@ int attention(int dtype, const void* q, int64_t ldq, const KVCache& kv, int64_t 
   const bool aligned = ((reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(out) |
                          reinterpret_cast<uintptr_t>(kv.k) | reinterpret_cast<uintptr_t>(kv.v)) & 15) == 0 &&
                        ldq % 8 == 0 && ldo % 8 == 0 && kv.block_stride % 8 == 0 && kv.head_stride % 8 == 0;
-  if (dtype == BF16 && !force_generic && aligned && T >= 16) {
+  const bool tc_ok = dtype == BF16 && attn_tc::supported(q, ldq, kv, hd, T);
+  const bool fa_ok = dtype == BF16 && aligned && (hd == 64 || hd == 128);
+  if (impl == 3 && !tc_ok) return fail("attention: the tcgen05 kernel does not support this layout");
+  if (impl == 2 && !fa_ok) return fail("attention: the mma.sync kernel does not support this layout");
+  if (impl == 3 || (impl == 0 && tc_ok && T >= 64))
+    return attn_tc::launch(q, ldq, kv, n_slots, positions, out, ldo, B, T, nh, nkv, hd, scale, st);
+  if (impl == 2 || (impl == 0 && fa_ok && T >= 16)) {
     if (hd == 128) return launch_fa<128>(q, ldq, kv, n_slots, positions, out, ldo, B, T, nh, nkv, scale, st);
-    if (hd == 64) return launch_fa<64>(q, ldq, kv, n_slots, positions, out, ldo, B, T, nh, nkv, scale, st);
+    return launch_fa<64>(q, ldq, kv, n_slots, positions, out, ldo, B, T, nh, nkv, scale, st);
   }
   dim3 grid(static_cast<unsigned>(B * T), static_cast<unsigned>(nh));
   if (dtype == F32)

@@ -1,0 +1,473 @@
+// Prefill attention on the 5th-generation tensor cores (tcgen05 + TMEM + TMA), bf16, head_dim 64 or 128.
+//
+// Same semantics as attention.cu (forgeserve/model.py:69-76): GQA (query head h reads KV head h / rep), key slot s
+// visible to a query at position p iff s <= p and s < n_slots, scale 1/sqrt(hd), output bf16.
+//
+// One CTA computes 128 queries of one head against the keys 0 .. min(n_slots, max position + 1) - 1, 128 keys per
+// step:
+//   warp 4      TMA producer: the Q tile once; per step the K and V tiles, fetched in 16-key boxes through the
+//               block table (a paged pool's blocks or a contiguous cache's one block per row), 2-stage ring
+//   warp 5      MMA issuer (one thread): S_j = Q K_j^T into one of two TMEM buffers; O += P_{j-1} V_{j-1} with
+//               P read from TMEM and V from shared memory (MN-major operand)
+//   warps 0-3   softmax, one thread per query row: S row from TMEM, causal mask, running max in the log2
+//               domain, P = exp2(S - m) packed to bf16 into TMEM; O rescaled in TMEM only when the running max
+//               grows by more than 2^8 (otherwise the stale max is kept, bounding P by 2^8); final O / l to global
+// TMEM: S0 [0,128) S1 [128,256) P [256,320) O [384, 384+hd). Every wait is bounded (common.cuh).
+// No TMA multicast (the kernel also runs in multi-GPU jobs).
+#include <cudaTypedefs.h>
+
+#include "common.cuh"
+#include "kernels.h"
+
+namespace fs {
+namespace attn_tc {
+
+constexpr int BM = 128, BN = 128, CHUNK = 16, STAGES = 2, THREADS = 192;
+constexpr int S_COL = 0, P_COL = 256, O_COL = 384, TMEM_COLS = 512;
+constexpr float RESCALE_THRESHOLD = 8.0f;   // log2 units
+
+template <int HD>
+struct Geo {
+  static constexpr int HALVES = HD / 64;                 // 64-column (128-byte) swizzle panels
+  static constexpr int Q_PANEL = BM * 128;               // bytes of one 64-column panel of Q
+  static constexpr int KV_PANEL = BN * 128;
+  static constexpr int Q_BYTES = Q_PANEL * HALVES;
+  static constexpr int KV_BYTES = KV_PANEL * HALVES;     // one K (or V) tile
+  static constexpr int K_OFF = Q_BYTES;
+  static constexpr int V_OFF = Q_BYTES + STAGES * KV_BYTES;
+  static constexpr int BAR_OFF = Q_BYTES + 2 * STAGES * KV_BYTES;
+  static constexpr int SMEM = BAR_OFF + 256 + 1024;      // + barriers + alignment slack
+  static constexpr uint32_t IDESC_S = idesc_bf16_f32(BM, BN);
+  static constexpr uint32_t IDESC_O = idesc_bf16_f32(BM, HD) | (1u << 16);  // B (= V) is MN-major
+};
+
+struct Params {
+  const int64_t* positions;
+  const int64_t* table;
+  int64_t table_stride;
+  int64_t n_slots;
+  int64_t block_size;
+  int64_t rows_per_block;   // block_stride / hd
+  int64_t rows_per_head;    // head_stride / hd
+  int64_t num_blocks;
+  __nv_bfloat16* out;
+  int64_t ldo;
+  int T, nh, rep, n_qb;
+  float scale_log2;
+  unsigned* err;
+};
+
+__device__ __forceinline__ void mma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
+                                       uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+__device__ __forceinline__ void tmem_st_32x32b_x16(uint32_t taddr, const uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
+      "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]),
+      "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
+      : "memory");
+}
+__device__ __forceinline__ void tmem_st_32x32b_x32(uint32_t taddr, const uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
+      "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
+      "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]),
+      "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]), "r"(r[16]), "r"(r[17]), "r"(r[18]),
+      "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]),
+      "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
+      : "memory");
+}
+__device__ __forceinline__ void tc_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+__device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
+// MN-major operand with 128-byte swizzle: 64-element MN panels `panel_bytes` apart (leading byte offset), 8-row
+// K groups 1024 bytes apart (stride byte offset).
+__device__ __forceinline__ uint64_t sw128_mnmajor_desc(uint32_t smem_addr, uint32_t panel_bytes) {
+  uint64_t d = 0;
+  d |= static_cast<uint64_t>((smem_addr >> 4) & 0x3FFFu);
+  d |= static_cast<uint64_t>((panel_bytes >> 4) & 0x3FFFu) << 16;
+  d |= static_cast<uint64_t>(1024u >> 4) << 32;
+  d |= static_cast<uint64_t>(1u) << 46;
+  d |= static_cast<uint64_t>(2u) << 61;
+  return d;
+}
+
+__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
+  __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&h);
+}
+
+template <int HD>
+__global__ void __launch_bounds__(THREADS, 1)
+    attn_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                   const __grid_constant__ CUtensorMap tmV, Params p) {
+  using G = Geo<HD>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + G::BAR_OFF);
+  uint64_t* q_full = bars + 0;
+  uint64_t* kv_full = bars + 1;      // [STAGES]
+  uint64_t* kv_empty = bars + 3;     // [STAGES]
+  uint64_t* s_full = bars + 5;       // [2]
+  uint64_t* s_empty = bars + 7;      // [2]
+  uint64_t* p_full = bars + 9;
+  uint64_t* pv_done = bars + 10;
+  uint64_t* o_full = bars + 11;
+  uint64_t* mma_done = bars + 12;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 13);
+  int* s_ntiles = reinterpret_cast<int*>(bars + 14);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 15);
+  __shared__ int64_t s_maxpos[4];
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int qb = p.n_qb - 1 - static_cast<int>(blockIdx.x);   // heaviest (latest) query blocks first
+  const int h = blockIdx.y, r = blockIdx.z;
+  const int g = h / p.rep;
+  const int j0 = qb * BM;
+  const int64_t tok0 = static_cast<int64_t>(r) * p.T;
+  const int valid_rows = p.T - j0 < BM ? p.T - j0 : BM;
+
+  // ---- setup: barriers, TMEM, the key range of this CTA (max position of its rows)
+  int64_t my_pos = 0;
+  if (warp < 4) {
+    const int row = warp * 32 + lane;
+    my_pos = row < valid_rows ? p.positions[tok0 + j0 + row] : 0;
+    if (my_pos < 0) my_pos = 0;
+    int64_t m = my_pos;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const int64_t w = __shfl_xor_sync(0xffffffffu, m, o);
+      m = w > m ? w : m;
+    }
+    if (lane == 0) s_maxpos[warp] = m;
+  }
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&kv_full[s], 1);
+      mbar_init(&kv_empty[s], 1);
+    }
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(&s_full[s], 1);
+      mbar_init(&s_empty[s], BM);
+    }
+    mbar_init(p_full, BM);
+    mbar_init(pv_done, 1);
+    mbar_init(o_full, 1);
+    mbar_init(mma_done, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 4) {
+    tmem_alloc(tmem_slot, TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (threadIdx.x == 0) {
+    int64_t mp = s_maxpos[0];
+    for (int i = 1; i < 4; ++i) mp = s_maxpos[i] > mp ? s_maxpos[i] : mp;
+    int64_t n_keys = mp + 1 < p.n_slots ? mp + 1 : p.n_slots;
+    if (n_keys < 1) n_keys = 1;
+    s_ntiles[0] = static_cast<int>((n_keys + BN - 1) / BN);
+    s_ntiles[1] = static_cast<int>(n_keys);
+  }
+  __syncthreads();
+  const uint32_t tmem = *tmem_slot;
+  const int n_tiles = s_ntiles[0];
+  const int n_keys = s_ntiles[1];
+
+  if (warp == 4) {
+    // ------------------------------------------------------------------------------------------ producer
+    if (lane == 0) {
+      prefetch_tmap(&tmQ);
+      prefetch_tmap(&tmK);
+      prefetch_tmap(&tmV);
+      mbar_arrive_expect_tx(q_full, G::Q_BYTES);
+      for (int hf = 0; hf < G::HALVES; ++hf)
+        tma_load_2d(smem + hf * G::Q_PANEL, &tmQ, q_full, h * HD + 64 * hf, static_cast<int>(tok0 + j0));
+      for (int j = 0; j < n_tiles; ++j) {
+        const int s = j % STAGES;
+        if (!mbar_wait(&kv_empty[s], ((j / STAGES) & 1) ^ 1, p.err) || *abort_flag) {
+          *abort_flag = 1;
+          break;
+        }
+        const int key0 = j * BN;
+        const int rem = n_keys - key0;
+        const int nch = rem >= BN ? BN / CHUNK : (rem + CHUNK - 1) / CHUNK;
+        mbar_arrive_expect_tx(&kv_full[s], static_cast<uint32_t>(nch * CHUNK * 128 * G::HALVES * 2));
+        for (int c = 0; c < nch; ++c) {
+          const int64_t s0 = key0 + c * CHUNK;
+          int64_t blk = p.table[static_cast<int64_t>(r) * p.table_stride + s0 / p.block_size];
+          if (blk < 0 || blk >= p.num_blocks) {
+            flag_error(p.err, ERR_BAD_SLOT);
+            blk = 0;
+          }
+          const int row = static_cast<int>(blk * p.rows_per_block + g * p.rows_per_head + s0 % p.block_size);
+          for (int hf = 0; hf < G::HALVES; ++hf) {
+            tma_load_2d(smem + G::K_OFF + s * G::KV_BYTES + hf * G::KV_PANEL + c * CHUNK * 128, &tmK, &kv_full[s],
+                        64 * hf, row);
+            tma_load_2d(smem + G::V_OFF + s * G::KV_BYTES + hf * G::KV_PANEL + c * CHUNK * 128, &tmV, &kv_full[s],
+                        64 * hf, row);
+          }
+        }
+      }
+    }
+  } else if (warp == 5) {
+    // ------------------------------------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      const uint32_t q_addr = smem_u32(smem);
+      bool ok = mbar_wait(q_full, 0, p.err);
+      auto issue_pv = [&](int i) -> bool {
+        if (!mbar_wait(p_full, i & 1, p.err) || *abort_flag) return false;
+        tc_fence_after();
+        const uint32_t v_addr = smem_u32(smem + G::V_OFF + (i % STAGES) * G::KV_BYTES);
+#pragma unroll
+        for (int ks = 0; ks < BN / 16; ++ks) {
+          const uint64_t bdesc = sw128_mnmajor_desc(v_addr + ks * 2048u, G::KV_PANEL);
+          mma_ts(tmem + O_COL, tmem + P_COL + ks * 8, bdesc, G::IDESC_O, (i | ks) != 0);
+        }
+        tc_commit(pv_done);
+        tc_commit(&kv_empty[i % STAGES]);
+        return true;
+      };
+      for (int j = 0; j < n_tiles && ok; ++j) {
+        const int s = j % STAGES;
+        if (!mbar_wait(&kv_full[s], (j / STAGES) & 1, p.err) || !mbar_wait(&s_empty[j & 1], ((j >> 1) & 1) ^ 1, p.err) ||
+            *abort_flag) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t k_addr = smem_u32(smem + G::K_OFF + s * G::KV_BYTES);
+#pragma unroll
+        for (int ks = 0; ks < HD / 16; ++ks) {
+          const int hf = ks / 4, kk = ks % 4;
+          const uint64_t adesc = sw128_kmajor_desc(q_addr + hf * G::Q_PANEL) + 2u * kk;
+          const uint64_t bdesc = sw128_kmajor_desc(k_addr + hf * G::KV_PANEL) + 2u * kk;
+          tc_mma_f16(tmem + S_COL + (j & 1) * 128, adesc, bdesc, G::IDESC_S, ks != 0);
+        }
+        tc_commit(&s_full[j & 1]);
+        if (j >= 1 && !issue_pv(j - 1)) ok = false;
+      }
+      if (ok && n_tiles > 0) ok = issue_pv(n_tiles - 1);
+      if (ok) tc_commit(o_full);
+      if (!ok) *abort_flag = 1;
+      tc_commit(mma_done);
+    }
+  } else {
+    // ------------------------------------------------------------------------------------------ softmax
+    const int row = warp * 32 + lane;
+    const uint32_t lane_base = static_cast<uint32_t>(warp * 32) << 16;
+    float m_ref = -INFINITY, l = 0.f;
+    bool ok = true;
+    for (int j = 0; j < n_tiles; ++j) {
+      const int sb = j & 1;
+      ok = __all_sync(0xffffffffu, mbar_wait(&s_full[sb], (j >> 1) & 1, p.err));
+      if (!ok) break;
+      tc_fence_after();
+      float v[BN];
+#pragma unroll
+      for (int c = 0; c < BN / 32; ++c) {
+        uint32_t t[32];
+        tmem_ld_32x32b_x32(tmem + lane_base + S_COL + sb * 128 + c * 32, t);
+        tc_wait_ld();
+#pragma unroll
+        for (int i = 0; i < 32; ++i) v[c * 32 + i] = __uint_as_float(t[i]);
+      }
+      tc_fence_before();
+      mbar_arrive(&s_empty[sb]);
+      const int64_t key0 = static_cast<int64_t>(j) * BN;
+      float mx = -INFINITY;
+#pragma unroll
+      for (int c = 0; c < BN; ++c) {
+        const int64_t k = key0 + c;
+        const bool vis = k <= my_pos && k < p.n_slots;
+        v[c] = vis ? v[c] * p.scale_log2 : -INFINITY;
+        mx = fmaxf(mx, v[c]);
+      }
+      const float m_new = fmaxf(m_ref, mx);
+      if (j >= 1) {
+        ok = __all_sync(0xffffffffu, mbar_wait(pv_done, (j - 1) & 1, p.err));
+        if (!ok) break;
+        tc_fence_after();
+      }
+      if (m_ref == -INFINITY || m_new > m_ref + RESCALE_THRESHOLD) {
+        if (j >= 1 && m_ref != -INFINITY) {
+          const float corr = exp2f(m_ref - m_new);
+          l *= corr;
+#pragma unroll 1
+          for (int c = 0; c < HD / 32; ++c) {
+            uint32_t t[32];
+            const uint32_t addr = tmem + lane_base + O_COL + c * 32;
+            tmem_ld_32x32b_x32(addr, t);
+            tc_wait_ld();
+#pragma unroll
+            for (int i = 0; i < 32; ++i) t[i] = __float_as_uint(__uint_as_float(t[i]) * corr);
+            tmem_st_32x32b_x32(addr, t);
+          }
+        }
+        m_ref = m_new;
+      }
+      const float sub = m_ref == -INFINITY ? 0.f : m_ref;
+      float sum = 0.f;
+#pragma unroll
+      for (int c = 0; c < BN / 32; ++c) {
+        uint32_t pk[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          const float p0 = exp2f(v[c * 32 + 2 * i] - sub), p1 = exp2f(v[c * 32 + 2 * i + 1] - sub);
+          sum += p0 + p1;
+          pk[i] = pack_bf16x2(p0, p1);
+        }
+        tmem_st_32x32b_x16(tmem + lane_base + P_COL + c * 16, pk);
+      }
+      tc_wait_st();
+      l += sum;
+      if (key0 + BN > n_keys && key0 + row >= n_keys) {
+        // V rows past the last key hold stale data; P is 0 there but 0 * NaN is not, so zero them
+        uint4* vrow = reinterpret_cast<uint4*>(smem + G::V_OFF + (j % STAGES) * G::KV_BYTES + row * 128);
+#pragma unroll
+        for (int hf = 0; hf < G::HALVES; ++hf)
+#pragma unroll
+          for (int i = 0; i < 8; ++i) vrow[hf * (G::KV_PANEL / 16) + i] = make_uint4(0, 0, 0, 0);
+        fence_async_smem();
+      }
+      tc_fence_before();
+      mbar_arrive(p_full);
+    }
+    if (ok && n_tiles > 0) ok = __all_sync(0xffffffffu, mbar_wait(o_full, 0, p.err));
+    if (ok) {
+      tc_fence_after();
+      const float inv = l > 0.f ? 1.f / l : 0.f;
+      __nv_bfloat16* orow = p.out + (tok0 + j0 + row) * p.ldo + static_cast<int64_t>(h) * HD;
+#pragma unroll 1
+      for (int c = 0; c < HD / 32; ++c) {
+        uint32_t t[32];
+        tmem_ld_32x32b_x32(tmem + lane_base + O_COL + c * 32, t);
+        tc_wait_ld();
+        if (row < valid_rows) {
+          uint4* dst = reinterpret_cast<uint4*>(orow + c * 32);
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            uint4 w;
+            w.x = pack_bf16x2(__uint_as_float(t[8 * i + 0]) * inv, __uint_as_float(t[8 * i + 1]) * inv);
+            w.y = pack_bf16x2(__uint_as_float(t[8 * i + 2]) * inv, __uint_as_float(t[8 * i + 3]) * inv);
+            w.z = pack_bf16x2(__uint_as_float(t[8 * i + 4]) * inv, __uint_as_float(t[8 * i + 5]) * inv);
+            w.w = pack_bf16x2(__uint_as_float(t[8 * i + 6]) * inv, __uint_as_float(t[8 * i + 7]) * inv);
+            dst[i] = w;
+          }
+        }
+      }
+    } else {
+      *abort_flag = 1;
+    }
+  }
+
+  __syncthreads();
+  if (warp == 4) {
+    mbar_wait(mma_done, 0, p.err);   // every MMA has completed before TMEM is released
+    tc_fence_after();
+    tmem_dealloc(tmem, TMEM_COLS);
+  }
+}
+
+// ------------------------------------------------------------------------------------------------ host
+static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  if (!fn) {
+    cudaDriverEntryPointQueryResult q;
+    void* ptr = nullptr;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+  }
+  return fn;
+}
+
+static int make_map(CUtensorMap* map, const void* ptr, int64_t cols, int64_t rows, int64_t ld, int box_rows) {
+  auto fn = encode_fn();
+  if (!fn) return fail("cuTensorMapEncodeTiled is unavailable from the CUDA driver");
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(ld) * 2};
+  cuuint32_t box[2] = {64, static_cast<cuuint32_t>(box_rows)};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult res = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(ptr), dims, strides, box, estr,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (res != CUDA_SUCCESS) return fail("cuTensorMapEncodeTiled failed with CUresult " + std::to_string(int(res)));
+  return 0;
+}
+
+bool supported(const void* q, int64_t ldq, const KVCache& kv, int64_t hd, int64_t T) {
+  if (hd != 64 && hd != 128) return false;
+  if (T < 1 || kv.block_size % CHUNK != 0) return false;
+  if (kv.block_stride % hd != 0 || kv.head_stride % hd != 0 || kv.head_stride / hd < kv.block_size) return false;
+  if (ldq % 8 != 0) return false;
+  const uintptr_t a = reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(kv.k) | reinterpret_cast<uintptr_t>(kv.v);
+  if (a & 15) return false;
+  const int64_t rows = kv.num_blocks * (kv.block_stride / hd);
+  return rows < (int64_t(1) << 31);
+}
+
+template <int HD>
+static int launch_t(const void* q, int64_t ldq, const KVCache& kv, int64_t n_slots, const int64_t* positions, void* out,
+                    int64_t ldo, int64_t B, int64_t T, int64_t nh, int64_t nkv, float scale, cudaStream_t st) {
+  using G = Geo<HD>;
+  CUtensorMap mq, mk, mv;
+  const int64_t q_rows = B * T;
+  if (make_map(&mq, q, ldq, q_rows, ldq, BM)) return -1;
+  const int64_t kv_rows = kv.num_blocks * (kv.block_stride / HD);
+  if (make_map(&mk, kv.k, HD, kv_rows, HD, CHUNK)) return -1;
+  if (make_map(&mv, kv.v, HD, kv_rows, HD, CHUNK)) return -1;
+  Params p;
+  p.positions = positions;
+  p.table = kv.table;
+  p.table_stride = kv.table_stride;
+  p.n_slots = n_slots;
+  p.block_size = kv.block_size;
+  p.rows_per_block = kv.block_stride / HD;
+  p.rows_per_head = kv.head_stride / HD;
+  p.num_blocks = kv.num_blocks;
+  p.out = static_cast<__nv_bfloat16*>(out);
+  p.ldo = ldo;
+  p.T = static_cast<int>(T);
+  p.nh = static_cast<int>(nh);
+  p.rep = static_cast<int>(nh / nkv);
+  p.n_qb = static_cast<int>((T + BM - 1) / BM);
+  p.scale_log2 = scale * 1.4426950408889634f;
+  p.err = error_word();
+  if (!p.err) return -1;
+  static bool attr[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev >= 0 && dev < 64 && !attr[dev]) {
+    if (cudaFuncSetAttribute(attn_tc_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, G::SMEM) != cudaSuccess)
+      return check_launch("attn_tc set smem");
+    attr[dev] = true;
+  }
+  dim3 grid(static_cast<unsigned>(p.n_qb), static_cast<unsigned>(nh), static_cast<unsigned>(B));
+  attn_tc_kernel<HD><<<grid, THREADS, G::SMEM, st>>>(mq, mk, mv, p);
+  return check_launch("attn_tc_kernel");
+}
+
+int launch(const void* q, int64_t ldq, const KVCache& kv, int64_t n_slots, const int64_t* positions, void* out,
+           int64_t ldo, int64_t B, int64_t T, int64_t nh, int64_t nkv, int64_t hd, float scale, cudaStream_t st) {
+  if (B > 65535 || nh > 65535) return fail("attention: grid too large");
+  if (hd == 128) return launch_t<128>(q, ldq, kv, n_slots, positions, out, ldo, B, T, nh, nkv, scale, st);
+  if (hd == 64) return launch_t<64>(q, ldq, kv, n_slots, positions, out, ldo, B, T, nh, nkv, scale, st);
+  return fail("attention (tcgen05): head_dim must be 64 or 128");
+}
+
+}  // namespace attn_tc
+}  // namespace fs

@@ -33,8 +33,15 @@ int argmax(int dtype, const void* x, int64_t rows, int64_t n, int64_t row_stride
 
 // Attention of B*T new queries against the cache (GQA, mask: key slot s visible iff s <= position and
 // s < n_slots). q: row (b*T + t) holds nh heads of hd at stride ldq; out likewise at stride ldo.
+// impl: 0 = automatic, 1 = CUDA-core kernel, 2 = mma.sync kernel, 3 = tcgen05 kernel.
 int attention(int dtype, const void* q, int64_t ldq, const KVCache& kv, int64_t n_slots, const int64_t* positions,
               void* out, int64_t ldo, int64_t B, int64_t T, int64_t nh, int64_t nkv, int64_t hd, float scale,
-              int force_generic, cudaStream_t st);
+              int impl, cudaStream_t st);
+
+namespace attn_tc {
+bool supported(const void* q, int64_t ldq, const KVCache& kv, int64_t hd, int64_t T);
+int launch(const void* q, int64_t ldq, const KVCache& kv, int64_t n_slots, const int64_t* positions, void* out,
+           int64_t ldo, int64_t B, int64_t T, int64_t nh, int64_t nkv, int64_t hd, float scale, cudaStream_t st);
+}  // namespace attn_tc
 
 }  // namespace fs

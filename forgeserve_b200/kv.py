@@ -65,6 +65,7 @@ class ContiguousKV:
             new_cap = need
         if self.max_len is not None and need <= self.max_len:
             new_cap = min(new_cap, self.max_len)
+        new_cap = -(-new_cap // 16) * 16     # whole 16-slot chunks: the tensor-core attention reads the cache in those
         k = torch.empty(batch, n_kv, new_cap, head_dim, dtype=dtype, device=device)
         v = torch.empty_like(k)
         if self._len:

@@ -120,13 +120,14 @@ def rope_kv_write(qkv: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor, posit
 
 
 def attention(q: torch.Tensor, kv: L.KVCacheDesc, n_slots: int, positions: torch.Tensor, out: torch.Tensor, B: int,
-              T: int, nh: int, nkv: int, hd: int, generic: bool = False) -> torch.Tensor:
+              T: int, nh: int, nkv: int, hd: int, impl: int = L.FS_ATTN_AUTO) -> torch.Tensor:
+    """GQA attention over a cache; impl selects the kernel (FS_ATTN_*), automatic by default."""
     require_cuda(q, positions, out)
     _, ldq = _rows(q)
     _, ldo = _rows(out)
-    fn = L.load().fs_attention_generic if generic else L.load().fs_attention
-    L.check(fn(_p(q), ldq, ctypes.byref(kv), n_slots, _p(positions), _p(out), ldo, B, T, nh, nkv, hd,
-               1.0 / math.sqrt(hd), dtype_code(q.dtype), _stream(q)), "fs_attention")
+    L.check(L.load().fs_attention_impl(_p(q), ldq, ctypes.byref(kv), n_slots, _p(positions), _p(out), ldo, B, T, nh,
+                                       nkv, hd, 1.0 / math.sqrt(hd), int(impl), dtype_code(q.dtype), _stream(q)),
+            "fs_attention")
     return out
 
 

@@ -45,13 +45,13 @@ _PAIR_GROUPS: Dict[int, list] = {}
 
 # NCCL kernels stay resident on the SMs they run on while a receive waits for its data. Pipeline stages keep a
 # few SMs out of the persistent GEMM grid for them, and cap NCCL's point-to-point channels to match.
-COMM_SMS = int(os.environ.get("FORGESERVE_COMM_SMS", "4"))
+COMM_SMS = int(os.environ.get("FORGESERVE_COMM_SMS", "12"))
 
 
 def _pair_groups():
     world = dist.get_world_size()
     if world not in _PAIR_GROUPS:
-        os.environ.setdefault("NCCL_MAX_P2P_NCHANNELS", str(max(COMM_SMS, 1)))
+        os.environ.setdefault("NCCL_MAX_P2P_NCHANNELS", "2")
         # every rank creates every pair group, in the same order (new_group is collective over the world)
         _PAIR_GROUPS[world] = [dist.new_group([i, i + 1]) for i in range(world - 1)]
     return _PAIR_GROUPS[world]

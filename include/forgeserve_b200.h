@@ -96,15 +96,19 @@ int fs_paged_gather(const void* pool, const int64_t* table, int64_t B, int64_t n
 
 /* GQA attention of B*T new queries over the cache: key slot s visible iff s <= positions[r, j] and s < n_slots
  * (model.py:69-76: cache update, repeat_interleave, mask, scaled_dot_product_attention with scale 1/sqrt(hd)).
- * q rows (B*T, ldq) hold nh heads; out rows (B*T, ldo). bf16 with hd 64/128 runs on tensor cores. */
+ * q rows (B*T, ldq) hold nh heads; out rows (B*T, ldo). bf16 with hd 64/128 runs on tensor cores: the
+ * tcgen05/TMEM kernel for T >= 64 (cache block_size a multiple of 16), the mma.sync kernel for shorter query blocks. */
 int fs_attention(const void* q, int64_t ldq, const fs_kv_cache* kv, int64_t n_slots, const int64_t* positions,
                  void* out, int64_t ldo, int64_t B, int64_t T, int64_t nh, int64_t nkv, int64_t hd, float scale,
                  int dtype, void* stream);
 
-/* Same as fs_attention on the CUDA-core kernel only (cross-checking). */
-int fs_attention_generic(const void* q, int64_t ldq, const fs_kv_cache* kv, int64_t n_slots, const int64_t* positions,
-                         void* out, int64_t ldo, int64_t B, int64_t T, int64_t nh, int64_t nkv, int64_t hd,
-                         float scale, int dtype, void* stream);
+/* fs_attention with an explicit kernel: FS_ATTN_AUTO, FS_ATTN_CUDA_CORE (fp32/bf16, any even hd <= 256),
+ * FS_ATTN_MMA_SYNC (bf16, hd 64/128) or FS_ATTN_TCGEN05 (bf16, hd 64/128, block_size % 16 == 0); a kernel that
+ * cannot take the layout returns an error. For cross-checking the kernels against each other. */
+enum { FS_ATTN_AUTO = 0, FS_ATTN_CUDA_CORE = 1, FS_ATTN_MMA_SYNC = 2, FS_ATTN_TCGEN05 = 3 };
+int fs_attention_impl(const void* q, int64_t ldq, const fs_kv_cache* kv, int64_t n_slots, const int64_t* positions,
+                      void* out, int64_t ldo, int64_t B, int64_t T, int64_t nh, int64_t nkv, int64_t hd, float scale,
+                      int impl, int dtype, void* stream);
 
 /* Token embedding gather out[i] = table[ids[i]] (nn.Embedding at pipeline.py:106 / model.py:134-135). */
 int fs_embed(const int64_t* ids, int64_t n, const void* table, int64_t vocab, int64_t dim, void* out, int dtype,

@@ -191,16 +191,16 @@ def attention_ref(q, k_all, v_all, positions, rep):
     return torch.nn.functional.scaled_dot_product_attention(q.double(), k_all, v_all, attn_mask=mask)
 
 
-def run_contiguous_attention(dtype, B, T, start, nh, nkv, hd, generic=False):
+def run_contiguous_attention(dtype, B, T, start, nh, nkv, hd, impl=L.FS_ATTN_AUTO, cap_multiple=1):
     S = start + T
-    cap = S + 3
+    cap = -(-(S + 3) // cap_multiple) * cap_multiple
     k = torch.randn(B, nkv, cap, hd, device=DEV).to(dtype)
     v = torch.randn(B, nkv, cap, hd, device=DEV).to(dtype)
     q = torch.randn(B * T, nh * hd, device=DEV).to(dtype)
     positions = (start + torch.arange(T, device=DEV))[None].expand(B, T).contiguous()
     out = torch.empty(B * T, nh * hd, device=DEV, dtype=dtype)
     desc = ops.contiguous_desc(k, v, torch.arange(B, device=DEV))
-    ops.attention(q, desc, S, positions, out, B, T, nh, nkv, hd, generic=generic)
+    ops.attention(q, desc, S, positions, out, B, T, nh, nkv, hd, impl=impl)
     want = attention_ref(q.view(B, T, nh, hd).transpose(1, 2), k[:, :, :S], v[:, :, :S], positions, nh // nkv)
     return out.view(B, T, nh, hd).transpose(1, 2), want
 
@@ -221,10 +221,71 @@ def test_attention_tensorcore_bf16(B, T, start, nh, nkv, hd):
 
 
 def test_attention_generic_bf16_matches_tensorcore():
-    got_tc, want = run_contiguous_attention(torch.bfloat16, 2, 96, 5, 8, 2, 128)
-    torch.manual_seed(0)
-    got_gen, want2 = run_contiguous_attention(torch.bfloat16, 2, 96, 5, 8, 2, 128, generic=True)
+    got_tc, want = run_contiguous_attention(torch.bfloat16, 2, 96, 5, 8, 2, 128, impl=L.FS_ATTN_MMA_SYNC)
+    assert (got_tc.double() - want).abs().max().item() < 2e-2
+    got_gen, want2 = run_contiguous_attention(torch.bfloat16, 2, 96, 5, 8, 2, 128, impl=L.FS_ATTN_CUDA_CORE)
     assert (got_gen.double() - want2).abs().max().item() < 2e-2
+
+
+@pytest.mark.parametrize("B,T,start,nh,nkv,hd", [(1, 128, 0, 4, 1, 128), (2, 300, 0, 8, 2, 128), (1, 2048, 0, 8, 2, 128),
+                                                 (2, 200, 37, 4, 4, 128), (2, 64, 0, 4, 2, 64), (1, 333, 21, 8, 2, 64),
+                                                 (3, 1, 50, 4, 1, 128), (1, 17, 0, 8, 8, 128)])
+def test_attention_tcgen05(B, T, start, nh, nkv, hd):
+    got, want = run_contiguous_attention(torch.bfloat16, B, T, start, nh, nkv, hd, impl=L.FS_ATTN_TCGEN05,
+                                         cap_multiple=16)
+    err = (got.double() - want).abs().max().item()
+    assert err < 2e-2, err
+
+
+def test_attention_tcgen05_large_logits():
+    """Scores far apart (the running max jumps by more than 2^8 between key tiles): the lazy rescale path."""
+    B, T, nh, nkv, hd = 1, 512, 4, 1, 128
+    k = torch.randn(B, nkv, 512, hd, device=DEV)
+    k[:, :, 300:] *= 40.0                                    # later keys dominate by a wide margin
+    k, v = k.bfloat16(), torch.randn(B, nkv, 512, hd, device=DEV).bfloat16()
+    q = (torch.randn(B * T, nh * hd, device=DEV) * 2).bfloat16()
+    positions = torch.arange(T, device=DEV)[None]
+    out = torch.empty(B * T, nh * hd, device=DEV, dtype=torch.bfloat16)
+    ops.attention(q, ops.contiguous_desc(k, v, torch.arange(B, device=DEV)), T, positions, out, B, T, nh, nkv, hd,
+                  impl=L.FS_ATTN_TCGEN05)
+    want = attention_ref(q.view(B, T, nh, hd).transpose(1, 2), k, v, positions, nh)
+    got = out.view(B, T, nh, hd).transpose(1, 2).double()
+    assert torch.isfinite(got).all()
+    assert (got - want).abs().max().item() < 3e-2
+
+
+def test_attention_tcgen05_paged_scattered_blocks():
+    """Prefill of rows with different lengths into 16-slot blocks taken from a shuffled free list."""
+    nh, nkv, hd, bs = 8, 2, 128, 16
+    lengths = [200, 77, 130]
+    B, T = len(lengths), max(lengths)
+    nblk = 64
+    blocks = list(range(nblk))
+    random.Random(1).shuffle(blocks)
+    it = iter(blocks)
+    width = -(-T // bs)
+    table = torch.tensor([[next(it) for _ in range(width)] for _ in lengths], device=DEV)
+    pool_k = torch.randn(nblk, nkv, bs, hd, device=DEV).bfloat16()
+    pool_v = torch.randn(nblk, nkv, bs, hd, device=DEV).bfloat16()
+    positions = torch.stack([torch.arange(T) for _ in lengths]).to(DEV)
+    q = torch.randn(B * T, nh * hd, device=DEV).bfloat16()
+    out = torch.empty_like(q)
+    ops.attention(q, ops.paged_desc(pool_k, pool_v, table), width * bs, positions, out, B, T, nh, nkv, hd,
+                  impl=L.FS_ATTN_TCGEN05)
+    k_all = pool_k[table].permute(0, 2, 1, 3, 4).reshape(B, nkv, -1, hd)
+    v_all = pool_v[table].permute(0, 2, 1, 3, 4).reshape(B, nkv, -1, hd)
+    want = attention_ref(q.view(B, T, nh, hd).transpose(1, 2), k_all, v_all, positions, nh // nkv)
+    got = out.view(B, T, nh, hd).transpose(1, 2).double()
+    assert (got - want).abs().max().item() < 2e-2
+
+
+def test_attention_kernel_selector_refuses_unsupported_layouts():
+    q = torch.randn(4, 8 * 16, device=DEV).bfloat16()
+    k = torch.randn(1, 4, 8, 16, device=DEV).bfloat16()
+    out = torch.empty_like(q)
+    desc = ops.contiguous_desc(k, k.clone(), torch.arange(1, device=DEV))
+    with pytest.raises(RuntimeError, match="tcgen05"):
+        ops.attention(q, desc, 4, torch.arange(4, device=DEV)[None], out, 1, 4, 8, 4, 16, impl=L.FS_ATTN_TCGEN05)
 
 
 @pytest.mark.parametrize("dtype,hd", [(torch.float32, 16), (torch.bfloat16, 128), (torch.bfloat16, 64)])
