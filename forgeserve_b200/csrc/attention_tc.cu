@@ -302,22 +302,24 @@ __global__ void __launch_bounds__(THREADS, 1)
         if (!ok) break;
         tc_fence_after();
       }
-      if (m_ref == -INFINITY || m_new > m_ref + RESCALE_THRESHOLD) {
-        if (j >= 1 && m_ref != -INFINITY) {
-          const float corr = exp2f(m_ref - m_new);
-          l *= corr;
+      // Whether a row moves its reference max is decided per row, but the TMEM accesses that rescale O are
+      // .sync.aligned warp instructions: the warp takes the rescale path if any of its rows needs it, and rows that
+      // do not need it multiply by 1.
+      const bool need = m_ref == -INFINITY || m_new > m_ref + RESCALE_THRESHOLD;
+      const float corr = (need && m_ref != -INFINITY) ? exp2f(m_ref - m_new) : 1.f;
+      if (need) m_ref = m_new;
+      l *= corr;
+      if (j >= 1 && __any_sync(0xffffffffu, corr != 1.f)) {
 #pragma unroll 1
-          for (int c = 0; c < HD / 32; ++c) {
-            uint32_t t[32];
-            const uint32_t addr = tmem + lane_base + O_COL + c * 32;
-            tmem_ld_32x32b_x32(addr, t);
-            tc_wait_ld();
+        for (int c = 0; c < HD / 32; ++c) {
+          uint32_t t[32];
+          const uint32_t addr = tmem + lane_base + O_COL + c * 32;
+          tmem_ld_32x32b_x32(addr, t);
+          tc_wait_ld();
 #pragma unroll
-            for (int i = 0; i < 32; ++i) t[i] = __float_as_uint(__uint_as_float(t[i]) * corr);
-            tmem_st_32x32b_x32(addr, t);
-          }
+          for (int i = 0; i < 32; ++i) t[i] = __float_as_uint(__uint_as_float(t[i]) * corr);
+          tmem_st_32x32b_x32(addr, t);
         }
-        m_ref = m_new;
       }
       const float sub = m_ref == -INFINITY ? 0.f : m_ref;
       float sum = 0.f;
