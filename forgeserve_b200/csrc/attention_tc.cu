@@ -109,7 +109,8 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
 template <int HD>
 __global__ void __launch_bounds__(THREADS, 1)
     attn_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
-                   const __grid_constant__ CUtensorMap tmV, Params p) {
+                   const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmK128,
+                   const __grid_constant__ CUtensorMap tmV128, Params p) {
   using G = Geo<HD>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -193,32 +194,55 @@ __global__ void __launch_bounds__(THREADS, 1)
       prefetch_tmap(&tmQ);
       prefetch_tmap(&tmK);
       prefetch_tmap(&tmV);
+      prefetch_tmap(&tmK128);
+      prefetch_tmap(&tmV128);
       mbar_arrive_expect_tx(q_full, G::Q_BYTES);
       for (int hf = 0; hf < G::HALVES; ++hf)
         tma_load_2d(smem + hf * G::Q_PANEL, &tmQ, q_full, h * HD + 64 * hf, static_cast<int>(tok0 + j0));
       for (int j = 0; j < n_tiles; ++j) {
         const int s = j % STAGES;
+        const int key0 = j * BN;
+        const int rem = n_keys - key0;
+        const int nch = rem >= BN ? BN / CHUNK : (rem + CHUNK - 1) / CHUNK;
+        // Block numbers of the tile's 16-key chunks, all loaded before any copy is issued (the copies are
+        // compiler barriers: a lookup placed between them would be one full memory round trip each).
+        const bool one_block = (key0 % p.block_size) + BN <= p.block_size;
+        int64_t blk[BN / CHUNK];
+#pragma unroll
+        for (int c = 0; c < BN / CHUNK; ++c) {
+          const int64_t s0 = key0 + c * CHUNK;
+          blk[c] = (c < nch && (c == 0 || !one_block)) ? p.table[static_cast<int64_t>(r) * p.table_stride + s0 / p.block_size]
+                                                      : 0;
+        }
+#pragma unroll
+        for (int c = 0; c < BN / CHUNK; ++c)
+          if (blk[c] < 0 || blk[c] >= p.num_blocks) {
+            if (c < nch) flag_error(p.err, ERR_BAD_SLOT);
+            blk[c] = 0;
+          }
         if (!mbar_wait(&kv_empty[s], ((j / STAGES) & 1) ^ 1, p.err) || *abort_flag) {
           *abort_flag = 1;
           break;
         }
-        const int key0 = j * BN;
-        const int rem = n_keys - key0;
-        const int nch = rem >= BN ? BN / CHUNK : (rem + CHUNK - 1) / CHUNK;
-        mbar_arrive_expect_tx(&kv_full[s], static_cast<uint32_t>(nch * CHUNK * 128 * G::HALVES * 2));
-        for (int c = 0; c < nch; ++c) {
-          const int64_t s0 = key0 + c * CHUNK;
-          int64_t blk = p.table[static_cast<int64_t>(r) * p.table_stride + s0 / p.block_size];
-          if (blk < 0 || blk >= p.num_blocks) {
-            flag_error(p.err, ERR_BAD_SLOT);
-            blk = 0;
-          }
-          const int row = static_cast<int>(blk * p.rows_per_block + g * p.rows_per_head + s0 % p.block_size);
+        uint8_t* kdst = smem + G::K_OFF + s * G::KV_BYTES;
+        uint8_t* vdst = smem + G::V_OFF + s * G::KV_BYTES;
+        if (one_block) {
+          // the whole tile lies in one block (a contiguous cache): one 128-row box per panel
+          mbar_arrive_expect_tx(&kv_full[s], static_cast<uint32_t>(BN * 128 * G::HALVES * 2));
+          const int row = static_cast<int>(blk[0] * p.rows_per_block + g * p.rows_per_head + key0 % p.block_size);
           for (int hf = 0; hf < G::HALVES; ++hf) {
-            tma_load_2d(smem + G::K_OFF + s * G::KV_BYTES + hf * G::KV_PANEL + c * CHUNK * 128, &tmK, &kv_full[s],
-                        64 * hf, row);
-            tma_load_2d(smem + G::V_OFF + s * G::KV_BYTES + hf * G::KV_PANEL + c * CHUNK * 128, &tmV, &kv_full[s],
-                        64 * hf, row);
+            tma_load_2d(kdst + hf * G::KV_PANEL, &tmK128, &kv_full[s], 64 * hf, row);
+            tma_load_2d(vdst + hf * G::KV_PANEL, &tmV128, &kv_full[s], 64 * hf, row);
+          }
+        } else {
+          mbar_arrive_expect_tx(&kv_full[s], static_cast<uint32_t>(nch * CHUNK * 128 * G::HALVES * 2));
+          for (int c = 0; c < nch; ++c) {
+            const int64_t s0 = key0 + c * CHUNK;
+            const int row = static_cast<int>(blk[c] * p.rows_per_block + g * p.rows_per_head + s0 % p.block_size);
+            for (int hf = 0; hf < G::HALVES; ++hf) {
+              tma_load_2d(kdst + hf * G::KV_PANEL + c * CHUNK * 128, &tmK, &kv_full[s], 64 * hf, row);
+              tma_load_2d(vdst + hf * G::KV_PANEL + c * CHUNK * 128, &tmV, &kv_full[s], 64 * hf, row);
+            }
           }
         }
       }
@@ -277,13 +301,15 @@ __global__ void __launch_bounds__(THREADS, 1)
       if (!ok) break;
       tc_fence_after();
       float v[BN];
+      {
+        uint32_t t[BN / 32][32];
 #pragma unroll
-      for (int c = 0; c < BN / 32; ++c) {
-        uint32_t t[32];
-        tmem_ld_32x32b_x32(tmem + lane_base + S_COL + sb * 128 + c * 32, t);
+        for (int c = 0; c < BN / 32; ++c) tmem_ld_32x32b_x32(tmem + lane_base + S_COL + sb * 128 + c * 32, t[c]);
         tc_wait_ld();
 #pragma unroll
-        for (int i = 0; i < 32; ++i) v[c * 32 + i] = __uint_as_float(t[i]);
+        for (int c = 0; c < BN / 32; ++c)
+#pragma unroll
+          for (int i = 0; i < 32; ++i) v[c * 32 + i] = __uint_as_float(t[c][i]);
       }
       tc_fence_before();
       mbar_arrive(&s_empty[sb]);
@@ -297,45 +323,48 @@ __global__ void __launch_bounds__(THREADS, 1)
         mx = fmaxf(mx, v[c]);
       }
       const float m_new = fmaxf(m_ref, mx);
-      if (j >= 1) {
-        ok = __all_sync(0xffffffffu, mbar_wait(pv_done, (j - 1) & 1, p.err));
-        if (!ok) break;
-        tc_fence_after();
-      }
       // Whether a row moves its reference max is decided per row, but the TMEM accesses that rescale O are
       // .sync.aligned warp instructions: the warp takes the rescale path if any of its rows needs it, and rows that
       // do not need it multiply by 1.
       const bool need = m_ref == -INFINITY || m_new > m_ref + RESCALE_THRESHOLD;
       const float corr = (need && m_ref != -INFINITY) ? exp2f(m_ref - m_new) : 1.f;
       if (need) m_ref = m_new;
-      l *= corr;
-      if (j >= 1 && __any_sync(0xffffffffu, corr != 1.f)) {
-#pragma unroll 1
-        for (int c = 0; c < HD / 32; ++c) {
-          uint32_t t[32];
-          const uint32_t addr = tmem + lane_base + O_COL + c * 32;
-          tmem_ld_32x32b_x32(addr, t);
-          tc_wait_ld();
-#pragma unroll
-          for (int i = 0; i < 32; ++i) t[i] = __float_as_uint(__uint_as_float(t[i]) * corr);
-          tmem_st_32x32b_x32(addr, t);
-        }
-      }
       const float sub = m_ref == -INFINITY ? 0.f : m_ref;
+      // P for this tile, in registers, before waiting for the previous P V product
+      uint32_t pk[BN / 2];
       float sum = 0.f;
 #pragma unroll
-      for (int c = 0; c < BN / 32; ++c) {
-        uint32_t pk[16];
+      for (int i = 0; i < BN / 2; ++i) {
+        const float p0 = exp2f(v[2 * i] - sub), p1 = exp2f(v[2 * i + 1] - sub);
+        sum += p0 + p1;
+        pk[i] = pack_bf16x2(p0, p1);
+      }
+      l = l * corr + sum;
+      if (j >= 1) {
+        ok = __all_sync(0xffffffffu, mbar_wait(pv_done, (j - 1) & 1, p.err));
+        if (!ok) break;
+        tc_fence_after();
+        if (__any_sync(0xffffffffu, corr != 1.f)) {
+#pragma unroll 1
+          for (int c = 0; c < HD / 32; ++c) {
+            uint32_t t[32];
+            const uint32_t addr = tmem + lane_base + O_COL + c * 32;
+            tmem_ld_32x32b_x32(addr, t);
+            tc_wait_ld();
 #pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          const float p0 = exp2f(v[c * 32 + 2 * i] - sub), p1 = exp2f(v[c * 32 + 2 * i + 1] - sub);
-          sum += p0 + p1;
-          pk[i] = pack_bf16x2(p0, p1);
+            for (int i = 0; i < 32; ++i) t[i] = __float_as_uint(__uint_as_float(t[i]) * corr);
+            tmem_st_32x32b_x32(addr, t);
+          }
         }
-        tmem_st_32x32b_x16(tmem + lane_base + P_COL + c * 16, pk);
+      }
+#pragma unroll
+      for (int c = 0; c < BN / 32; ++c) {
+        uint32_t q16[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) q16[i] = pk[c * 16 + i];
+        tmem_st_32x32b_x16(tmem + lane_base + P_COL + c * 16, q16);
       }
       tc_wait_st();
-      l += sum;
       if (key0 + BN > n_keys && key0 + row >= n_keys) {
         // V rows past the last key hold stale data; P is 0 there but 0 * NaN is not, so zero them
         uint4* vrow = reinterpret_cast<uint4*>(smem + G::V_OFF + (j % STAGES) * G::KV_BYTES + row * 128);
@@ -430,8 +459,11 @@ static int launch_t(const void* q, int64_t ldq, const KVCache& kv, int64_t n_slo
   const int64_t q_rows = B * T;
   if (make_map(&mq, q, ldq, q_rows, ldq, BM)) return -1;
   const int64_t kv_rows = kv.num_blocks * (kv.block_stride / HD);
+  CUtensorMap mk128, mv128;
   if (make_map(&mk, kv.k, HD, kv_rows, HD, CHUNK)) return -1;
   if (make_map(&mv, kv.v, HD, kv_rows, HD, CHUNK)) return -1;
+  if (make_map(&mk128, kv.k, HD, kv_rows, HD, BN)) return -1;
+  if (make_map(&mv128, kv.v, HD, kv_rows, HD, BN)) return -1;
   Params p;
   p.positions = positions;
   p.table = kv.table;
@@ -459,7 +491,7 @@ static int launch_t(const void* q, int64_t ldq, const KVCache& kv, int64_t n_slo
     attr[dev] = true;
   }
   dim3 grid(static_cast<unsigned>(p.n_qb), static_cast<unsigned>(nh), static_cast<unsigned>(B));
-  attn_tc_kernel<HD><<<grid, THREADS, G::SMEM, st>>>(mq, mk, mv, p);
+  attn_tc_kernel<HD><<<grid, THREADS, G::SMEM, st>>>(mq, mk, mv, mk128, mv128, p);
   return check_launch("attn_tc_kernel");
 }
 
