@@ -22,7 +22,7 @@
 namespace fs {
 namespace attn_tc {
 
-constexpr int BM = 128, BN = 128, CHUNK = 16, STAGES = 2, THREADS = 192;
+constexpr int BM = 128, BN = 128, CHUNK = 16, K_STAGES = 3, V_STAGES = 2, THREADS = 192;
 constexpr int S_COL = 0, P_COL = 256, O_COL = 384, TMEM_COLS = 512;
 constexpr float RESCALE_THRESHOLD = 8.0f;   // log2 units
 
@@ -34,8 +34,8 @@ struct Geo {
   static constexpr int Q_BYTES = Q_PANEL * HALVES;
   static constexpr int KV_BYTES = KV_PANEL * HALVES;     // one K (or V) tile
   static constexpr int K_OFF = Q_BYTES;
-  static constexpr int V_OFF = Q_BYTES + STAGES * KV_BYTES;
-  static constexpr int BAR_OFF = Q_BYTES + 2 * STAGES * KV_BYTES;
+  static constexpr int V_OFF = Q_BYTES + K_STAGES * KV_BYTES;
+  static constexpr int BAR_OFF = V_OFF + V_STAGES * KV_BYTES;
   static constexpr int SMEM = BAR_OFF + 256 + 1024;      // + barriers + alignment slack
   static constexpr uint32_t IDESC_S = idesc_bf16_f32(BM, BN);
   static constexpr uint32_t IDESC_O = idesc_bf16_f32(BM, HD) | (1u << 16);  // B (= V) is MN-major
@@ -116,17 +116,19 @@ __global__ void __launch_bounds__(THREADS, 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + G::BAR_OFF);
   uint64_t* q_full = bars + 0;
-  uint64_t* kv_full = bars + 1;      // [STAGES]
-  uint64_t* kv_empty = bars + 3;     // [STAGES]
-  uint64_t* s_full = bars + 5;       // [2]
-  uint64_t* s_empty = bars + 7;      // [2]
-  uint64_t* p_full = bars + 9;
-  uint64_t* pv_done = bars + 10;
-  uint64_t* o_full = bars + 11;
-  uint64_t* mma_done = bars + 12;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 13);
-  int* s_ntiles = reinterpret_cast<int*>(bars + 14);
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 15);
+  uint64_t* k_full = bars + 1;       // [K_STAGES]
+  uint64_t* k_empty = bars + 4;      // [K_STAGES]
+  uint64_t* v_full = bars + 7;       // [V_STAGES]
+  uint64_t* v_empty = bars + 9;      // [V_STAGES]
+  uint64_t* s_full = bars + 11;      // [2]
+  uint64_t* s_empty = bars + 13;     // [2]
+  uint64_t* p_full = bars + 15;
+  uint64_t* pv_done = bars + 16;
+  uint64_t* o_full = bars + 17;
+  uint64_t* mma_done = bars + 18;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 19);
+  int* s_ntiles = reinterpret_cast<int*>(bars + 20);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 21);
   __shared__ int64_t s_maxpos[4];
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -153,9 +155,13 @@ __global__ void __launch_bounds__(THREADS, 1)
   }
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
-    for (int s = 0; s < STAGES; ++s) {
-      mbar_init(&kv_full[s], 1);
-      mbar_init(&kv_empty[s], 1);
+    for (int s = 0; s < K_STAGES; ++s) {
+      mbar_init(&k_full[s], 1);
+      mbar_init(&k_empty[s], 1);
+    }
+    for (int s = 0; s < V_STAGES; ++s) {
+      mbar_init(&v_full[s], 1);
+      mbar_init(&v_empty[s], 1);
     }
     for (int s = 0; s < 2; ++s) {
       mbar_init(&s_full[s], 1);
@@ -200,7 +206,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       for (int hf = 0; hf < G::HALVES; ++hf)
         tma_load_2d(smem + hf * G::Q_PANEL, &tmQ, q_full, h * HD + 64 * hf, static_cast<int>(tok0 + j0));
       for (int j = 0; j < n_tiles; ++j) {
-        const int s = j % STAGES;
+        const int ks = j % K_STAGES, vs = j % V_STAGES;
         const int key0 = j * BN;
         const int rem = n_keys - key0;
         const int nch = rem >= BN ? BN / CHUNK : (rem + CHUNK - 1) / CHUNK;
@@ -220,31 +226,33 @@ __global__ void __launch_bounds__(THREADS, 1)
             if (c < nch) flag_error(p.err, ERR_BAD_SLOT);
             blk[c] = 0;
           }
-        if (!mbar_wait(&kv_empty[s], ((j / STAGES) & 1) ^ 1, p.err) || *abort_flag) {
-          *abort_flag = 1;
-          break;
-        }
-        uint8_t* kdst = smem + G::K_OFF + s * G::KV_BYTES;
-        uint8_t* vdst = smem + G::V_OFF + s * G::KV_BYTES;
-        if (one_block) {
-          // the whole tile lies in one block (a contiguous cache): one 128-row box per panel
-          mbar_arrive_expect_tx(&kv_full[s], static_cast<uint32_t>(BN * 128 * G::HALVES * 2));
-          const int row = static_cast<int>(blk[0] * p.rows_per_block + g * p.rows_per_head + key0 % p.block_size);
-          for (int hf = 0; hf < G::HALVES; ++hf) {
-            tma_load_2d(kdst + hf * G::KV_PANEL, &tmK128, &kv_full[s], 64 * hf, row);
-            tma_load_2d(vdst + hf * G::KV_PANEL, &tmV128, &kv_full[s], 64 * hf, row);
+        const uint32_t bytes = one_block ? BN * 128 * G::HALVES : nch * CHUNK * 128 * G::HALVES;
+        for (int which = 0; which < 2; ++which) {   // K then V, each into its own ring
+          uint64_t* full = which == 0 ? &k_full[ks] : &v_full[vs];
+          uint64_t* empty = which == 0 ? &k_empty[ks] : &v_empty[vs];
+          const int nst = which == 0 ? K_STAGES : V_STAGES;
+          if (!mbar_wait(empty, ((j / nst) & 1) ^ 1, p.err) || *abort_flag) {
+            *abort_flag = 1;
+            break;
           }
-        } else {
-          mbar_arrive_expect_tx(&kv_full[s], static_cast<uint32_t>(nch * CHUNK * 128 * G::HALVES * 2));
-          for (int c = 0; c < nch; ++c) {
-            const int64_t s0 = key0 + c * CHUNK;
-            const int row = static_cast<int>(blk[c] * p.rows_per_block + g * p.rows_per_head + s0 % p.block_size);
-            for (int hf = 0; hf < G::HALVES; ++hf) {
-              tma_load_2d(kdst + hf * G::KV_PANEL + c * CHUNK * 128, &tmK, &kv_full[s], 64 * hf, row);
-              tma_load_2d(vdst + hf * G::KV_PANEL + c * CHUNK * 128, &tmV, &kv_full[s], 64 * hf, row);
+          uint8_t* dst = smem + (which == 0 ? G::K_OFF + ks * G::KV_BYTES : G::V_OFF + vs * G::KV_BYTES);
+          const CUtensorMap* map16 = which == 0 ? &tmK : &tmV;
+          const CUtensorMap* map128 = which == 0 ? &tmK128 : &tmV128;
+          mbar_arrive_expect_tx(full, bytes);
+          if (one_block) {
+            // the whole tile lies in one block (a contiguous cache): one 128-row box per panel
+            const int row = static_cast<int>(blk[0] * p.rows_per_block + g * p.rows_per_head + key0 % p.block_size);
+            for (int hf = 0; hf < G::HALVES; ++hf) tma_load_2d(dst + hf * G::KV_PANEL, map128, full, 64 * hf, row);
+          } else {
+            for (int c = 0; c < nch; ++c) {
+              const int64_t s0 = key0 + c * CHUNK;
+              const int row = static_cast<int>(blk[c] * p.rows_per_block + g * p.rows_per_head + s0 % p.block_size);
+              for (int hf = 0; hf < G::HALVES; ++hf)
+                tma_load_2d(dst + hf * G::KV_PANEL + c * CHUNK * 128, map16, full, 64 * hf, row);
             }
           }
         }
+        if (*abort_flag) break;
       }
     }
   } else if (warp == 5) {
@@ -252,39 +260,46 @@ __global__ void __launch_bounds__(THREADS, 1)
     if (lane == 0) {
       const uint32_t q_addr = smem_u32(smem);
       bool ok = mbar_wait(q_full, 0, p.err);
-      auto issue_pv = [&](int i) -> bool {
-        if (!mbar_wait(p_full, i & 1, p.err) || *abort_flag) return false;
+      // S_j = Q K_j^T into TMEM buffer j & 1; frees K stage j once the MMAs have read it
+      auto issue_s = [&](int j) -> bool {
+        const int ks = j % K_STAGES;
+        if (!mbar_wait(&k_full[ks], (j / K_STAGES) & 1, p.err) ||
+            !mbar_wait(&s_empty[j & 1], ((j >> 1) & 1) ^ 1, p.err) || *abort_flag)
+          return false;
         tc_fence_after();
-        const uint32_t v_addr = smem_u32(smem + G::V_OFF + (i % STAGES) * G::KV_BYTES);
+        const uint32_t k_addr = smem_u32(smem + G::K_OFF + ks * G::KV_BYTES);
 #pragma unroll
-        for (int ks = 0; ks < BN / 16; ++ks) {
-          const uint64_t bdesc = sw128_mnmajor_desc(v_addr + ks * 2048u, G::KV_PANEL);
-          mma_ts(tmem + O_COL, tmem + P_COL + ks * 8, bdesc, G::IDESC_O, (i | ks) != 0);
-        }
-        tc_commit(pv_done);
-        tc_commit(&kv_empty[i % STAGES]);
-        return true;
-      };
-      for (int j = 0; j < n_tiles && ok; ++j) {
-        const int s = j % STAGES;
-        if (!mbar_wait(&kv_full[s], (j / STAGES) & 1, p.err) || !mbar_wait(&s_empty[j & 1], ((j >> 1) & 1) ^ 1, p.err) ||
-            *abort_flag) {
-          ok = false;
-          break;
-        }
-        tc_fence_after();
-        const uint32_t k_addr = smem_u32(smem + G::K_OFF + s * G::KV_BYTES);
-#pragma unroll
-        for (int ks = 0; ks < HD / 16; ++ks) {
-          const int hf = ks / 4, kk = ks % 4;
-          const uint64_t adesc = sw128_kmajor_desc(q_addr + hf * G::Q_PANEL) + 2u * kk;
-          const uint64_t bdesc = sw128_kmajor_desc(k_addr + hf * G::KV_PANEL) + 2u * kk;
-          tc_mma_f16(tmem + S_COL + (j & 1) * 128, adesc, bdesc, G::IDESC_S, ks != 0);
+        for (int kk = 0; kk < HD / 16; ++kk) {
+          const int hf = kk / 4, kq = kk % 4;
+          const uint64_t adesc = sw128_kmajor_desc(q_addr + hf * G::Q_PANEL) + 2u * kq;
+          const uint64_t bdesc = sw128_kmajor_desc(k_addr + hf * G::KV_PANEL) + 2u * kq;
+          tc_mma_f16(tmem + S_COL + (j & 1) * 128, adesc, bdesc, G::IDESC_S, kk != 0);
         }
         tc_commit(&s_full[j & 1]);
-        if (j >= 1 && !issue_pv(j - 1)) ok = false;
+        tc_commit(&k_empty[ks]);
+        return true;
+      };
+      // O += P_j V_j (P from TMEM); frees V stage j
+      auto issue_pv = [&](int j) -> bool {
+        const int vs = j % V_STAGES;
+        if (!mbar_wait(&v_full[vs], (j / V_STAGES) & 1, p.err) || !mbar_wait(p_full, j & 1, p.err) || *abort_flag)
+          return false;
+        tc_fence_after();
+        const uint32_t v_addr = smem_u32(smem + G::V_OFF + vs * G::KV_BYTES);
+#pragma unroll
+        for (int kk = 0; kk < BN / 16; ++kk) {
+          const uint64_t bdesc = sw128_mnmajor_desc(v_addr + kk * 2048u, G::KV_PANEL);
+          mma_ts(tmem + O_COL, tmem + P_COL + kk * 8, bdesc, G::IDESC_O, (j | kk) != 0);
+        }
+        tc_commit(pv_done);
+        tc_commit(&v_empty[vs]);
+        return true;
+      };
+      if (ok) ok = issue_s(0);
+      for (int j = 0; j < n_tiles && ok; ++j) {
+        if (j + 1 < n_tiles) ok = issue_s(j + 1);   // the next scores overlap this tile's softmax
+        if (ok) ok = issue_pv(j);
       }
-      if (ok && n_tiles > 0) ok = issue_pv(n_tiles - 1);
       if (ok) tc_commit(o_full);
       if (!ok) *abort_flag = 1;
       tc_commit(mma_done);
@@ -315,13 +330,18 @@ __global__ void __launch_bounds__(THREADS, 1)
       mbar_arrive(&s_empty[sb]);
       const int64_t key0 = static_cast<int64_t>(j) * BN;
       float mx = -INFINITY;
+      const int64_t last_vis = my_pos < p.n_slots - 1 ? my_pos : p.n_slots - 1;
+      if (key0 + BN - 1 <= last_vis) {            // every key of the tile is visible to this row
 #pragma unroll
-      for (int c = 0; c < BN; ++c) {
-        const int64_t k = key0 + c;
-        const bool vis = k <= my_pos && k < p.n_slots;
-        v[c] = vis ? v[c] * p.scale_log2 : -INFINITY;
-        mx = fmaxf(mx, v[c]);
+        for (int c = 0; c < BN; ++c) mx = fmaxf(mx, v[c]);
+      } else {
+#pragma unroll
+        for (int c = 0; c < BN; ++c) {
+          v[c] = key0 + c <= last_vis ? v[c] : -INFINITY;
+          mx = fmaxf(mx, v[c]);
+        }
       }
+      mx *= p.scale_log2;                          // max in the log2 domain (the scale is positive)
       const float m_new = fmaxf(m_ref, mx);
       // Whether a row moves its reference max is decided per row, but the TMEM accesses that rescale O are
       // .sync.aligned warp instructions: the warp takes the rescale path if any of its rows needs it, and rows that
@@ -335,7 +355,8 @@ __global__ void __launch_bounds__(THREADS, 1)
       float sum = 0.f;
 #pragma unroll
       for (int i = 0; i < BN / 2; ++i) {
-        const float p0 = exp2f(v[2 * i] - sub), p1 = exp2f(v[2 * i + 1] - sub);
+        const float p0 = exp2f(fmaf(v[2 * i], p.scale_log2, -sub));
+        const float p1 = exp2f(fmaf(v[2 * i + 1], p.scale_log2, -sub));
         sum += p0 + p1;
         pk[i] = pack_bf16x2(p0, p1);
       }
@@ -365,14 +386,19 @@ __global__ void __launch_bounds__(THREADS, 1)
         tmem_st_32x32b_x16(tmem + lane_base + P_COL + c * 16, q16);
       }
       tc_wait_st();
-      if (key0 + BN > n_keys && key0 + row >= n_keys) {
-        // V rows past the last key hold stale data; P is 0 there but 0 * NaN is not, so zero them
-        uint4* vrow = reinterpret_cast<uint4*>(smem + G::V_OFF + (j % STAGES) * G::KV_BYTES + row * 128);
+      if (key0 + BN > n_keys) {                    // the tile with the last key: same for every row
+        // V rows past the last key hold stale data; P is 0 there but 0 * NaN is not, so zero them. V_j is waited
+        // for first (softmax j follows S_j, which only waited for K_j).
+        ok = __all_sync(0xffffffffu, mbar_wait(&v_full[j % V_STAGES], (j / V_STAGES) & 1, p.err));
+        if (!ok) break;
+        if (key0 + row >= n_keys) {
+          uint4* vrow = reinterpret_cast<uint4*>(smem + G::V_OFF + (j % V_STAGES) * G::KV_BYTES + row * 128);
 #pragma unroll
-        for (int hf = 0; hf < G::HALVES; ++hf)
+          for (int hf = 0; hf < G::HALVES; ++hf)
 #pragma unroll
-          for (int i = 0; i < 8; ++i) vrow[hf * (G::KV_PANEL / 16) + i] = make_uint4(0, 0, 0, 0);
-        fence_async_smem();
+            for (int i = 0; i < 8; ++i) vrow[hf * (G::KV_PANEL / 16) + i] = make_uint4(0, 0, 0, 0);
+          fence_async_smem();
+        }
       }
       tc_fence_before();
       mbar_arrive(p_full);
