@@ -41,6 +41,7 @@ SIGNATURES = {
     "fs_device_error": (c_int, [c_int, ctypes.POINTER(ctypes.c_uint)]),
     "fs_launch_count": (c_i64, []),
     "fs_set_persistent_sms": (c_int, [c_int]),
+    "fs_set_gemm_pair_mode": (c_int, [c_int]),
     "fs_rmsnorm": (c_int, [c_vp, c_i64, c_vp, c_vp, c_i64, c_i64, c_i64, c_float, c_int, c_vp]),
     "fs_gemm": (c_int, [c_vp, c_i64, c_vp, c_i64, c_vp, c_i64, c_vp, c_i64, c_i64, c_i64, c_i64, c_i64, c_int, c_int,
                         c_vp]),

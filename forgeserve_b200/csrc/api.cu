@@ -95,6 +95,8 @@ int64_t fs_launch_count(void) { return g_launches.load(std::memory_order_relaxed
 
 int fs_set_persistent_sms(int n) { return tcg::set_persistent_sms(n); }
 
+int fs_set_gemm_pair_mode(int on) { return tcg::set_pair_mode(on); }
+
 int fs_rmsnorm(const void* x, int64_t x_stride, const void* w, void* y, int64_t y_stride, int64_t rows, int64_t dim,
                float eps, int dtype, void* stream) {
   if (!x || !w || !y) return rows <= 0 ? 0 : fail("fs_rmsnorm: NULL pointer");

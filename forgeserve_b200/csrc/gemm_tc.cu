@@ -90,6 +90,65 @@ __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, unsign
   return __all_sync(0xffffffffu, ok);
 }
 
+// One accumulator (128 rows x 256 fp32 columns in TMEM, lanes 32q..32q+31 read by this warp) -> global memory,
+// with the fused epilogue. `row` is this thread's output row.
+template <int EPI>
+__device__ __forceinline__ void epilogue_tile(const Params& p, uint32_t tmem_base, int acc, int q, int lane, int row,
+                                              int n_blk, bool vec_ok) {
+  const bool row_ok = row < p.M;
+  __nv_bfloat16* crow = p.C + static_cast<int64_t>(row) * p.ldc;
+  const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(acc * BN);
+  if constexpr (EPI == EPI_SWIGLU) {
+#pragma unroll 1
+    for (int c = 0; c < BN / 64; ++c) {
+      uint32_t g[32], u[32];
+      tmem_ld_32x32b_x32(taddr + c * 32, g);
+      tmem_ld_32x32b_x32(taddr + BN / 2 + c * 32, u);
+      tc_wait_ld();
+      float v[32];
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {
+        const float gb = rnd<__nv_bfloat16>(__uint_as_float(g[i]));
+        const float ub = rnd<__nv_bfloat16>(__uint_as_float(u[i]));
+        v[i] = rnd<__nv_bfloat16>(silu_f(gb)) * ub;
+      }
+      if (row_ok) store_row32(crow, n_blk * (BN / 2) + c * 32, p.n_out, vec_ok, v);
+    }
+  } else {
+#pragma unroll 1
+    for (int c = 0; c < BN / 32; ++c) {
+      uint32_t r[32];
+      tmem_ld_32x32b_x32(taddr + c * 32, r);
+      tc_wait_ld();
+      const int col0 = n_blk * BN + c * 32;
+      float v[32];
+#pragma unroll
+      for (int i = 0; i < 32; ++i) v[i] = rnd<__nv_bfloat16>(__uint_as_float(r[i]));
+      if constexpr (EPI == EPI_RESIDUAL) {
+        if (row_ok) {
+          const __nv_bfloat16* rrow = p.R + static_cast<int64_t>(row) * p.ldr;
+          if (vec_ok && col0 + 32 <= p.n_out) {
+            const uint4* src = reinterpret_cast<const uint4*>(rrow + col0);
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              const uint4 w = src[i];
+              v[8 * i + 0] += bf16_lo(w.x), v[8 * i + 1] += bf16_hi(w.x);
+              v[8 * i + 2] += bf16_lo(w.y), v[8 * i + 3] += bf16_hi(w.y);
+              v[8 * i + 4] += bf16_lo(w.z), v[8 * i + 5] += bf16_hi(w.z);
+              v[8 * i + 6] += bf16_lo(w.w), v[8 * i + 7] += bf16_hi(w.w);
+            }
+          } else {
+#pragma unroll
+            for (int i = 0; i < 32; ++i)
+              if (col0 + i < p.n_out) v[i] += __bfloat162float(rrow[col0 + i]);
+          }
+        }
+      }
+      if (row_ok) store_row32(crow, col0, p.n_out, vec_ok, v);
+    }
+  }
+}
+
 template <int EPI>
 __global__ void __launch_bounds__(THREADS, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, Params p) {
@@ -218,59 +277,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       tc_fence_after();
       int m_blk, n_blk;
       tile_coords(tile, p.num_m_blocks, m_blk, n_blk);
-      const int row = m_blk * BM + q * 32 + lane;
-      const bool row_ok = row < p.M;
-      __nv_bfloat16* crow = p.C + static_cast<int64_t>(row) * p.ldc;
-      const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(acc * BN);
-      if constexpr (EPI == EPI_SWIGLU) {
-#pragma unroll 1
-        for (int c = 0; c < BN / 64; ++c) {
-          uint32_t g[32], u[32];
-          tmem_ld_32x32b_x32(taddr + c * 32, g);
-          tmem_ld_32x32b_x32(taddr + BN / 2 + c * 32, u);
-          tc_wait_ld();
-          float v[32];
-#pragma unroll
-          for (int i = 0; i < 32; ++i) {
-            const float gb = rnd<__nv_bfloat16>(__uint_as_float(g[i]));
-            const float ub = rnd<__nv_bfloat16>(__uint_as_float(u[i]));
-            v[i] = rnd<__nv_bfloat16>(silu_f(gb)) * ub;
-          }
-          if (row_ok) store_row32(crow, n_blk * (BN / 2) + c * 32, p.n_out, vec_ok, v);
-        }
-      } else {
-#pragma unroll 1
-        for (int c = 0; c < BN / 32; ++c) {
-          uint32_t r[32];
-          tmem_ld_32x32b_x32(taddr + c * 32, r);
-          tc_wait_ld();
-          const int col0 = n_blk * BN + c * 32;
-          float v[32];
-#pragma unroll
-          for (int i = 0; i < 32; ++i) v[i] = rnd<__nv_bfloat16>(__uint_as_float(r[i]));
-          if constexpr (EPI == EPI_RESIDUAL) {
-            if (row_ok) {
-              const __nv_bfloat16* rrow = p.R + static_cast<int64_t>(row) * p.ldr;
-              if (vec_ok && col0 + 32 <= p.n_out) {
-                const uint4* src = reinterpret_cast<const uint4*>(rrow + col0);
-#pragma unroll
-                for (int i = 0; i < 4; ++i) {
-                  const uint4 w = src[i];
-                  v[8 * i + 0] += bf16_lo(w.x), v[8 * i + 1] += bf16_hi(w.x);
-                  v[8 * i + 2] += bf16_lo(w.y), v[8 * i + 3] += bf16_hi(w.y);
-                  v[8 * i + 4] += bf16_lo(w.z), v[8 * i + 5] += bf16_hi(w.z);
-                  v[8 * i + 6] += bf16_lo(w.w), v[8 * i + 7] += bf16_hi(w.w);
-                }
-              } else {
-#pragma unroll
-                for (int i = 0; i < 32; ++i)
-                  if (col0 + i < p.n_out) v[i] += __bfloat162float(rrow[col0 + i]);
-              }
-            }
-          }
-          if (row_ok) store_row32(crow, col0, p.n_out, vec_ok, v);
-        }
-      }
+      epilogue_tile<EPI>(p, tmem_base, acc, q, lane, m_blk * BM + q * 32 + lane, n_blk, vec_ok);
       tc_fence_before();
       mbar_arrive(&tempty[acc]);
       if (++acc == NUM_ACC) acc = 0, acc_ph ^= 1u;
@@ -284,6 +291,207 @@ __global__ void __launch_bounds__(THREADS, 1)
     tc_fence_after();
     tmem_dealloc(tmem_base, TMEM_COLS);
   }
+}
+
+// ============================================================================ 2-SM (cta_group::2) variant
+// A CTA pair (cluster of 2) computes a 256 x 256 tile with tcgen05.mma.cta_group::2 (M 256, N 256): each CTA stages
+// its own 128 rows of A and its own 128-row half of B (32 KB per k-block instead of 48 KB), so shared-memory
+// traffic per FLOP drops by a third against the 1-SM kernel, and 6 stages fit. The leader CTA (rank 0) issues
+// the MMAs; every copy completes on the leader's barrier; the leader signals both CTAs' barriers; both CTAs'
+// epilogues read their own TMEM (their 128 rows) and report to the leader's accumulator-free barrier.
+constexpr int STAGES2 = 6;
+constexpr int STAGE2_BYTES = A_BYTES + BH_BYTES;  // 32 KiB per CTA per k-block
+constexpr int SMEM2_BYTES = STAGES2 * STAGE2_BYTES + 1024 + BAR_BYTES;
+constexpr uint32_t IDESC2 = idesc_bf16_f32(2 * BM, BN);
+
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+// Address of the same shared-memory offset in CTA `cta` of the cluster.
+__device__ __forceinline__ uint32_t map_to_cta(uint32_t smem_addr, uint32_t cta) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_addr), "r"(cta));
+  return r;
+}
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void mbar_arrive_remote(uint32_t cluster_addr) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
+// 2-D TMA load into this CTA's shared memory whose completion is counted on a barrier of either CTA of the pair.
+__device__ __forceinline__ void tma_load_2d_pair(void* smem_dst, const CUtensorMap* map, uint32_t bar_cluster_addr,
+                                                 int x, int y) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], "
+      "[%2];" ::"r"(smem_u32(smem_dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(bar_cluster_addr), "r"(x), "r"(y)
+      : "memory");
+}
+__device__ __forceinline__ void tc_mma_f16_pair(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                                uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+// Arrive on a barrier (of either CTA of the pair) once every pair MMA issued so far by this thread has completed.
+__device__ __forceinline__ void tc_commit_pair(uint32_t bar_cluster_addr) {
+  asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar_cluster_addr)
+               : "memory");
+}
+__device__ __forceinline__ void tmem_alloc_pair(uint32_t* smem_slot, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(smem_slot)),
+               "r"(ncols)
+               : "memory");
+}
+__device__ __forceinline__ void tmem_relinquish_pair() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+
+template <int EPI>
+__global__ void __launch_bounds__(THREADS, 1)
+    gemm_tc2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, Params p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* tiles = smem;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + STAGES2 * STAGE2_BYTES);
+  uint64_t* full = bars;                          // leader's: both CTAs' copies complete here
+  uint64_t* empty = bars + STAGES2;               // each CTA's own: the leader's MMAs released the stage
+  uint64_t* tfull = bars + 2 * STAGES2;           // each CTA's own: accumulator ready
+  uint64_t* tempty = bars + 2 * STAGES2 + NUM_ACC;  // leader's: both epilogues released the accumulator
+  uint64_t* mma_done = bars + 2 * STAGES2 + 2 * NUM_ACC;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t cta = cluster_ctarank();
+  const int pair = blockIdx.x >> 1, num_pairs = gridDim.x >> 1;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES2; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < NUM_ACC; ++a) {
+      mbar_init(&tfull[a], 1);
+      mbar_init(&tempty[a], 2 * 128);
+    }
+    mbar_init(mma_done, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 2) {
+    tmem_alloc_pair(tmem_slot, TMEM_COLS);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync_all();   // both CTAs' barriers exist before any copy or arrive reaches them
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  const int num_m_pairs = (p.num_m_blocks + 1) >> 1;
+
+  if (warp == 0) {
+    // -------------------------------------------------------------------------------- TMA producer (both CTAs)
+    if (lane == 0) {
+      int s = 0;
+      uint32_t ph = 0;
+      bool ok = true;
+      for (int tile = pair; tile < p.num_tiles && ok; tile += num_pairs) {
+        const int m_pair = tile % num_m_pairs, n_blk = tile / num_m_pairs;
+        const int a_row = m_pair * 2 * BM + static_cast<int>(cta) * BM;
+        const int b_row = EPI == EPI_SWIGLU ? (cta == 0 ? n_blk * (BN / 2) : p.n_out + n_blk * (BN / 2))
+                                            : n_blk * BN + static_cast<int>(cta) * (BN / 2);
+        for (int kb = 0; kb < p.k_blocks; ++kb) {
+          if (!mbar_wait(&empty[s], ph ^ 1u, p.err) || *abort_flag) {
+            ok = false;
+            break;
+          }
+          const uint32_t leader_full = map_to_cta(smem_u32(&full[s]), 0);
+          if (cta == 0) mbar_arrive_expect_tx(&full[s], 2 * STAGE2_BYTES);
+          tma_load_2d_pair(tiles + s * STAGE2_BYTES, &tmA, leader_full, kb * BK, a_row);
+          tma_load_2d_pair(tiles + s * STAGE2_BYTES + A_BYTES, &tmB, leader_full, kb * BK, b_row);
+          if (++s == STAGES2) s = 0, ph ^= 1u;
+        }
+      }
+      if (!ok) *abort_flag = 1;
+    }
+  } else if (warp == 1) {
+    // -------------------------------------------------------------------------------- MMA issuer (leader only)
+    if (lane == 0 && cta == 0) {
+      int s = 0, acc = 0;
+      uint32_t ph = 0, acc_ph = 0;
+      bool ok = true;
+      for (int tile = pair; tile < p.num_tiles && ok; tile += num_pairs) {
+        if (!mbar_wait(&tempty[acc], acc_ph ^ 1u, p.err) || *abort_flag) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
+        for (int kb = 0; kb < p.k_blocks; ++kb) {
+          if (!mbar_wait(&full[s], ph, p.err) || *abort_flag) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_addr = smem_u32(tiles + s * STAGE2_BYTES);
+          const uint64_t adesc = sw128_kmajor_desc(a_addr);
+          const uint64_t bdesc = sw128_kmajor_desc(a_addr + A_BYTES);
+#pragma unroll
+          for (int k = 0; k < BK / 16; ++k) tc_mma_f16_pair(d_tmem, adesc + 2u * k, bdesc + 2u * k, IDESC2, (kb | k) != 0);
+          const uint32_t e = smem_u32(&empty[s]);
+          tc_commit_pair(map_to_cta(e, 0));
+          tc_commit_pair(map_to_cta(e, 1));
+          if (++s == STAGES2) s = 0, ph ^= 1u;
+        }
+        if (!ok) break;
+        const uint32_t f = smem_u32(&tfull[acc]);
+        tc_commit_pair(map_to_cta(f, 0));
+        tc_commit_pair(map_to_cta(f, 1));
+        if (++acc == NUM_ACC) acc = 0, acc_ph ^= 1u;
+      }
+      if (!ok) *abort_flag = 1;
+      const uint32_t d = smem_u32(mma_done);
+      tc_commit_pair(map_to_cta(d, 0));
+      tc_commit_pair(map_to_cta(d, 1));
+    }
+  } else if (warp >= 4) {
+    // -------------------------------------------------------------------------------- epilogue (both CTAs)
+    const int q = warp - 4;
+    const bool vec_ok = ((p.ldc & 7) == 0) && ((reinterpret_cast<uintptr_t>(p.C) & 15) == 0) &&
+                        (EPI != EPI_RESIDUAL || (((p.ldr & 7) == 0) && ((reinterpret_cast<uintptr_t>(p.R) & 15) == 0)));
+    int acc = 0;
+    uint32_t acc_ph = 0;
+    for (int tile = pair; tile < p.num_tiles; tile += num_pairs) {
+      if (!warp_wait(&tfull[acc], acc_ph, p.err)) break;
+      tc_fence_after();
+      const int m_pair = tile % num_m_pairs, n_blk = tile / num_m_pairs;
+      const int row = m_pair * 2 * BM + static_cast<int>(cta) * BM + q * 32 + lane;
+      epilogue_tile<EPI>(p, tmem_base, acc, q, lane, row, n_blk, vec_ok);
+      tc_fence_before();
+      const uint32_t te = smem_u32(&tempty[acc]);
+      if (cta == 0) mbar_arrive(&tempty[acc]);
+      else mbar_arrive_remote(map_to_cta(te, 0));
+      if (++acc == NUM_ACC) acc = 0, acc_ph ^= 1u;
+    }
+  }
+
+  __syncthreads();
+  if (warp == 2) {
+    mbar_wait(mma_done, 0, p.err);   // every pair MMA has completed (this CTA's TMEM included)
+    tc_fence_after();
+    tmem_dealloc_pair(tmem_base, TMEM_COLS);
+  }
+  cluster_sync_all();   // neither CTA leaves while the other may still signal its barriers
 }
 
 // ------------------------------------------------------------------------------------------------ host
@@ -355,6 +563,41 @@ static int launch_t(const CUtensorMap& ma, const CUtensorMap& mb, const Params& 
   return check_launch("gemm_tc_kernel");
 }
 
+template <int EPI>
+static int launch_pair_t(const CUtensorMap& ma, const CUtensorMap& mb, const Params& p, int grid, cudaStream_t st) {
+  static bool attr_set[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev >= 0 && dev < 64 && !attr_set[dev]) {
+    if (cudaFuncSetAttribute(gemm_tc2_kernel<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM2_BYTES) !=
+        cudaSuccess)
+      return check_launch("gemm_tc2 set smem");
+    attr_set[dev] = true;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(grid));
+  cfg.blockDim = dim3(THREADS);
+  cfg.dynamicSmemBytes = SMEM2_BYTES;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, gemm_tc2_kernel<EPI>, ma, mb, p);
+  if (e != cudaSuccess) return fail(std::string("gemm_tc2_kernel launch: ") + cudaGetErrorString(e));
+  return check_launch("gemm_tc2_kernel");
+}
+
+static int g_pair_mode = 1;   // 1: use the 2-SM kernel for M > 128; 0: always the 1-SM kernel
+
+int set_pair_mode(int on) {
+  g_pair_mode = on ? 1 : 0;
+  return 0;
+}
+
 int gemm_tc(const void* A, int64_t lda, const void* B, int64_t ldb, void* C, int64_t ldc, const void* R,
             int64_t ldr, int64_t M, int64_t N, int64_t K, int64_t n_out, int epi, cudaStream_t stream) {
   if (M <= 0 || N <= 0 || n_out <= 0) return 0;
@@ -376,6 +619,17 @@ int gemm_tc(const void* A, int64_t lda, const void* B, int64_t ldb, void* C, int
   p.k_blocks = static_cast<int>((K + BK - 1) / BK);
   p.err = error_word();
   if (!p.err) return -1;
+  if (g_pair_mode && M > BM) {
+    const int num_m_pairs = (p.num_m_blocks + 1) / 2;
+    p.num_tiles = num_m_pairs * num_n_blocks;
+    const int pairs = p.num_tiles < sm_count() / 2 ? p.num_tiles : sm_count() / 2;
+    switch (epi) {
+      case EPI_STORE: return launch_pair_t<EPI_STORE>(ma, mb, p, 2 * pairs, stream);
+      case EPI_RESIDUAL: return launch_pair_t<EPI_RESIDUAL>(ma, mb, p, 2 * pairs, stream);
+      case EPI_SWIGLU: return launch_pair_t<EPI_SWIGLU>(ma, mb, p, 2 * pairs, stream);
+      default: return fail("gemm: unknown epilogue");
+    }
+  }
   const int grid = p.num_tiles < sm_count() ? p.num_tiles : sm_count();
   switch (epi) {
     case EPI_STORE: return launch_t<EPI_STORE>(ma, mb, p, grid, stream);

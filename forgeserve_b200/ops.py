@@ -63,6 +63,11 @@ def set_persistent_sms(n: int) -> None:
     L.check(L.load().fs_set_persistent_sms(int(n)), "fs_set_persistent_sms")
 
 
+def set_gemm_pair_mode(on: bool) -> None:
+    """Choose the 2-SM (CTA pair) GEMM for M > 128 (default) or always the 1-SM GEMM."""
+    L.check(L.load().fs_set_gemm_pair_mode(int(bool(on))), "fs_set_gemm_pair_mode")
+
+
 def rmsnorm(x: torch.Tensor, w: torch.Tensor, eps: float, out: Optional[torch.Tensor] = None) -> torch.Tensor:
     """RMSNorm over the last dim (forgeserve/model.py:29-31)."""
     require_cuda(x, w)

@@ -40,6 +40,10 @@ int64_t fs_launch_count(void);
  * that no GEMM CTA waits behind a resident communication kernel. No counterpart in the reference (CPU/gloo). */
 int fs_set_persistent_sms(int n);
 
+/* on != 0 (default): bf16 GEMMs with M > 128 run on CTA pairs (tcgen05 cta_group::2, 256 x 256 tiles); 0: always on
+ * single CTAs (128 x 256 tiles). Process-wide. For comparing the two kernels. No counterpart in the reference. */
+int fs_set_gemm_pair_mode(int on);
+
 /* RMSNorm over rows: y = T(T(x * rsqrt(mean(x^2) + eps)) * w), fp32 statistics.
  * Replaces RMSNorm.forward, forgeserve/model.py:29-31. y may alias x. */
 int fs_rmsnorm(const void* x, int64_t x_stride, const void* w, void* y, int64_t y_stride, int64_t rows, int64_t dim,

@@ -371,3 +371,22 @@ def test_kv_store_and_paged_gather_round_trip():
     torch.testing.assert_close(k_all[:, :, :10], k, atol=0, rtol=0)
     torch.testing.assert_close(pool_k[2, :, 1], k[0, :, 5], atol=0, rtol=0)
     torch.testing.assert_close(ops.paged_gather(pool_v, table)[:, :, :10], v, atol=0, rtol=0)
+
+
+@pytest.mark.parametrize("epi", [L.FS_EPI_STORE, L.FS_EPI_RESIDUAL, L.FS_EPI_SWIGLU])
+@pytest.mark.parametrize("M,N,K", [(256, 512, 192), (300, 1000, 256), (1000, 768, 4096), (8192, 1024, 512)])
+def test_gemm_pair_kernel_matches_single_cta_kernel(epi, M, N, K):
+    """The 2-SM (CTA pair) GEMM and the 1-SM GEMM give the same result on the same inputs."""
+    a = torch.randn(M, K, device=DEV).bfloat16()
+    w = (torch.randn(N, K, device=DEV) / math.sqrt(K)).bfloat16()
+    r = torch.randn(M, N, device=DEV).bfloat16()
+    kw = dict(residual=r) if epi == L.FS_EPI_RESIDUAL else {}
+    try:
+        ops.set_gemm_pair_mode(False)
+        single = ops.linear(a, w, epi, **kw)
+    finally:
+        ops.set_gemm_pair_mode(True)
+    pair = ops.linear(a, w, epi, **kw)
+    bf16_close(pair, single.float(), rel=2 ** -8)
+    if epi == L.FS_EPI_STORE:
+        bf16_close(pair, a.double() @ w.double().t())
