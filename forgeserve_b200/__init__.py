@@ -9,6 +9,7 @@ from .model import ForgeModel
 from .paged import BlockAllocator, OutOfBlocks, PagedKVPool
 from .parallel import SINGLE, TPContext
 from .pipeline import PipelineStage, PipelineState, bubble_fraction, pipeline_forward, pipeline_generate, stage_layers
+from .pipeline_engine import PipelineEngine
 from .sampling import generate, sample
 from .speculative import speculative_generate, verify_draft
 

@@ -9,6 +9,9 @@ What runs differently: the pool lives on the model's device in the model's dtype
 for the last position only; greedy rows are sampled together by one argmax kernel and read back with one copy,
 and temperature rows draw from the engine's seeded CPU generator in row order (the order of the reference's
 per-row `sample` calls, so the generator stream is consumed identically).
+
+`Scheduler` holds the scheduling; `Engine` runs it over one model, `PipelineEngine` (pipeline_engine.py) over the
+stages of a pipeline.
 """
 
 from collections import deque
@@ -35,10 +38,13 @@ class Request:
     finished: bool = False
 
 
-class Engine:
-    def __init__(self, model, num_blocks: int, block_size: int = 16, max_batch: int = 8, seed: int = 0):
-        self.model, self.cfg = model, model.cfg
-        self.pool = PagedKVPool(self.cfg, num_blocks, block_size, tp=model.tp, dtype=model.dtype, device=model.device)
+class Scheduler:
+    """The reference's continuous-batching scheduler (engine.py:36-139) over an abstract forward step.
+
+    Subclasses provide `self.pool` (a PagedKVPool), `self.cfg` and `_forward_rows(reqs, idx, positions, tables)`,
+    which runs one model step for the given rows and returns one sampled token per row."""
+
+    def _init_scheduler(self, max_batch: int, seed: int) -> None:
         self.max_batch = max_batch
         self.generator = torch.Generator().manual_seed(seed)
         self.waiting: Deque[Request] = deque()
@@ -89,10 +95,9 @@ class Engine:
         self.waiting.popleft()
         req.blocks = self.pool.allocator.allocate(need)
         positions = torch.arange(len(tokens))[None]
-        views = self.pool.views(torch.tensor([req.blocks]), positions)
-        logits = self.model(torch.tensor([tokens]), positions, views, last_only=True)
+        token = self._forward_rows([req], torch.tensor([tokens]), positions, torch.tensor([req.blocks]))[0]
         req.cached = len(tokens)
-        self._append(req, self._sample_rows(logits[:, -1], [req])[0])
+        self._append(req, token)
         if not req.finished:
             self.running.append(req)
         return True
@@ -127,14 +132,17 @@ class Engine:
         tables = torch.tensor([r.blocks + [0] * (width - len(r.blocks)) for r in self.running])
         positions = torch.tensor([[r.cached] for r in self.running])
         idx = torch.tensor([[r.output[-1]] for r in self.running])
-        logits = self.model(idx, positions, self.pool.views(tables, positions), last_only=True)
         rows = list(self.running)
-        tokens = self._sample_rows(logits[:, -1], rows)
+        tokens = self._forward_rows(rows, idx, positions, tables)
         for req, tok in zip(rows, tokens):
             req.cached += 1
             self._append(req, tok)
             if req.finished:
                 self.running.remove(req)
+
+    def _forward_rows(self, reqs: List[Request], idx: torch.Tensor, positions: torch.Tensor,
+                      tables: torch.Tensor) -> List[int]:
+        raise NotImplementedError
 
     def _sample_rows(self, logits: torch.Tensor, reqs: List[Request]) -> List[int]:
         """One token per row of logits (R, V): greedy rows by one argmax kernel, the others from the engine's
@@ -156,3 +164,16 @@ class Engine:
             req.finished = True
             self.pool.allocator.release(req.blocks)
             req.blocks = []
+
+
+class Engine(Scheduler):
+    """Continuous batching of one model on one GPU (forgeserve/engine.py:36-45)."""
+
+    def __init__(self, model, num_blocks: int, block_size: int = 16, max_batch: int = 8, seed: int = 0):
+        self.model, self.cfg = model, model.cfg
+        self.pool = PagedKVPool(self.cfg, num_blocks, block_size, tp=model.tp, dtype=model.dtype, device=model.device)
+        self._init_scheduler(max_batch, seed)
+
+    def _forward_rows(self, reqs, idx, positions, tables):
+        logits = self.model(idx, positions, self.pool.views(tables, positions), last_only=True)
+        return self._sample_rows(logits[:, -1], reqs)

@@ -172,7 +172,11 @@ def layer_forward_(blk: "Block", x: torch.Tensor, positions: torch.Tensor, kv, r
         ops.rope_kv_write(qkv2, rope_cos, rope_sin, positions, desc, B, T, nh, nkv, hd, slot_base=base,
                           slot_from_pos=from_pos)
     attn = torch.empty(B, T, nh * hd, dtype=x.dtype, device=x.device)
-    ops.attention(qkv2[:, : nh * hd], desc, n_slots, positions, attn.view(M, nh * hd), B, T, nh, nkv, hd)
+    if T == 1 and hd in (64, 128) and nh // nkv <= 8:
+        # one new token per row (decode): split-KV kernel reading each K/V row once per KV head
+        ops.attention_decode(qkv2[:, : nh * hd], desc, n_slots, positions, attn.view(M, nh * hd), B, nh, nkv, hd)
+    else:
+        ops.attention(qkv2[:, : nh * hd], desc, n_slots, positions, attn.view(M, nh * hd), B, T, nh, nkv, hd)
     if bound is not None:
         commit()
     del keep

@@ -136,6 +136,35 @@ def attention(q: torch.Tensor, kv: L.KVCacheDesc, n_slots: int, positions: torch
     return out
 
 
+_DECODE_WS = {}
+
+
+def decode_workspace(device: torch.device, nbytes: int) -> torch.Tensor:
+    """A per-device scratch buffer for split decode attention, grown on demand and reused across calls (calls are
+    ordered on one stream; concurrent streams would need their own)."""
+    key = str(device)
+    ws = _DECODE_WS.get(key)
+    if ws is None or ws.numel() < nbytes:
+        ws = torch.empty(max(nbytes, 1 << 20), dtype=torch.uint8, device=device)
+        _DECODE_WS[key] = ws
+    return ws
+
+
+def attention_decode(q: torch.Tensor, kv: L.KVCacheDesc, n_slots: int, positions: torch.Tensor, out: torch.Tensor,
+                     B: int, nh: int, nkv: int, hd: int) -> torch.Tensor:
+    """Split-KV decode attention: one query per row (positions (B,) or (B, 1))."""
+    require_cuda(q, positions, out)
+    _, ldq = _rows(q)
+    _, ldo = _rows(out)
+    lib = L.load()
+    need = int(lib.fs_attention_decode_workspace(B, nh, nkv, hd, n_slots))
+    ws = decode_workspace(q.device, need) if need > 0 else None
+    L.check(lib.fs_attention_decode(_p(q), ldq, ctypes.byref(kv), n_slots, _p(positions), _p(out), ldo, B, nh, nkv, hd,
+                                    1.0 / math.sqrt(hd), _p(ws), 0 if ws is None else ws.numel(),
+                                    dtype_code(q.dtype), _stream(q)), "fs_attention_decode")
+    return out
+
+
 def kv_store(k: torch.Tensor, v: torch.Tensor, positions: torch.Tensor, kv: L.KVCacheDesc) -> None:
     require_cuda(k, v, positions)
     B, nkv, T, hd = k.shape

@@ -114,6 +114,16 @@ int fs_attention_impl(const void* q, int64_t ldq, const fs_kv_cache* kv, int64_t
                       void* out, int64_t ldo, int64_t B, int64_t T, int64_t nh, int64_t nkv, int64_t hd, float scale,
                       int impl, int dtype, void* stream);
 
+/* Decode attention: one new query per batch row (positions[r] its position), split over the keys ("flash decoding")
+ * so that every K/V row is read once for all query heads of its KV head. Same semantics as fs_attention with T = 1
+ * (model.py:69-76 on the decode step of the Engine, engine.py:125). head_dim 64 or 128, n_heads / n_kv_heads <= 8.
+ * workspace: device memory of at least fs_attention_decode_workspace(...) bytes (0 bytes when one split suffices),
+ * owned by the caller, not read before being written; calls that overlap on the GPU need separate workspaces. */
+int64_t fs_attention_decode_workspace(int64_t B, int64_t nh, int64_t nkv, int64_t hd, int64_t n_slots);
+int fs_attention_decode(const void* q, int64_t ldq, const fs_kv_cache* kv, int64_t n_slots, const int64_t* positions,
+                        void* out, int64_t ldo, int64_t B, int64_t nh, int64_t nkv, int64_t hd, float scale,
+                        void* workspace, int64_t workspace_bytes, int dtype, void* stream);
+
 /* Token embedding gather out[i] = table[ids[i]] (nn.Embedding at pipeline.py:106 / model.py:134-135). */
 int fs_embed(const int64_t* ids, int64_t n, const void* table, int64_t vocab, int64_t dim, void* out, int dtype,
              void* stream);

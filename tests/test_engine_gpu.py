@@ -75,3 +75,52 @@ def test_engine_bf16_matches_own_generate():
         want = generate(m, torch.tensor([p]), 12)[0, len(p):].tolist()
         agree = sum(a == b for a, b in zip(out[rid], want))
         assert agree >= 10, (out[rid], want)       # bf16: paged/batched and contiguous paths may flip a near-tie
+
+
+def pipeline_engine_worker(rank, size, cfg_dict, full_sd, requests, num_blocks, max_batch, microbatches, dtype):
+    from forgeserve_b200 import PipelineEngine, PipelineStage
+    cfg = ModelConfig(**cfg_dict)
+    stage = PipelineStage(cfg, rank, size)
+    stage.load_from_full(full_sd)
+    stage = stage.to(dtype).eval()
+    eng = PipelineEngine(stage, num_blocks=num_blocks, block_size=4 if cfg.head_dim < 64 else 16,
+                         max_batch=max_batch, microbatches=microbatches)
+    ids = [eng.add_request(p, n) for p, n in requests]
+    out = eng.run()
+    return [out[i] for i in ids], eng.steps, eng.preemptions, eng.pool.allocator.num_free
+
+
+@pytest.mark.parametrize("size,microbatches", [(2, 1), (3, 2)])
+@pytest.mark.parametrize("key,num_blocks,max_batch", [("engine", 64, 3), ("engine_preempt", 12, 5)])
+def test_pipeline_engine_equals_reference_engine(setup, size, microbatches, key, num_blocks, max_batch):
+    """Continuous batching through pipeline stages reproduces the reference engine (outputs, steps, preemptions)."""
+    from forgeserve_b200.tensor_parallel import run_in_threads
+    g, _ = setup
+    sd = O.test_model_weights(O.Cfg(**g["cfg"]), *g["weights"][1:])
+    e = g[key]
+    res = run_in_threads(pipeline_engine_worker, size, g["cfg"], sd, e["requests"], num_blocks, max_batch,
+                         microbatches, torch.float32)
+    for outputs, steps, preemptions, free in res:          # every stage ends in the same state
+        assert outputs == e["outputs"]
+        assert steps == e["steps"] and preemptions == e["preemptions"] and free == num_blocks
+
+
+def test_pipeline_engine_bf16_decode_kernel_matches_single_engine():
+    """head_dim 128 in bf16: decode steps run the split-KV decode kernel on every stage."""
+    from forgeserve_b200.tensor_parallel import run_in_threads
+    cfg = ModelConfig(vocab_size=512, d_model=512, n_layers=4, n_heads=4, n_kv_heads=2, max_seq_len=512)
+    sd = O.test_model_weights(O.Cfg(**cfg.to_dict()), seed=11, scale=0.05)
+    gen = torch.Generator().manual_seed(4)
+    requests = [(torch.randint(0, 512, (n,), generator=gen).tolist(), 20) for n in (9, 130, 40, 75)]
+    m = ForgeModel(cfg, device="cuda")
+    m.load_state_dict(sd)
+    m = m.to(torch.bfloat16).eval()
+    single = Engine(m, num_blocks=64, block_size=16, max_batch=4)
+    ids = [single.add_request(p, n) for p, n in requests]
+    want = single.run()
+    res = run_in_threads(pipeline_engine_worker, 2, cfg.to_dict(), sd, requests, 64, 4, 2, torch.bfloat16)
+    for outputs, steps, _, _ in res:
+        for rid, got in zip(ids, outputs):
+            agree = sum(a == b for a, b in zip(got, want[rid]))
+            assert agree >= 18, (got, want[rid])          # bf16: micro-batched rows may flip a near-tie
+        assert steps == single.steps

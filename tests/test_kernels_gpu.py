@@ -390,3 +390,65 @@ def test_gemm_pair_kernel_matches_single_cta_kernel(epi, M, N, K):
     bf16_close(pair, single.float(), rel=2 ** -8)
     if epi == L.FS_EPI_STORE:
         bf16_close(pair, a.double() @ w.double().t())
+
+
+# ------------------------------------------------------------------------------------- decode attention
+@pytest.mark.parametrize("dtype,hd,nh,nkv,lengths", [
+    (torch.bfloat16, 128, 32, 8, [3000, 17, 700, 1]),        # long rows: several splits
+    (torch.bfloat16, 128, 32, 8, [200] * 64),                # a full decode batch: one split
+    (torch.bfloat16, 64, 8, 8, [513, 64, 65]),               # no GQA sharing
+    (torch.bfloat16, 128, 8, 1, [1000]),                     # one KV head for 8 query heads
+    (torch.float32, 128, 16, 4, [333, 2048, 5]),
+])
+def test_attention_decode_paged(dtype, hd, nh, nkv, lengths):
+    """One query per row at its own position, over scattered 16-slot blocks (padded tables), against fp64 SDPA."""
+    bs = 16
+    B = len(lengths)
+    widths = [-(-(n + 1) // bs) for n in lengths]
+    nblk = sum(widths) + 3
+    blocks = list(range(nblk))
+    random.Random(2).shuffle(blocks)
+    it = iter(blocks)
+    W = max(widths)
+    table = torch.tensor([[next(it) for _ in range(w)] + [0] * (W - w) for w in widths], device=DEV)
+    pool_k = torch.randn(nblk, nkv, bs, hd, device=DEV).to(dtype)
+    pool_v = torch.randn(nblk, nkv, bs, hd, device=DEV).to(dtype)
+    positions = torch.tensor([[n] for n in lengths], device=DEV)
+    q = torch.randn(B, nh * hd, device=DEV).to(dtype)
+    out = torch.empty_like(q)
+    ops.attention_decode(q, ops.paged_desc(pool_k, pool_v, table), W * bs, positions, out, B, nh, nkv, hd)
+    k_all = pool_k[table].permute(0, 2, 1, 3, 4).reshape(B, nkv, -1, hd)
+    v_all = pool_v[table].permute(0, 2, 1, 3, 4).reshape(B, nkv, -1, hd)
+    want = attention_ref(q.view(B, 1, nh, hd).transpose(1, 2), k_all, v_all, positions, nh // nkv)
+    got = out.view(B, 1, nh, hd).transpose(1, 2).double()
+    tol = 1e-5 if dtype == torch.float32 else 2e-2
+    assert (got - want).abs().max().item() < tol
+
+
+def test_attention_decode_contiguous_matches_generic():
+    """Contiguous cache (one block per row), the decode kernel against the CUDA-core kernel."""
+    B, nh, nkv, hd, S = 3, 32, 8, 128, 1500
+    k = torch.randn(B, nkv, 1504, hd, device=DEV).bfloat16()
+    v = torch.randn(B, nkv, 1504, hd, device=DEV).bfloat16()
+    q = torch.randn(B, nh * hd, device=DEV).bfloat16()
+    positions = torch.tensor([[S - 1], [10], [700]], device=DEV)
+    desc = ops.contiguous_desc(k, v, torch.arange(B, device=DEV))
+    a, b = torch.empty_like(q), torch.empty_like(q)
+    ops.attention_decode(q, desc, S, positions, a, B, nh, nkv, hd)
+    ops.attention(q, desc, S, positions, b, B, 1, nh, nkv, hd, impl=L.FS_ATTN_CUDA_CORE)
+    assert (a.float() - b.float()).abs().max().item() < 2e-2
+
+
+def test_attention_decode_refuses_a_small_workspace():
+    B, nh, nkv, hd = 1, 32, 8, 128
+    k = torch.zeros(1, nkv, 4096, hd, device=DEV).bfloat16()
+    q = torch.zeros(B, nh * hd, device=DEV).bfloat16()
+    desc = ops.contiguous_desc(k, k, torch.arange(1, device=DEV))
+    need = L.load().fs_attention_decode_workspace(B, nh, nkv, hd, 4096)
+    assert need > 0
+    import ctypes
+    rc = L.load().fs_attention_decode(ctypes.c_void_p(q.data_ptr()), nh * hd, ctypes.byref(desc), 4096,
+                                      ctypes.c_void_p(torch.zeros(1, 1, dtype=torch.int64, device=DEV).data_ptr()),
+                                      ctypes.c_void_p(q.data_ptr()), nh * hd, B, nh, nkv, hd, 0.1, None, 0, L.FS_BF16,
+                                      None)
+    assert rc != 0 and b"workspace" in L.load().fs_last_error()
