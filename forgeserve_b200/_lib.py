@@ -58,6 +58,8 @@ SIGNATURES = {
     "fs_attention_decode_workspace": (c_i64, [c_i64, c_i64, c_i64, c_i64, c_i64]),
     "fs_attention_decode": (c_int, [c_vp, c_i64, ctypes.POINTER(KVCacheDesc), c_i64, c_vp, c_vp, c_i64, c_i64, c_i64,
                                     c_i64, c_i64, c_float, c_vp, c_i64, c_int, c_vp]),
+    "fs_attention_decode_static": (c_int, [c_vp, c_i64, ctypes.POINTER(KVCacheDesc), c_i64, c_vp, c_vp, c_i64, c_i64,
+                                           c_i64, c_i64, c_i64, c_float, c_int, c_vp]),
     "fs_embed": (c_int, [c_vp, c_i64, c_vp, c_i64, c_i64, c_vp, c_int, c_vp]),
     "fs_argmax": (c_int, [c_vp, c_i64, c_i64, c_i64, c_vp, c_int, c_vp]),
 }

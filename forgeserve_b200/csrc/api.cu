@@ -47,8 +47,17 @@ static int check_kv(const fs_kv_cache* c) {
 
 static bool dtype_ok(int dtype) { return dtype == F32 || dtype == BF16; }
 
+static unsigned* g_error_words[64] = {nullptr};
+
+// The device's error word if it has been created already (no allocation); nullptr otherwise.
+unsigned* error_word_if_present() {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
+  return g_error_words[dev];
+}
+
 unsigned* error_word() {
-  static unsigned* words[64] = {nullptr};
+  unsigned** words = g_error_words;
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) {
     fail("error_word: no current CUDA device");

@@ -14,6 +14,9 @@
 //   attn_combine_kernel  grid (B, nh): merges the splits (log-sum-exp weights) into the output.
 //
 // Workspace (fp32): O partials [B][nh][splits][hd], then (max, sum) pairs [B][nh][splits][2].
+#include <string>
+
+#include "../../include/forgeserve_b200.h"
 #include "common.cuh"
 #include "kernels.h"
 
@@ -263,3 +266,135 @@ int launch(int dtype, const void* q, int64_t ldq, const KVCache& kv, int64_t n_s
 
 }  // namespace decode
 }  // namespace fs
+
+// =============================================================================================================
+// Decode attention without any device allocation.
+//
+// Some callers cannot allocate device memory at the point where they run a decode step: a host framework that
+// has reserved all of the GPU's memory in its own pool up front (and fails any other cudaMalloc), a plugin that
+// is only handed device pointers by its host, or a serving loop that cannot afford the device-wide
+// synchronisation a cudaMalloc / cudaFree may cause in the middle of a step. fs_attention_decode needs a
+// workspace for its per-split partial results; this entry point uses a fixed scratch area that is part of the
+// library image instead: a file-scope __device__ array of kStaticScratchBytes (4 MiB), which every GPU that
+// loads the library holds until the process exits.
+//
+// * Set-up: the first call on a device resolves the array's device address with cudaGetSymbolAddress (and sets
+//   the kernels' shared-memory attribute) with that device current; make that first call before any stream
+//   capture on that device.
+// * Limit: calls whose split partials need more than kStaticScratchBytes are refused with an error naming the
+//   size (fs_attention_decode_workspace() gives the size a call needs).
+// * Sharing: every call uses the same array and leaves its contents behind; each call writes every partial it
+//   reads, so nothing needs clearing, but calls that overlap on the GPU (different streams, no ordering) race on
+//   the array and must not be issued.
+// * It allocates nothing: no cudaMalloc, cudaFree or allocating library routine. Device-side input errors (a block
+//   table entry outside the pool) are recorded in the library's error word only if that word already exists on
+//   the device (any other entry point creates it); the kernel never reads outside the cache either way.
+// =============================================================================================================
+namespace fs {
+namespace decode {
+
+constexpr int64_t kStaticScratchBytes = int64_t(4) << 20;
+static __device__ __align__(256) unsigned char g_static_scratch[kStaticScratchBytes];
+
+struct StaticScratch {
+  float* ptr = nullptr;
+  bool ready = false;
+};
+
+static int static_scratch(float** out) {
+  static StaticScratch per_dev[64];
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return fail("no current CUDA device");
+  StaticScratch& s = per_dev[dev];
+  if (!s.ready) {
+    void* p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&p, g_static_scratch);
+    if (e != cudaSuccess) return fail(std::string("cudaGetSymbolAddress(decode scratch): ") + cudaGetErrorString(e));
+    using S128 = Smem<float, 128>;
+    using S64 = Smem<float, 64>;
+    if (cudaFuncSetAttribute(attn_decode_kernel<float, 128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             S128::BYTES) != cudaSuccess ||
+        cudaFuncSetAttribute(attn_decode_kernel<float, 64>, cudaFuncAttributeMaxDynamicSharedMemorySize, S64::BYTES) !=
+            cudaSuccess ||
+        cudaFuncSetAttribute(attn_decode_kernel<__nv_bfloat16, 128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             Smem<__nv_bfloat16, 128>::BYTES) != cudaSuccess ||
+        cudaFuncSetAttribute(attn_decode_kernel<__nv_bfloat16, 64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             Smem<__nv_bfloat16, 64>::BYTES) != cudaSuccess)
+      return check_launch("decode scratch set-up");
+    s.ptr = static_cast<float*>(p);
+    s.ready = true;
+  }
+  *out = s.ptr;
+  return 0;
+}
+
+template <typename T, int HD>
+static int launch_static_t(const void* q, int64_t ldq, const KVCache& kv, int64_t n_slots, const int64_t* positions,
+                           void* out, int64_t ldo, int64_t B, int64_t nh, int64_t nkv, float scale, int splits,
+                           float* ws, unsigned* err, cudaStream_t st) {
+  using S = Smem<T, HD>;
+  dim3 grid(static_cast<unsigned>(splits), static_cast<unsigned>(nkv), static_cast<unsigned>(B));
+  attn_decode_kernel<T, HD><<<grid, THREADS, S::BYTES, st>>>(
+      static_cast<const T*>(q), ldq, kv, n_slots, positions, static_cast<T*>(out), ldo, static_cast<int>(nh),
+      static_cast<int>(nh / nkv), splits, scale, ws, err);
+  if (check_launch("attn_decode_kernel")) return -1;
+  if (splits > 1) {
+    attn_combine_kernel<T, HD><<<dim3(static_cast<unsigned>(B), static_cast<unsigned>(nh)), THREADS, 0, st>>>(
+        ws, static_cast<int>(B), static_cast<int>(nh), splits, static_cast<T*>(out), ldo);
+    return check_launch("attn_combine_kernel");
+  }
+  return 0;
+}
+
+}  // namespace decode
+unsigned* error_word_if_present();
+}  // namespace fs
+
+extern "C" int fs_attention_decode_static(const void* q, int64_t ldq, const fs_kv_cache* kvd, int64_t n_slots,
+                                          const int64_t* positions, void* out, int64_t ldo, int64_t B, int64_t nh,
+                                          int64_t nkv, int64_t hd, float scale, int dtype, void* stream) {
+  using namespace fs;
+  using namespace fs::decode;
+  if (B <= 0) return 0;
+  if (!kvd || !kvd->k || !kvd->v || !kvd->table) return fail("fs_attention_decode_static: NULL cache pointer");
+  if (kvd->block_size <= 0 || kvd->num_blocks <= 0 || kvd->table_cols <= 0)
+    return fail("fs_attention_decode_static: empty cache");
+  KVCache cache;
+  cache.k = kvd->k;
+  cache.v = kvd->v;
+  cache.table = kvd->table;
+  cache.table_stride = kvd->table_stride;
+  cache.table_cols = kvd->table_cols;
+  cache.block_size = kvd->block_size;
+  cache.block_stride = kvd->block_stride;
+  cache.head_stride = kvd->head_stride;
+  cache.num_blocks = kvd->num_blocks;
+  const KVCache* kv = &cache;
+  if (!q || !positions || !out) return fail("fs_attention_decode_static: NULL pointer");
+  if (n_slots <= 0) return fail("fs_attention_decode_static: the cache view has no slots");
+  if (dtype != F32 && dtype != BF16) return fail("fs_attention_decode_static: unsupported dtype");
+  if (ldq < nh * hd || ldo < nh * hd) return fail("fs_attention_decode_static: row stride too small");
+  if (B > 65535 || nkv > 65535) return fail("fs_attention_decode_static: grid too large");
+  if (!supported(dtype, hd, nh, nkv, q, ldq, *kv))
+    return fail("fs_attention_decode_static: needs head_dim 64 or 128, n_heads / n_kv_heads <= 8, aligned rows");
+  int sms = 0, dev = 0;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const int splits = choose_splits(B, nkv, n_slots, 2 * (sms > 0 ? sms : 148));
+  const int64_t need = workspace_bytes(B, nh, hd, splits);
+  if (need > kStaticScratchBytes)
+    return fail("fs_attention_decode_static: this call needs " + std::to_string(need) +
+                " bytes of scratch, more than the fixed " + std::to_string(kStaticScratchBytes) +
+                " bytes; use fs_attention_decode with a caller-owned workspace");
+  float* ws = nullptr;
+  if (static_scratch(&ws)) return -1;
+  unsigned* err = error_word_if_present();
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (dtype == BF16 && hd == 128)
+    return launch_static_t<__nv_bfloat16, 128>(q, ldq, *kv, n_slots, positions, out, ldo, B, nh, nkv, scale, splits, ws, err, st);
+  if (dtype == BF16)
+    return launch_static_t<__nv_bfloat16, 64>(q, ldq, *kv, n_slots, positions, out, ldo, B, nh, nkv, scale, splits, ws, err, st);
+  if (hd == 128)
+    return launch_static_t<float, 128>(q, ldq, *kv, n_slots, positions, out, ldo, B, nh, nkv, scale, splits, ws, err, st);
+  return launch_static_t<float, 64>(q, ldq, *kv, n_slots, positions, out, ldo, B, nh, nkv, scale, splits, ws, err, st);
+}

@@ -124,6 +124,18 @@ int fs_attention_decode(const void* q, int64_t ldq, const fs_kv_cache* kv, int64
                         void* out, int64_t ldo, int64_t B, int64_t nh, int64_t nkv, int64_t hd, float scale,
                         void* workspace, int64_t workspace_bytes, int dtype, void* stream);
 
+/* fs_attention_decode for callers that cannot allocate device memory where they run a decode step (a host that
+ * owns all device memory through its own pool, a plugin that is only handed device pointers, a loop that cannot
+ * take the synchronisation of a cudaMalloc mid-step): the split partials go to a fixed 4 MiB scratch array that is
+ * part of the library image (held on every GPU that loads the library until exit) instead of a caller workspace.
+ * Allocates nothing. The first call on a device looks up that array's address (make it before any stream capture
+ * on the device). Calls needing more scratch than 4 MiB (see fs_attention_decode_workspace) are refused with an
+ * error. All calls share the array, so calls that overlap on the GPU race and must not be issued.
+ * No counterpart in the reference (it has no kernels or device memory). */
+int fs_attention_decode_static(const void* q, int64_t ldq, const fs_kv_cache* kv, int64_t n_slots,
+                               const int64_t* positions, void* out, int64_t ldo, int64_t B, int64_t nh, int64_t nkv,
+                               int64_t hd, float scale, int dtype, void* stream);
+
 /* Token embedding gather out[i] = table[ids[i]] (nn.Embedding at pipeline.py:106 / model.py:134-135). */
 int fs_embed(const int64_t* ids, int64_t n, const void* table, int64_t vocab, int64_t dim, void* out, int dtype,
              void* stream);
