@@ -306,7 +306,7 @@ def run_reference(args):
             "wall_s": round(wall, 1)}
 
 
-def profile_case(name: str, reps: int):
+def profile_case(name: str, reps: int, timed: bool = False):
     """A few launches of one kernel on a small case (inputs larger than L2, a few GB at most) for ncu captures."""
     from forgeserve_b200 import _lib as L
     from forgeserve_b200 import ops
@@ -321,16 +321,20 @@ def profile_case(name: str, reps: int):
     if name == "gemm_gateup":          # one micro-batch's gate/up projection: M 8192, N 2 x 14336, K 4096
         a, w = rnd(M, d), rnd(2 * F, d, scale=0.02)
         fn = lambda: ops.linear(a, w, L.FS_EPI_SWIGLU)
+        work = (2.0 * M * 2 * F * d, "FLOP")
     elif name == "gemm_qkv":
         a, w = rnd(M, d), rnd((nh + 2 * nkv) * hd, d, scale=0.02)
         fn = lambda: ops.linear(a, w)
+        work = (2.0 * M * w.shape[0] * d, "FLOP")
     elif name == "gemm_down":
         a, w, x = rnd(M, F), rnd(d, F, scale=0.02), rnd(M, d)
         fn = lambda: ops.linear(a, w, L.FS_EPI_RESIDUAL, residual=x, out=x)
+        work = (2.0 * M * d * F, "FLOP")
     elif name == "gemm_head":
         a, w = rnd(M, d), rnd(V, d, scale=0.02)
         out = torch.empty(M, V, device=dev, dtype=torch.bfloat16)
         fn = lambda: ops.linear(a, w, out=out)
+        work = (2.0 * M * V * d, "FLOP")
     elif name == "attention":          # one micro-batch's causal prefill attention: 4 x 2048 queries, 32/8 heads
         kc, vc = rnd(MB_ROWS, nkv, SEQ, hd), rnd(MB_ROWS, nkv, SEQ, hd)
         q = rnd(M, (nh + 2 * nkv) * hd)
@@ -339,6 +343,7 @@ def profile_case(name: str, reps: int):
         table = torch.arange(MB_ROWS, device=dev)
         desc = ops.contiguous_desc(kc, vc, table)
         fn = lambda: ops.attention(q[:, : nh * hd], desc, SEQ, pos, out, MB_ROWS, SEQ, nh, nkv, hd)
+        work = (4.0 * MB_ROWS * nh * hd * SEQ * (SEQ + 1) / 2, "FLOP")
     elif name == "rope_kv":
         kc, vc = rnd(MB_ROWS, nkv, SEQ, hd), rnd(MB_ROWS, nkv, SEQ, hd)
         q = rnd(M, (nh + 2 * nkv) * hd)
@@ -347,15 +352,60 @@ def profile_case(name: str, reps: int):
         cos, sin = (t.to(dev) for t in precompute_rope(hd, CFG["max_seq_len"], CFG["rope_theta"]))
         desc = ops.contiguous_desc(kc, vc, torch.arange(MB_ROWS, device=dev))
         fn = lambda: ops.rope_kv_write(q, cos, sin, pos, desc, MB_ROWS, SEQ, nh, nkv, hd, 0, False)
+        work = (2.0 * M * (nh + 2 * nkv) * hd * 2, "B")     # q rotated in place; k, v read and stored
     elif name == "rmsnorm":
         x, w = rnd(M, d), rnd(d)
         fn = lambda: ops.rmsnorm(x, w, 1e-5)
+        work = (2.0 * M * d * 2, "B")
+    elif name == "decode":             # one layer's decode attention of the C4 batch: 64 rows, paged bs 16
+        import random
+        rng = random.Random(0)
+        bs, rows = 16, 64
+        lengths = [rng.randint(512, 4096) + 128 for _ in range(rows)]       # mid-generation context lengths
+        widths = [-(-(n + 1) // bs) for n in lengths]
+        nblk = sum(widths) + 64
+        blocks = list(range(nblk))
+        rng.shuffle(blocks)
+        it = iter(blocks)
+        W = max(widths)
+        table = torch.tensor([[next(it) for _ in range(w)] + [0] * (W - w) for w in widths], device=dev)
+        pool_k, pool_v = rnd(nblk, nkv, bs, hd), rnd(nblk, nkv, bs, hd)
+        q = rnd(rows, nh * hd)
+        out = torch.empty_like(q)
+        positions = torch.tensor([[n] for n in lengths], device=dev)
+        desc = ops.paged_desc(pool_k, pool_v, table)
+        kv_bytes = sum(n + 1 for n in lengths) * nkv * hd * 2 * 2
+        print(json.dumps({"decode_kv_bytes": kv_bytes, "keys": sum(n + 1 for n in lengths),
+                          "splits_workspace": L.load().fs_attention_decode_workspace(rows, nh, nkv, hd, W * bs)}))
+        fn = lambda: ops.attention_decode(q, desc, W * bs, positions, out, rows, nh, nkv, hd)
+        work = (kv_bytes + 2.0 * rows * nh * hd * 2, "B")  # K and V of every key, q in, o out
     else:
         raise SystemExit(f"unknown profile case {name}")
     for _ in range(reps):
         fn()
     torch.cuda.synchronize()
-    print(json.dumps({"profile_case": name, "reps": reps, "device_error": L.device_error()}))
+    res = {"profile_case": name, "reps": reps}
+    if timed:
+        # cold-L2 launches timed with CUDA events on the launching stream (a 256 MB write between launches)
+        flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+        st = torch.cuda.current_stream(dev)
+        times = []
+        for _ in range(max(reps, 3) * 4):
+            flush.zero_()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(st)
+            fn()
+            e1.record(st)
+            e1.synchronize()
+            times.append(e0.elapsed_time(e1) * 1e3)
+        us = statistics.median(times)
+        amount, unit = work
+        res.update({"us_median": round(us, 2), "us_min": round(min(times), 2),
+                    ("TFLOP/s" if unit == "FLOP" else "GB/s"):
+                        round(amount / (us * 1e-6) / (1e12 if unit == "FLOP" else 1e9), 1),
+                    "work_per_launch": amount, "work_unit": unit})
+    res["device_error"] = L.device_error()
+    print(json.dumps(res))
 
 
 def main():
@@ -367,9 +417,10 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--profile-case", default=None, help="run a few launches of one kernel (for ncu) and exit")
     ap.add_argument("--reps", type=int, default=3)
+    ap.add_argument("--timed", action="store_true", help="with --profile-case: also time cold-L2 launches")
     args = ap.parse_args()
     if args.profile_case:
-        profile_case(args.profile_case, args.reps)
+        profile_case(args.profile_case, args.reps, args.timed)
         return
     if args.warmup < 3 and args.impl == "ours":
         print("warning: fewer than 3 warm-up steps", file=sys.stderr)

@@ -197,18 +197,18 @@ int fs_attention_impl(const void* q, int64_t ldq, const fs_kv_cache* kv, int64_t
   return attention_common(impl, q, ldq, kv, n_slots, positions, out, ldo, B, T, nh, nkv, hd, scale, dtype, stream);
 }
 
-static int decode_sm_target() {
+static int decode_sms() {
   static int n[64] = {0};
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev < 0 || dev >= 64) dev = 0;
   if (!n[dev]) cudaDeviceGetAttribute(&n[dev], cudaDevAttrMultiProcessorCount, dev);
-  return 2 * (n[dev] > 0 ? n[dev] : 148);
+  return n[dev] > 0 ? n[dev] : 148;
 }
 
 int64_t fs_attention_decode_workspace(int64_t B, int64_t nh, int64_t nkv, int64_t hd, int64_t n_slots) {
   if (B <= 0 || nh <= 0 || nkv <= 0 || hd <= 0 || n_slots <= 0) return 0;
-  return decode::workspace_bytes(B, nh, hd, decode::choose_splits(B, nkv, n_slots, decode_sm_target()));
+  return decode::workspace_bytes(B, nh, hd, decode::choose_splits(B, nkv, n_slots, decode_sms()));
 }
 
 int fs_attention_decode(const void* q, int64_t ldq, const fs_kv_cache* kv, int64_t n_slots, const int64_t* positions,
@@ -223,12 +223,14 @@ int fs_attention_decode(const void* q, int64_t ldq, const fs_kv_cache* kv, int64
   const KVCache c = to_internal(kv);
   if (!decode::supported(dtype, hd, nh, nkv, q, ldq, c))
     return fail("fs_attention_decode: needs head_dim 64 or 128, n_heads / n_kv_heads <= 8 and 16-byte aligned rows");
-  const int splits = decode::choose_splits(B, nkv, n_slots, decode_sm_target());
+  const int splits = decode::choose_splits(B, nkv, n_slots, decode_sms());
   const int64_t need = decode::workspace_bytes(B, nh, hd, splits);
   if (need > 0 && (!workspace || workspace_bytes < need))
     return fail("fs_attention_decode: workspace of " + std::to_string(need) + " bytes needed");
+  unsigned* err = error_word();
+  if (!err) return -1;
   return decode::launch(dtype, q, ldq, c, n_slots, positions, out, ldo, B, nh, nkv, hd, scale, splits,
-                        static_cast<float*>(workspace), static_cast<cudaStream_t>(stream));
+                        static_cast<float*>(workspace), err, static_cast<cudaStream_t>(stream));
 }
 
 int fs_embed(const int64_t* ids, int64_t n, const void* table, int64_t vocab, int64_t dim, void* out, int dtype,

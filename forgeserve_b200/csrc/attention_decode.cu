@@ -2,18 +2,26 @@
 //
 // Same semantics as attention.cu (forgeserve/model.py:69-76): query head h reads KV head h / rep, key slot s is
 // visible iff s <= position and s < n_slots, scale 1/sqrt(hd). This is the step the reference's Engine runs for
-// every running request (forgeserve/engine.py:125, paged gather at forgeserve/paged.py:80-81). It is HBM-bound,
-// so each CTA reads every K/V row of its key range exactly once, for all `rep` query heads of its KV head:
+// every running request (forgeserve/engine.py:125, paged gather at forgeserve/paged.py:80-81). It is HBM-bound:
+// every K/V row of the visible context is read once, for all `rep` query heads of its KV head, and the kernels
+// are built to keep enough bytes in flight to stream at HBM speed.
 //
-//   attn_decode_kernel   grid (splits, n_kv, B), 128 threads. Per 64-key chunk: K and V rows fetched with
-//                        cp.async through the block table into row-padded shared memory (conflict-free 16-byte
-//                        reads); scores of the rep heads (fp32 FMA); online softmax statistics per head (one warp
-//                        per head, kept in shared memory); P V accumulated per output dimension. With one split the
-//                        normalised output is written directly; otherwise the split's unnormalised O and its
-//                        (max, sum) go to the workspace.
-//   attn_combine_kernel  grid (B, nh): merges the splits (log-sum-exp weights) into the output.
+//   attn_decode_tc_kernel  (bf16, block size a multiple of 16) grid (splits, n_kv, B), 4 warps. A split's keys go
+//                          in 16-key tiles (one paged block at block size 16) to the warps in turn; each warp owns
+//                          a 3-stage ring of TMA tile loads (128-byte swizzle, K and V of one tile = 8 KB at hd
+//                          128) and keeps its own online-softmax state, so the main loop has no block barrier.
+//                          Scores S^T = K Q^T and the output O^T = V^T P^T are mma.sync m16n8k16 products with the
+//                          <= 8 query heads of the KV head as the N = 8 side (keys / head dims are the M side);
+//                          P^T reaches the B-operand layout through movmatrix. The warps' partial results are
+//                          merged through shared memory at the end.
+//   attn_decode_kernel     CUDA-core fallback (fp32, or layouts the tile loads cannot address): grid as above,
+//                          128 threads, 64-key chunks fetched with cp.async into row-padded shared memory.
+//   attn_combine_kernel    grid (B, nh): merges the splits (log-sum-exp weights) into the output.
 //
-// Workspace (fp32): O partials [B][nh][splits][hd], then (max, sum) pairs [B][nh][splits][2].
+// Splits: a split covers a fixed number of key slots (chosen from the batch size, n_slots and the SM count so
+// that there are several CTAs per SM), so CTAs carry similar work whatever the spread of context lengths; splits
+// past a row's context end at once. Workspace (fp32): O partials [B][nh][splits][hd], then (max, sum) pairs
+// [B][nh][splits][2] (natural-log domain).
 #include <string>
 
 #include "../../include/forgeserve_b200.h"
@@ -198,9 +206,345 @@ __global__ void __launch_bounds__(THREADS)
   if (d < HD) out[static_cast<int64_t>(r) * ldo + static_cast<int64_t>(h) * HD + d] = from_f<T>(L > 0.f ? o / L : 0.f);
 }
 
+// ------------------------------------------------------------------------------ tensor-core tile kernel
+namespace tcd {
+
+constexpr int TILE = 16, WARPS = 4, THREADS_TC = 32 * WARPS, STAGES = 3, BOX_BYTES = TILE * 128;
+
+template <int HD>
+struct Geo {
+  static constexpr int NB = HD / 64;                       // 128-byte column boxes per K (or V) row
+  static constexpr int KV_BYTES = NB * BOX_BYTES;          // K (or V) of one 16-key tile
+  static constexpr int STAGE_BYTES = 2 * KV_BYTES;
+  static constexpr int RING_BYTES = WARPS * STAGES * STAGE_BYTES;
+  static constexpr int BAR_OFF = RING_BYTES;
+  static constexpr int STAT_OFF = BAR_OFF + WARPS * STAGES * 8;   // m and l: [WARPS][8] floats each
+  static constexpr int SMEM = STAT_OFF + 2 * WARPS * 8 * 4 + 1024;  // + slack for the 1024-byte alignment
+  static_assert(WARPS * 8 * HD * 4 <= RING_BYTES, "the warp-merge area must fit in the rings");
+};
+
+struct Params {
+  const __nv_bfloat16* q;
+  int64_t ldq;
+  const int64_t* table;
+  int64_t table_stride, table_cols, block_size, rows_per_block, rows_per_head, num_blocks, kv_rows;
+  int64_t n_slots;
+  const int64_t* positions;
+  __nv_bfloat16* out;
+  int64_t ldo;
+  int nh, rep, splits, per;
+  float scale_log2;
+  float* ws;
+  unsigned* err;
+};
+
+__device__ __forceinline__ void ldsm_x4(uint32_t (&r)[4], uint32_t addr) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(addr));
+}
+__device__ __forceinline__ void ldsm_x4_trans(uint32_t (&r)[4], uint32_t addr) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(addr));
+}
+// c (16 x 8, fp32) += a (16 x 16, bf16, row-major) * b (16 x 8, bf16, column-major)
+__device__ __forceinline__ void mma16816(float (&c)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};"
+      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ uint32_t movmatrix_trans(uint32_t x) {
+  uint32_t y;
+  asm volatile("movmatrix.sync.aligned.m8n8.trans.b16 %0, %1;" : "=r"(y) : "r"(x));
+  return y;
+}
+__device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
+  uint32_t d;
+  asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(d) : "f"(hi), "f"(lo));
+  return d;
+}
+__device__ __forceinline__ void st_shared_zero16(uint32_t addr) {
+  asm volatile("st.shared.v4.u32 [%0], {%1, %1, %1, %1};" ::"r"(addr), "r"(0u) : "memory");
+}
+// Orders this thread's earlier shared-memory accesses before later async-proxy (TMA) writes to the same bytes.
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+// Byte address of 16-byte chunk `chunk` (8 bf16 of the row) of tile row `row` in a 128-byte-swizzled box pair.
+__device__ __forceinline__ uint32_t tile_addr(uint32_t base, int row, int chunk) {
+  return base + static_cast<uint32_t>((chunk >> 3) * BOX_BYTES + row * 128 + (((chunk & 7) ^ (row & 7)) << 4));
+}
+
+template <int HD>
+__global__ void __launch_bounds__(THREADS_TC)
+    attn_decode_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV, Params p) {
+  using G = Geo<HD>;
+  extern __shared__ uint8_t smem_raw[];
+  __shared__ int abort_flag;
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + G::BAR_OFF);
+  float* sm_m = reinterpret_cast<float*>(smem + G::STAT_OFF);
+  float* sm_l = sm_m + WARPS * 8;
+
+  const int split = blockIdx.x, g = blockIdx.y, r = blockIdx.z;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  int64_t pos = p.positions[r];
+  if (pos < 0) pos = 0;
+  const int64_t n_vis = pos + 1 < p.n_slots ? pos + 1 : p.n_slots;
+  const int64_t k_begin = static_cast<int64_t>(split) * p.per;
+  const int64_t k_end = k_begin + p.per < n_vis ? k_begin + p.per : n_vis;
+  const int n_tiles = k_end > k_begin ? static_cast<int>((k_end - k_begin + TILE - 1) / TILE) : 0;
+  const int my_n = n_tiles > warp ? (n_tiles - warp + WARPS - 1) / WARPS : 0;   // tiles warp, warp+4, ...
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < WARPS * STAGES; ++i) mbar_init(&full[i], 1);
+    abort_flag = 0;
+    fence_barrier_init();
+    prefetch_tmap(&tmK);
+    prefetch_tmap(&tmV);
+  }
+  __syncthreads();
+
+  uint8_t* ring = smem + warp * STAGES * G::STAGE_BYTES;
+  uint64_t* wfull = full + warp * STAGES;
+  // Lane 0 of the warp fetches the warp's j-th tile (keys k0 .. k0+15, all in one cache block) into stage j % STAGES.
+  auto issue = [&](int j) {
+    const int64_t k0 = k_begin + static_cast<int64_t>(warp + WARPS * j) * TILE;
+    const int64_t bi = k0 / p.block_size;
+    const int64_t blk = bi < p.table_cols ? p.table[static_cast<int64_t>(r) * p.table_stride + bi] : -1;
+    int64_t row;
+    if (blk < 0 || blk >= p.num_blocks) {
+      flag_error(p.err, ERR_BAD_SLOT);
+      row = p.kv_rows;   // a box wholly outside the tensor: TMA fills it with zeros
+    } else {
+      row = blk * p.rows_per_block + static_cast<int64_t>(g) * p.rows_per_head + k0 % p.block_size;
+    }
+    uint8_t* st = ring + (j % STAGES) * G::STAGE_BYTES;
+    uint64_t* bar = &wfull[j % STAGES];
+    mbar_arrive_expect_tx(bar, G::STAGE_BYTES);
+#pragma unroll
+    for (int b = 0; b < G::NB; ++b) {
+      tma_load_2d(st + b * BOX_BYTES, &tmK, bar, 64 * b, static_cast<int>(row));
+      tma_load_2d(st + G::KV_BYTES + b * BOX_BYTES, &tmV, bar, 64 * b, static_cast<int>(row));
+    }
+  };
+
+  // Q^T as the B operand: head lane/4, dims 16 ks + 2 (lane % 4) + {0, 1} (and + 8); heads >= rep are zero.
+  uint32_t qf[HD / 16][2];
+  {
+    const int hq = lane >> 2;
+    const bool ok = hq < p.rep;
+    const __nv_bfloat16* qrow = p.q + static_cast<int64_t>(r) * p.ldq +
+                                static_cast<int64_t>(g * p.rep + (ok ? hq : 0)) * HD + 2 * (lane & 3);
+#pragma unroll
+    for (int ks = 0; ks < HD / 16; ++ks) {
+      qf[ks][0] = ok ? *reinterpret_cast<const uint32_t*>(qrow + ks * 16) : 0u;
+      qf[ks][1] = ok ? *reinterpret_cast<const uint32_t*>(qrow + ks * 16 + 8) : 0u;
+    }
+  }
+  // This lane's score / output columns are heads h0 = 2 (lane % 4) and h0 + 1 (log2-domain softmax state).
+  float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
+  float acc[HD / 16][4];
+#pragma unroll
+  for (int mt = 0; mt < HD / 16; ++mt) acc[mt][0] = acc[mt][1] = acc[mt][2] = acc[mt][3] = 0.f;
+
+  if (lane == 0)
+    for (int j = 0; j < my_n && j < STAGES; ++j) issue(j);
+  int j = 0;
+  bool timed_out = false;
+  for (; j < my_n; ++j) {
+    const int s = j % STAGES;
+    const bool ok = mbar_wait(&wfull[s], static_cast<uint32_t>((j / STAGES) & 1), p.err);
+    if (!__all_sync(0xffffffffu, ok)) {
+      timed_out = true;
+      break;
+    }
+    const uint32_t kb = smem_u32(ring + s * G::STAGE_BYTES), vb = kb + G::KV_BYTES;
+    const int64_t k0 = k_begin + static_cast<int64_t>(warp + WARPS * j) * TILE;
+    const int n = static_cast<int>(k_end - k0 < TILE ? k_end - k0 : TILE);   // >= 1 visible key
+
+    // S^T (16 keys x 8 heads) = K (16 x HD) Q^T (HD x 8)
+    float c[4] = {0.f, 0.f, 0.f, 0.f};
+    {
+      const int mi = lane >> 3, key = ((mi & 1) << 3) | (lane & 7);
+#pragma unroll
+      for (int ks = 0; ks < HD / 16; ++ks) {
+        uint32_t a[4];
+        ldsm_x4(a, tile_addr(kb, key, ks * 2 + (mi >> 1)));
+        mma16816(c, a, qf[ks][0], qf[ks][1]);
+      }
+    }
+    const int kA = lane >> 2, kB = kA + 8;   // keys of c[0..1] and c[2..3]
+    const float s0 = kA < n ? c[0] * p.scale_log2 : -INFINITY, s1 = kA < n ? c[1] * p.scale_log2 : -INFINITY;
+    const float s2 = kB < n ? c[2] * p.scale_log2 : -INFINITY, s3 = kB < n ? c[3] * p.scale_log2 : -INFINITY;
+    float t0 = fmaxf(s0, s2), t1 = fmaxf(s1, s3);
+#pragma unroll
+    for (int o = 4; o < 32; o <<= 1) {
+      t0 = fmaxf(t0, __shfl_xor_sync(0xffffffffu, t0, o));
+      t1 = fmaxf(t1, __shfl_xor_sync(0xffffffffu, t1, o));
+    }
+    const float mn0 = fmaxf(m0, t0), mn1 = fmaxf(m1, t1);           // finite: the tile has a visible key
+    const float cr0 = exp2f(m0 - mn0), cr1 = exp2f(m1 - mn1);         // 0 on the warp's first tile
+    const float p0 = exp2f(s0 - mn0), p1 = exp2f(s1 - mn1), p2 = exp2f(s2 - mn0), p3 = exp2f(s3 - mn1);
+    l0 = l0 * cr0 + p0 + p2;   // per-lane partial sums; the lanes of one head are added up at the end
+    l1 = l1 * cr1 + p1 + p3;
+    m0 = mn0;
+    m1 = mn1;
+#pragma unroll
+    for (int mt = 0; mt < HD / 16; ++mt) {
+      acc[mt][0] *= cr0;
+      acc[mt][1] *= cr1;
+      acc[mt][2] *= cr0;
+      acc[mt][3] *= cr1;
+    }
+    // P^T (16 keys x 8 heads) as the B operand: transpose the two 8 x 8 halves of P held in C layout
+    const uint32_t pb0 = movmatrix_trans(pack_bf16(p0, p1)), pb1 = movmatrix_trans(pack_bf16(p2, p3));
+    if (n < TILE) {   // V rows past the last key hold stale cache contents (possibly non-finite): zero them
+      for (int i = lane; i < (TILE - n) * G::NB * 8; i += 32) {
+        const int row = n + i / (G::NB * 8), rest = i % (G::NB * 8);
+        st_shared_zero16(vb + static_cast<uint32_t>((rest >> 3) * BOX_BYTES + row * 128 + (rest & 7) * 16));
+      }
+      __syncwarp();
+    }
+    // O^T (HD x 8 heads) += V^T (HD x 16 keys) P^T (16 keys x 8 heads)
+    {
+      const int mi = lane >> 3, key = ((mi >> 1) << 3) | (lane & 7);
+#pragma unroll
+      for (int mt = 0; mt < HD / 16; ++mt) {
+        uint32_t a[4];
+        ldsm_x4_trans(a, tile_addr(vb, key, mt * 2 + (mi & 1)));
+        mma16816(acc[mt], a, pb0, pb1);
+      }
+    }
+    __syncwarp();   // every lane's reads of this stage are done before it is refilled
+    if (lane == 0 && j + STAGES < my_n) {
+      fence_proxy_async_smem();
+      issue(j + STAGES);
+    }
+  }
+  if (timed_out) {   // let the copies still in flight land (bounded) before the CTA gives its shared memory back
+    const int issued = my_n < j + STAGES ? my_n : j + STAGES;
+    for (int t = j; t < issued; ++t) mbar_wait(&wfull[t % STAGES], static_cast<uint32_t>((t / STAGES) & 1), p.err);
+    if (lane == 0) abort_flag = 1;
+  }
+#pragma unroll
+  for (int o = 4; o < 32; o <<= 1) {
+    l0 += __shfl_xor_sync(0xffffffffu, l0, o);
+    l1 += __shfl_xor_sync(0xffffffffu, l1, o);
+  }
+  __syncthreads();   // all warps are done with their rings: reuse them for the merge
+  if (abort_flag) return;
+  float* osm = reinterpret_cast<float*>(smem);   // [WARPS][8 heads][HD]
+  const int h0 = 2 * (lane & 3);
+  if (lane < 4) {
+    sm_m[warp * 8 + h0] = m0;
+    sm_m[warp * 8 + h0 + 1] = m1;
+    sm_l[warp * 8 + h0] = l0;
+    sm_l[warp * 8 + h0 + 1] = l1;
+  }
+#pragma unroll
+  for (int mt = 0; mt < HD / 16; ++mt) {
+    const int d = mt * 16 + (lane >> 2);
+    float* o0 = osm + (warp * 8 + h0) * HD;
+    o0[d] = acc[mt][0];
+    o0[HD + d] = acc[mt][1];
+    o0[d + 8] = acc[mt][2];
+    o0[HD + d + 8] = acc[mt][3];
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < p.rep * HD; i += THREADS_TC) {
+    const int h = i / HD, d = i % HD;
+    float M = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < WARPS; ++w) M = fmaxf(M, sm_m[w * 8 + h]);
+    float L = 0.f, o = 0.f;
+#pragma unroll
+    for (int w = 0; w < WARPS; ++w) {
+      const float mw = sm_m[w * 8 + h];
+      const float f = mw == -INFINITY ? 0.f : exp2f(mw - M);
+      L += f * sm_l[w * 8 + h];
+      o += f * osm[(w * 8 + h) * HD + d];
+    }
+    const int hh = g * p.rep + h;
+    if (p.splits == 1) {
+      p.out[static_cast<int64_t>(r) * p.ldo + static_cast<int64_t>(hh) * HD + d] =
+          __float2bfloat16_rn(L > 0.f ? o / L : 0.f);
+    } else {
+      const int64_t slot = (static_cast<int64_t>(r) * p.nh + hh) * p.splits + split;
+      p.ws[slot * HD + d] = o;
+      if (d == 0) {
+        float* ml = p.ws + static_cast<int64_t>(gridDim.z) * p.nh * p.splits * HD;
+        ml[2 * slot] = M == -INFINITY ? -INFINITY : M * 0.6931471805599453f;   // log2 -> natural-log domain
+        ml[2 * slot + 1] = L;
+      }
+    }
+  }
+}
+
+// The tile loads address the cache as one 2-D tensor of hd-wide rows (row = block * rows_per_block +
+// kv_head * rows_per_head + slot) in 16-row boxes, so a 16-key tile must sit inside one block.
+bool supported(const KVCache& kv, int64_t hd) {
+  if (kv.block_size % TILE != 0) return false;
+  if (kv.block_stride % hd != 0 || kv.head_stride % hd != 0 || kv.head_stride / hd < kv.block_size) return false;
+  const int64_t rows = kv.num_blocks * (kv.block_stride / hd);
+  return rows < (int64_t(1) << 31) - 2 * TILE;
+}
+
+template <int HD>
+int launch_t(const void* q, int64_t ldq, const KVCache& kv, int64_t n_slots, const int64_t* positions, void* out,
+             int64_t ldo, int64_t B, int64_t nh, int64_t nkv, float scale, int splits, float* ws, unsigned* err,
+             cudaStream_t st) {
+  using G = Geo<HD>;
+  const int64_t kv_rows = kv.num_blocks * (kv.block_stride / HD);
+  CUtensorMap mk, mv;
+  if (make_bf16_map(&mk, kv.k, HD, kv_rows, HD, TILE) || make_bf16_map(&mv, kv.v, HD, kv_rows, HD, TILE)) return -1;
+  Params p;
+  p.q = static_cast<const __nv_bfloat16*>(q);
+  p.ldq = ldq;
+  p.table = kv.table;
+  p.table_stride = kv.table_stride;
+  p.table_cols = kv.table_cols;
+  p.block_size = kv.block_size;
+  p.rows_per_block = kv.block_stride / HD;
+  p.rows_per_head = kv.head_stride / HD;
+  p.num_blocks = kv.num_blocks;
+  p.kv_rows = kv_rows;
+  p.n_slots = n_slots;
+  p.positions = positions;
+  p.out = static_cast<__nv_bfloat16*>(out);
+  p.ldo = ldo;
+  p.nh = static_cast<int>(nh);
+  p.rep = static_cast<int>(nh / nkv);
+  p.splits = splits;
+  const int64_t per = (n_slots + splits - 1) / splits;
+  p.per = static_cast<int>((per + TILE - 1) / TILE * TILE);
+  p.scale_log2 = scale * 1.4426950408889634f;
+  p.ws = ws;
+  p.err = err;
+  static bool attr[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev >= 0 && dev < 64 && !attr[dev]) {
+    if (cudaFuncSetAttribute(attn_decode_tc_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, G::SMEM) !=
+        cudaSuccess)
+      return check_launch("attn_decode_tc set smem");
+    attr[dev] = true;
+  }
+  dim3 grid(static_cast<unsigned>(splits), static_cast<unsigned>(nkv), static_cast<unsigned>(B));
+  attn_decode_tc_kernel<HD><<<grid, THREADS_TC, G::SMEM, st>>>(mk, mv, p);
+  return check_launch("attn_decode_tc_kernel");
+}
+
+}  // namespace tcd
+
 template <typename T, int HD>
 int launch_t(const void* q, int64_t ldq, const KVCache& kv, int64_t n_slots, const int64_t* positions, void* out,
-             int64_t ldo, int64_t B, int64_t nh, int64_t nkv, float scale, int splits, float* ws, cudaStream_t st) {
+             int64_t ldo, int64_t B, int64_t nh, int64_t nkv, float scale, int splits, float* ws, unsigned* err,
+             cudaStream_t st) {
   using S = Smem<T, HD>;
   static bool attr[64] = {false};
   int dev = 0;
@@ -211,26 +555,29 @@ int launch_t(const void* q, int64_t ldq, const KVCache& kv, int64_t n_slots, con
       return check_launch("attn_decode set smem");
     attr[dev] = true;
   }
-  unsigned* err = error_word();
-  if (!err) return -1;
   dim3 grid(static_cast<unsigned>(splits), static_cast<unsigned>(nkv), static_cast<unsigned>(B));
   attn_decode_kernel<T, HD><<<grid, THREADS, S::BYTES, st>>>(
       static_cast<const T*>(q), ldq, kv, n_slots, positions, static_cast<T*>(out), ldo, static_cast<int>(nh),
       static_cast<int>(nh / nkv), splits, scale, ws, err);
-  if (check_launch("attn_decode_kernel")) return -1;
-  if (splits > 1) {
-    attn_combine_kernel<T, HD><<<dim3(static_cast<unsigned>(B), static_cast<unsigned>(nh)), THREADS, 0, st>>>(
-        ws, static_cast<int>(B), static_cast<int>(nh), splits, static_cast<T*>(out), ldo);
-    return check_launch("attn_combine_kernel");
-  }
-  return 0;
+  return check_launch("attn_decode_kernel");
 }
 
-int choose_splits(int64_t B, int64_t nkv, int64_t n_slots, int sm_target) {
-  const int64_t base = B * nkv;
-  int64_t s = (sm_target + base - 1) / base;             // enough CTAs to fill the GPU
-  const int64_t by_len = (n_slots + 4 * CHUNK - 1) / (4 * CHUNK);   // at least 256 keys per split
-  if (s > by_len) s = by_len;
+template <typename T, int HD>
+int combine_t(float* ws, int64_t B, int64_t nh, int splits, void* out, int64_t ldo, cudaStream_t st) {
+  attn_combine_kernel<T, HD><<<dim3(static_cast<unsigned>(B), static_cast<unsigned>(nh)), THREADS, 0, st>>>(
+      ws, static_cast<int>(B), static_cast<int>(nh), splits, static_cast<T*>(out), ldo);
+  return check_launch("attn_combine_kernel");
+}
+
+int choose_splits(int64_t B, int64_t nkv, int64_t n_slots, int sms) {
+  // Keys per split: the batch's key slots (B * nkv * n_slots, an upper bound) over ~8 CTAs per SM, between 128
+  // and 512 slots, a multiple of 64; more only when that would exceed MAX_SPLITS.
+  if (sms <= 0) sms = 148;
+  int64_t per = (B * nkv * n_slots + 8 * static_cast<int64_t>(sms) - 1) / (8 * static_cast<int64_t>(sms));
+  per = (per + 63) / 64 * 64;
+  if (per < 2 * CHUNK) per = 2 * CHUNK;
+  if (per > 8 * CHUNK) per = 8 * CHUNK;
+  int64_t s = (n_slots + per - 1) / per;
   if (s > MAX_SPLITS) s = MAX_SPLITS;
   return s < 1 ? 1 : static_cast<int>(s);
 }
@@ -250,18 +597,30 @@ bool supported(int dtype, int64_t hd, int64_t nh, int64_t nkv, const void* q, in
 
 int launch(int dtype, const void* q, int64_t ldq, const KVCache& kv, int64_t n_slots, const int64_t* positions,
            void* out, int64_t ldo, int64_t B, int64_t nh, int64_t nkv, int64_t hd, float scale, int splits, float* ws,
-           cudaStream_t st) {
+           unsigned* err, cudaStream_t st) {
   if (B > 65535 || nkv > 65535) return fail("attention_decode: grid too large");
   if (splits > 1 && !ws) return fail("attention_decode: a workspace is needed for more than one split");
-  if (dtype == BF16 && hd == 128)
-    return launch_t<__nv_bfloat16, 128>(q, ldq, kv, n_slots, positions, out, ldo, B, nh, nkv, scale, splits, ws, st);
-  if (dtype == BF16 && hd == 64)
-    return launch_t<__nv_bfloat16, 64>(q, ldq, kv, n_slots, positions, out, ldo, B, nh, nkv, scale, splits, ws, st);
-  if (dtype == F32 && hd == 128)
-    return launch_t<float, 128>(q, ldq, kv, n_slots, positions, out, ldo, B, nh, nkv, scale, splits, ws, st);
-  if (dtype == F32 && hd == 64)
-    return launch_t<float, 64>(q, ldq, kv, n_slots, positions, out, ldo, B, nh, nkv, scale, splits, ws, st);
-  return fail("attention_decode: head_dim must be 64 or 128 and dtype fp32 or bf16");
+  if (hd != 64 && hd != 128) return fail("attention_decode: head_dim must be 64 or 128");
+  int rc;
+  if (dtype == BF16 && tcd::supported(kv, hd)) {
+    rc = hd == 128 ? tcd::launch_t<128>(q, ldq, kv, n_slots, positions, out, ldo, B, nh, nkv, scale, splits, ws, err, st)
+                   : tcd::launch_t<64>(q, ldq, kv, n_slots, positions, out, ldo, B, nh, nkv, scale, splits, ws, err, st);
+  } else if (dtype == BF16) {
+    rc = hd == 128
+             ? launch_t<__nv_bfloat16, 128>(q, ldq, kv, n_slots, positions, out, ldo, B, nh, nkv, scale, splits, ws, err, st)
+             : launch_t<__nv_bfloat16, 64>(q, ldq, kv, n_slots, positions, out, ldo, B, nh, nkv, scale, splits, ws, err, st);
+  } else if (dtype == F32) {
+    rc = hd == 128 ? launch_t<float, 128>(q, ldq, kv, n_slots, positions, out, ldo, B, nh, nkv, scale, splits, ws, err, st)
+                   : launch_t<float, 64>(q, ldq, kv, n_slots, positions, out, ldo, B, nh, nkv, scale, splits, ws, err, st);
+  } else {
+    return fail("attention_decode: dtype must be fp32 or bf16");
+  }
+  if (rc || splits == 1) return rc;
+  if (dtype == BF16)
+    return hd == 128 ? combine_t<__nv_bfloat16, 128>(ws, B, nh, splits, out, ldo, st)
+                     : combine_t<__nv_bfloat16, 64>(ws, B, nh, splits, out, ldo, st);
+  return hd == 128 ? combine_t<float, 128>(ws, B, nh, splits, out, ldo, st)
+                   : combine_t<float, 64>(ws, B, nh, splits, out, ldo, st);
 }
 
 }  // namespace decode
@@ -278,9 +637,9 @@ int launch(int dtype, const void* q, int64_t ldq, const KVCache& kv, int64_t n_s
 // library image instead: a file-scope __device__ array of kStaticScratchBytes (4 MiB), which every GPU that
 // loads the library holds until the process exits.
 //
-// * Set-up: the first call on a device resolves the array's device address with cudaGetSymbolAddress (and sets
-//   the kernels' shared-memory attribute) with that device current; make that first call before any stream
-//   capture on that device.
+// * Set-up: the first call on a device resolves the array's device address with cudaGetSymbolAddress (and the
+//   first launch of each kernel sets its shared-memory attribute) with that device current; make that first call
+//   before any stream capture on that device.
 // * Limit: calls whose split partials need more than kStaticScratchBytes are refused with an error naming the
 //   size (fs_attention_decode_workspace() gives the size a call needs).
 // * Sharing: every call uses the same array and leaves its contents behind; each call writes every partial it
@@ -310,39 +669,10 @@ static int static_scratch(float** out) {
     void* p = nullptr;
     const cudaError_t e = cudaGetSymbolAddress(&p, g_static_scratch);
     if (e != cudaSuccess) return fail(std::string("cudaGetSymbolAddress(decode scratch): ") + cudaGetErrorString(e));
-    using S128 = Smem<float, 128>;
-    using S64 = Smem<float, 64>;
-    if (cudaFuncSetAttribute(attn_decode_kernel<float, 128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             S128::BYTES) != cudaSuccess ||
-        cudaFuncSetAttribute(attn_decode_kernel<float, 64>, cudaFuncAttributeMaxDynamicSharedMemorySize, S64::BYTES) !=
-            cudaSuccess ||
-        cudaFuncSetAttribute(attn_decode_kernel<__nv_bfloat16, 128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             Smem<__nv_bfloat16, 128>::BYTES) != cudaSuccess ||
-        cudaFuncSetAttribute(attn_decode_kernel<__nv_bfloat16, 64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             Smem<__nv_bfloat16, 64>::BYTES) != cudaSuccess)
-      return check_launch("decode scratch set-up");
     s.ptr = static_cast<float*>(p);
     s.ready = true;
   }
   *out = s.ptr;
-  return 0;
-}
-
-template <typename T, int HD>
-static int launch_static_t(const void* q, int64_t ldq, const KVCache& kv, int64_t n_slots, const int64_t* positions,
-                           void* out, int64_t ldo, int64_t B, int64_t nh, int64_t nkv, float scale, int splits,
-                           float* ws, unsigned* err, cudaStream_t st) {
-  using S = Smem<T, HD>;
-  dim3 grid(static_cast<unsigned>(splits), static_cast<unsigned>(nkv), static_cast<unsigned>(B));
-  attn_decode_kernel<T, HD><<<grid, THREADS, S::BYTES, st>>>(
-      static_cast<const T*>(q), ldq, kv, n_slots, positions, static_cast<T*>(out), ldo, static_cast<int>(nh),
-      static_cast<int>(nh / nkv), splits, scale, ws, err);
-  if (check_launch("attn_decode_kernel")) return -1;
-  if (splits > 1) {
-    attn_combine_kernel<T, HD><<<dim3(static_cast<unsigned>(B), static_cast<unsigned>(nh)), THREADS, 0, st>>>(
-        ws, static_cast<int>(B), static_cast<int>(nh), splits, static_cast<T*>(out), ldo);
-    return check_launch("attn_combine_kernel");
-  }
   return 0;
 }
 
@@ -380,7 +710,7 @@ extern "C" int fs_attention_decode_static(const void* q, int64_t ldq, const fs_k
   int sms = 0, dev = 0;
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  const int splits = choose_splits(B, nkv, n_slots, 2 * (sms > 0 ? sms : 148));
+  const int splits = choose_splits(B, nkv, n_slots, sms);
   const int64_t need = workspace_bytes(B, nh, hd, splits);
   if (need > kStaticScratchBytes)
     return fail("fs_attention_decode_static: this call needs " + std::to_string(need) +
@@ -388,13 +718,6 @@ extern "C" int fs_attention_decode_static(const void* q, int64_t ldq, const fs_k
                 " bytes; use fs_attention_decode with a caller-owned workspace");
   float* ws = nullptr;
   if (static_scratch(&ws)) return -1;
-  unsigned* err = error_word_if_present();
-  cudaStream_t st = static_cast<cudaStream_t>(stream);
-  if (dtype == BF16 && hd == 128)
-    return launch_static_t<__nv_bfloat16, 128>(q, ldq, *kv, n_slots, positions, out, ldo, B, nh, nkv, scale, splits, ws, err, st);
-  if (dtype == BF16)
-    return launch_static_t<__nv_bfloat16, 64>(q, ldq, *kv, n_slots, positions, out, ldo, B, nh, nkv, scale, splits, ws, err, st);
-  if (hd == 128)
-    return launch_static_t<float, 128>(q, ldq, *kv, n_slots, positions, out, ldo, B, nh, nkv, scale, splits, ws, err, st);
-  return launch_static_t<float, 64>(q, ldq, *kv, n_slots, positions, out, ldo, B, nh, nkv, scale, splits, ws, err, st);
+  return launch(dtype, q, ldq, *kv, n_slots, positions, out, ldo, B, nh, nkv, hd, scale, splits, ws,
+                error_word_if_present(), static_cast<cudaStream_t>(stream));
 }

@@ -530,4 +530,9 @@ int launch(const void* q, int64_t ldq, const KVCache& kv, int64_t n_slots, const
 }
 
 }  // namespace attn_tc
+
+int make_bf16_map(CUtensorMap* map, const void* ptr, int64_t cols, int64_t rows, int64_t ld, int box_rows) {
+  return attn_tc::make_map(map, ptr, cols, rows, ld, box_rows);
+}
+
 }  // namespace fs

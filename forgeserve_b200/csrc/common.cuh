@@ -52,6 +52,10 @@ __device__ __forceinline__ void flag_error(unsigned* err, unsigned code) {
   if (err) atomicOr(err, code);
 }
 
+// 2-D bf16 tensor map with 128-byte swizzle and boxes of 64 columns x box_rows rows, over a row-major matrix of
+// `rows` rows of `cols` elements at a stride of `ld` elements (defined in attention_tc.cu).
+int make_bf16_map(CUtensorMap* map, const void* ptr, int64_t cols, int64_t rows, int64_t ld, int box_rows);
+
 // ---------------------------------------------------------------------------------------------------------
 // mbarrier / TMA / tcgen05 PTX wrappers
 // ---------------------------------------------------------------------------------------------------------

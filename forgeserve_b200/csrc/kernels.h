@@ -45,12 +45,12 @@ int launch(const void* q, int64_t ldq, const KVCache& kv, int64_t n_slots, const
 }  // namespace attn_tc
 
 namespace decode {
-int choose_splits(int64_t B, int64_t nkv, int64_t n_slots, int sm_target);
+int choose_splits(int64_t B, int64_t nkv, int64_t n_slots, int sms);
 int64_t workspace_bytes(int64_t B, int64_t nh, int64_t hd, int splits);
 bool supported(int dtype, int64_t hd, int64_t nh, int64_t nkv, const void* q, int64_t ldq, const KVCache& kv);
 int launch(int dtype, const void* q, int64_t ldq, const KVCache& kv, int64_t n_slots, const int64_t* positions,
            void* out, int64_t ldo, int64_t B, int64_t nh, int64_t nkv, int64_t hd, float scale, int splits, float* ws,
-           cudaStream_t st);
+           unsigned* err, cudaStream_t st);
 }  // namespace decode
 
 }  // namespace fs

@@ -393,16 +393,18 @@ def test_gemm_pair_kernel_matches_single_cta_kernel(epi, M, N, K):
 
 
 # ------------------------------------------------------------------------------------- decode attention
-@pytest.mark.parametrize("dtype,hd,nh,nkv,lengths", [
-    (torch.bfloat16, 128, 32, 8, [3000, 17, 700, 1]),        # long rows: several splits
-    (torch.bfloat16, 128, 32, 8, [200] * 64),                # a full decode batch: one split
-    (torch.bfloat16, 64, 8, 8, [513, 64, 65]),               # no GQA sharing
-    (torch.bfloat16, 128, 8, 1, [1000]),                     # one KV head for 8 query heads
-    (torch.float32, 128, 16, 4, [333, 2048, 5]),
+@pytest.mark.parametrize("dtype,hd,nh,nkv,lengths,bs", [
+    (torch.bfloat16, 128, 32, 8, [3000, 17, 700, 1], 16),    # long rows: several splits
+    (torch.bfloat16, 128, 32, 8, [200] * 64, 16),            # a full decode batch
+    (torch.bfloat16, 64, 8, 8, [513, 64, 65], 16),           # no GQA sharing
+    (torch.bfloat16, 128, 8, 1, [1000], 16),                 # one KV head for 8 query heads
+    (torch.bfloat16, 128, 32, 8, [900, 31, 2], 32),          # 16-key tiles inside 32-slot blocks
+    (torch.bfloat16, 128, 32, 8, [900, 31, 2], 8),           # blocks smaller than a tile: CUDA-core kernel
+    (torch.bfloat16, 128, 12, 4, [4000, 2500, 130, 17, 8, 3000, 600, 1], 16),   # rep 3, ragged lengths
+    (torch.float32, 128, 16, 4, [333, 2048, 5], 16),
 ])
-def test_attention_decode_paged(dtype, hd, nh, nkv, lengths):
-    """One query per row at its own position, over scattered 16-slot blocks (padded tables), against fp64 SDPA."""
-    bs = 16
+def test_attention_decode_paged(dtype, hd, nh, nkv, lengths, bs):
+    """One query per row at its own position, over scattered blocks (padded tables), against fp64 SDPA."""
     B = len(lengths)
     widths = [-(-(n + 1) // bs) for n in lengths]
     nblk = sum(widths) + 3
@@ -423,6 +425,53 @@ def test_attention_decode_paged(dtype, hd, nh, nkv, lengths):
     got = out.view(B, 1, nh, hd).transpose(1, 2).double()
     tol = 1e-5 if dtype == torch.float32 else 2e-2
     assert (got - want).abs().max().item() < tol
+
+
+def test_attention_decode_ignores_stale_slots():
+    """Slots past each row's position (in the last block, and whole unused blocks) hold NaN: they must not leak."""
+    B, nh, nkv, hd, bs = 3, 32, 8, 128, 16
+    lengths = [37, 16, 250]
+    widths = [-(-(n + 1) // bs) + 1 for n in lengths]          # one extra (unused) block per row
+    nblk = sum(widths)
+    table = torch.arange(nblk, device=DEV).flip(0)
+    rows, at = [], 0
+    for w in widths:
+        rows.append(table[at : at + w].tolist())
+        at += w
+    W = max(widths)
+    table = torch.tensor([r + [0] * (W - len(r)) for r in rows], device=DEV)
+    pool_k = torch.full((nblk, nkv, bs, hd), float("nan"), device=DEV).bfloat16()
+    pool_v = torch.full((nblk, nkv, bs, hd), float("nan"), device=DEV).bfloat16()
+    for r, n in enumerate(lengths):
+        for s in range(n + 1):
+            blk = int(table[r, s // bs])
+            pool_k[blk, :, s % bs] = torch.randn(nkv, hd, device=DEV).bfloat16()
+            pool_v[blk, :, s % bs] = torch.randn(nkv, hd, device=DEV).bfloat16()
+    q = torch.randn(B, nh * hd, device=DEV).bfloat16()
+    positions = torch.tensor([[n] for n in lengths], device=DEV)
+    out = torch.empty_like(q)
+    ops.attention_decode(q, ops.paged_desc(pool_k, pool_v, table), W * bs, positions, out, B, nh, nkv, hd)
+    torch.cuda.synchronize()
+    assert torch.isfinite(out.float()).all()
+    k_all = torch.nan_to_num(pool_k[table].permute(0, 2, 1, 3, 4).reshape(B, nkv, -1, hd).double())
+    v_all = torch.nan_to_num(pool_v[table].permute(0, 2, 1, 3, 4).reshape(B, nkv, -1, hd).double())
+    want = attention_ref(q.view(B, 1, nh, hd).transpose(1, 2), k_all, v_all, positions, nh // nkv)
+    got = out.view(B, 1, nh, hd).transpose(1, 2).double()
+    assert (got - want).abs().max().item() < 2e-2
+
+
+def test_attention_decode_flags_a_bad_block():
+    """A block id outside the pool inside the visible range sets the device error bit; nothing is read there."""
+    B, nh, nkv, hd, bs = 1, 32, 8, 128, 16
+    pool = torch.randn(4, nkv, bs, hd, device=DEV).bfloat16()
+    table = torch.tensor([[0, 1, 9]], device=DEV)             # block 9 does not exist
+    q = torch.randn(B, nh * hd, device=DEV).bfloat16()
+    out = torch.empty_like(q)
+    L.device_error(clear=True)
+    ops.attention_decode(q, ops.paged_desc(pool, pool, table), 3 * bs, torch.tensor([[40]], device=DEV), out, B, nh,
+                         nkv, hd)
+    torch.cuda.synchronize()
+    assert L.device_error(clear=True) & L.FS_ERR_BAD_SLOT
 
 
 def test_attention_decode_contiguous_matches_generic():
