@@ -132,6 +132,9 @@ def run_ours(args):
     cfg = ModelConfig(**CFG)
     stage = PipelineStage(cfg, rank, world, device=dev, dtype=torch.bfloat16).eval()
     init_stage_(stage, seed=1234, std=0.02)
+    split_head = world > 1 and not args.whole_head
+    if split_head:
+        stage.split_head_()   # every stage computes a vocab slice of the head (logits still land on the last stage)
     batch = MICROBATCHES * MB_ROWS
     g = torch.Generator(device="cpu").manual_seed(7)
     idx_host = torch.randint(0, cfg.vocab_size, (batch, SEQ), generator=g).pin_memory()
@@ -217,6 +220,7 @@ def run_ours(args):
             "data": "synthetic: uniform token ids, seeded N(0, 0.02) weights (no checkpoint or dataset)",
             "config": {"workload": WORKLOAD, "global_batch": batch, "seq_len": SEQ, "microbatches": MICROBATCHES,
                        "stages": world, "parallelism": f"pp{world}",
+                       "head": "split over the stages by vocab range" if split_head else "on the last stage",
                        "l2": "no flush needed: every step streams 16 GB of weights (> 126 MB L2)"},
             "bubble": {"measured": round(1.0 - busy_sum / (world * ms_max), 4),
                        "analytic": round(bubble_fraction(world, MICROBATCHES), 4)},
@@ -415,6 +419,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--whole-head", action="store_true", help="N > 1: keep the whole output head on the last stage")
     ap.add_argument("--profile-case", default=None, help="run a few launches of one kernel (for ncu) and exit")
     ap.add_argument("--reps", type=int, default=3)
     ap.add_argument("--timed", action="store_true", help="with --profile-case: also time cold-L2 launches")

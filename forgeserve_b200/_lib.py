@@ -12,6 +12,8 @@ LIB_PATH = Path(__file__).resolve().with_name("libforgeserve_b200.so")
 
 FS_F32, FS_BF16 = 0, 1
 FS_EPI_STORE, FS_EPI_RESIDUAL, FS_EPI_SWIGLU = 0, 1, 2
+FS_EPI_SYSTEM_FENCE = 0x100
+FS_IPC_HANDLE_BYTES = 64
 FS_ERR_WAIT_TIMEOUT, FS_ERR_BAD_TOKEN, FS_ERR_BAD_SLOT, FS_ERR_BAD_POSITION = 1, 2, 4, 8
 FS_ATTN_AUTO, FS_ATTN_CUDA_CORE, FS_ATTN_MMA_SYNC, FS_ATTN_TCGEN05 = 0, 1, 2, 3
 
@@ -42,6 +44,9 @@ SIGNATURES = {
     "fs_launch_count": (c_i64, []),
     "fs_set_persistent_sms": (c_int, [c_int]),
     "fs_set_gemm_pair_mode": (c_int, [c_int]),
+    "fs_ipc_handle": (c_int, [c_vp, c_vp, ctypes.POINTER(c_i64)]),
+    "fs_ipc_open": (c_int, [c_vp, ctypes.POINTER(c_vp)]),
+    "fs_ipc_close": (c_int, [c_vp]),
     "fs_rmsnorm": (c_int, [c_vp, c_i64, c_vp, c_vp, c_i64, c_i64, c_i64, c_float, c_int, c_vp]),
     "fs_gemm": (c_int, [c_vp, c_i64, c_vp, c_i64, c_vp, c_i64, c_vp, c_i64, c_i64, c_i64, c_i64, c_i64, c_int, c_int,
                         c_vp]),

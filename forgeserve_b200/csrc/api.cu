@@ -1,5 +1,8 @@
 // The C ABI (include/forgeserve_b200.h): argument checks, dispatch, error strings, launch counting.
+#include <cudaTypedefs.h>
+
 #include <atomic>
+#include <cstring>
 #include <string>
 
 #include "../../include/forgeserve_b200.h"
@@ -106,6 +109,52 @@ int fs_set_persistent_sms(int n) { return tcg::set_persistent_sms(n); }
 
 int fs_set_gemm_pair_mode(int on) { return tcg::set_pair_mode(on); }
 
+// ------------------------------------------------------------------------------------------ inter-process
+static PFN_cuMemGetAddressRange_v3020 address_range_fn() {
+  static PFN_cuMemGetAddressRange_v3020 fn = nullptr;
+  if (!fn) {
+    cudaDriverEntryPointQueryResult q;
+    void* ptr = nullptr;
+    if (cudaGetDriverEntryPoint("cuMemGetAddressRange", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuMemGetAddressRange_v3020>(ptr);
+  }
+  return fn;
+}
+
+int fs_ipc_handle(const void* ptr, void* handle, int64_t* offset) {
+  if (!ptr || !handle || !offset) return fail("fs_ipc_handle: NULL pointer");
+  auto range = address_range_fn();
+  if (!range) return fail("fs_ipc_handle: cuMemGetAddressRange is unavailable from the CUDA driver");
+  CUdeviceptr base = 0;
+  size_t size = 0;
+  if (range(&base, &size, reinterpret_cast<CUdeviceptr>(ptr)) != CUDA_SUCCESS)
+    return fail("fs_ipc_handle: the pointer is not inside a device allocation");
+  cudaIpcMemHandle_t h;
+  const cudaError_t e = cudaIpcGetMemHandle(&h, reinterpret_cast<void*>(base));
+  if (e != cudaSuccess) return fail(std::string("fs_ipc_handle: cudaIpcGetMemHandle: ") + cudaGetErrorString(e));
+  static_assert(sizeof(h) == FS_IPC_HANDLE_BYTES, "CUDA IPC handle size");
+  std::memcpy(handle, &h, sizeof(h));
+  *offset = static_cast<int64_t>(reinterpret_cast<CUdeviceptr>(ptr) - base);
+  return 0;
+}
+
+int fs_ipc_open(const void* handle, void** base) {
+  if (!handle || !base) return fail("fs_ipc_open: NULL pointer");
+  cudaIpcMemHandle_t h;
+  std::memcpy(&h, handle, sizeof(h));
+  const cudaError_t e = cudaIpcOpenMemHandle(base, h, cudaIpcMemLazyEnablePeerAccess);
+  if (e != cudaSuccess) return fail(std::string("fs_ipc_open: cudaIpcOpenMemHandle: ") + cudaGetErrorString(e));
+  return 0;
+}
+
+int fs_ipc_close(void* base) {
+  if (!base) return fail("fs_ipc_close: NULL pointer");
+  const cudaError_t e = cudaIpcCloseMemHandle(base);
+  if (e != cudaSuccess) return fail(std::string("fs_ipc_close: cudaIpcCloseMemHandle: ") + cudaGetErrorString(e));
+  return 0;
+}
+
 int fs_rmsnorm(const void* x, int64_t x_stride, const void* w, void* y, int64_t y_stride, int64_t rows, int64_t dim,
                float eps, int dtype, void* stream) {
   if (!x || !w || !y) return rows <= 0 ? 0 : fail("fs_rmsnorm: NULL pointer");
@@ -117,6 +166,8 @@ static int gemm_common(bool allow_tc, const void* A, int64_t lda, const void* B,
                        const void* R, int64_t ldr, int64_t M, int64_t N, int64_t K, int64_t n_out, int epi, int dtype,
                        void* stream) {
   if (M <= 0 || n_out <= 0) return 0;
+  const bool sys_fence = (epi & EPI_FLAG_SYSTEM_FENCE) != 0;
+  epi &= ~EPI_FLAG_SYSTEM_FENCE;
   if (!A || !B || !C) return fail("fs_gemm: NULL pointer");
   if (!dtype_ok(dtype)) return fail("fs_gemm: unsupported dtype");
   if (K <= 0 || N <= 0) return fail("fs_gemm: K and N must be positive");
@@ -132,7 +183,8 @@ static int gemm_common(bool allow_tc, const void* A, int64_t lda, const void* B,
   if (ldc < n_out || (epi == EPI_RESIDUAL && ldr < n_out)) return fail("fs_gemm: output row stride too small");
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (allow_tc && dtype == BF16 && tcg::supported(A, lda, B, ldb, K))
-    return tcg::gemm_tc(A, lda, B, ldb, C, ldc, R, ldr, M, N, K, n_out, epi, st);
+    return tcg::gemm_tc(A, lda, B, ldb, C, ldc, R, ldr, M, N, K, n_out, epi, sys_fence, st);
+  if (sys_fence) return fail("fs_gemm: FS_EPI_SYSTEM_FENCE needs the tensor-core kernel (bf16, aligned operands)");
   return gemm_simt(dtype, A, lda, B, ldb, C, ldc, R, ldr, M, N, K, n_out, epi, st);
 }
 

@@ -18,6 +18,10 @@
 //   warps 4-7   epilogue: tcgen05.ld 32 lanes x 32 columns, fused epilogue, vector stores to global memory
 // The two TMEM accumulators let the epilogue of one tile overlap the main loop of the next.
 // No TMA multicast is used anywhere (the kernel also runs in multi-GPU jobs).
+#include <map>
+#include <mutex>
+#include <utility>
+
 #include <cudaTypedefs.h>
 
 #include "common.cuh"
@@ -44,8 +48,12 @@ struct Params {
   int64_t ldc, ldr;
   int M, n_out;
   int num_m_blocks, num_tiles, k_blocks;
+  int sys_fence;   // C may be another GPU's memory: end every epilogue thread with a system-scope fence
+  unsigned* sched; // 1-SM kernel: [next tile, CTAs finished], zero at launch; the last CTA to finish re-zeroes it
   unsigned* err;
 };
+
+constexpr int TQ = 4;   // tile-queue entries (claimed tiles handed from the producer to the MMA and epilogue warps)
 
 __device__ __forceinline__ void tile_coords(int tile, int num_m_blocks, int& m_blk, int& n_blk) {
   // M-fastest order: the CTAs resident at one time share a few B (weight) tiles and stream all of A,
@@ -163,6 +171,9 @@ __global__ void __launch_bounds__(THREADS, 1)
   uint64_t* mma_done = bars + 2 * STAGES + 2 * NUM_ACC;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  uint64_t* tq_full = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES + 128);
+  uint64_t* tq_empty = tq_full + TQ;
+  volatile int* tq = reinterpret_cast<volatile int*>(tq_empty + TQ);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
@@ -174,6 +185,10 @@ __global__ void __launch_bounds__(THREADS, 1)
     for (int a = 0; a < NUM_ACC; ++a) {
       mbar_init(&tfull[a], 1);
       mbar_init(&tempty[a], 128);
+    }
+    for (int i = 0; i < TQ; ++i) {
+      mbar_init(&tq_full[i], 1);
+      mbar_init(&tq_empty[i], 1 + 4);   // the MMA thread and one lane of each epilogue warp
     }
     mbar_init(mma_done, 1);
     *abort_flag = 0;
@@ -192,6 +207,10 @@ __global__ void __launch_bounds__(THREADS, 1)
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
+  // Tiles are claimed at run time from a counter shared by the grid, in increasing order (M fastest), so a CTA
+  // slowed down by other work on its SM (a resident NCCL kernel) takes fewer tiles instead of holding the whole
+  // GEMM back. The producer claims; the tile queue hands each claim (or -1: no tiles left) to the MMA thread and
+  // the epilogue warps.
   if (warp == 0) {
     // ------------------------------------------------------------------ TMA producer
     if (lane == 0) {
@@ -202,7 +221,17 @@ __global__ void __launch_bounds__(THREADS, 1)
 #pragma unroll
       for (int i = 0; i < STAGES; ++i) issued[i] = false, last_ph[i] = 0;
       bool ok = true;
-      for (int tile = blockIdx.x; tile < p.num_tiles && ok; tile += gridDim.x) {
+      for (int i = 0; ok; ++i) {
+        const int slot = i & (TQ - 1);
+        if (!mbar_wait(&tq_empty[slot], static_cast<uint32_t>((i / TQ) & 1) ^ 1u, p.err) || *abort_flag) {
+          ok = false;
+          break;
+        }
+        int tile = static_cast<int>(atomicAdd(p.sched, 1u));
+        if (tile >= p.num_tiles) tile = -1;
+        tq[slot] = tile;
+        mbar_arrive(&tq_full[slot]);
+        if (tile < 0) break;
         int m_blk, n_blk;
         tile_coords(tile, p.num_m_blocks, m_blk, n_blk);
         const int b_row0 = EPI == EPI_SWIGLU ? n_blk * (BN / 2) : n_blk * BN;
@@ -234,7 +263,15 @@ __global__ void __launch_bounds__(THREADS, 1)
       int s = 0, acc = 0;
       uint32_t ph = 0, acc_ph = 0;
       bool ok = true;
-      for (int tile = blockIdx.x; tile < p.num_tiles && ok; tile += gridDim.x) {
+      for (int i = 0; ok; ++i) {
+        const int slot = i & (TQ - 1);
+        if (!mbar_wait(&tq_full[slot], static_cast<uint32_t>((i / TQ) & 1), p.err) || *abort_flag) {
+          ok = false;
+          break;
+        }
+        const int tile = tq[slot];
+        mbar_arrive(&tq_empty[slot]);
+        if (tile < 0) break;
         if (!mbar_wait(&tempty[acc], acc_ph ^ 1u, p.err) || *abort_flag) {
           ok = false;
           break;
@@ -272,7 +309,13 @@ __global__ void __launch_bounds__(THREADS, 1)
                         (EPI != EPI_RESIDUAL || (((p.ldr & 7) == 0) && ((reinterpret_cast<uintptr_t>(p.R) & 15) == 0)));
     int acc = 0;
     uint32_t acc_ph = 0;
-    for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x) {
+    for (int i = 0;; ++i) {
+      const int slot = i & (TQ - 1);
+      if (!warp_wait(&tq_full[slot], static_cast<uint32_t>((i / TQ) & 1), p.err)) break;
+      const int tile = tq[slot];
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tq_empty[slot]);
+      if (tile < 0) break;
       if (!warp_wait(&tfull[acc], acc_ph, p.err)) break;
       tc_fence_after();
       int m_blk, n_blk;
@@ -284,12 +327,22 @@ __global__ void __launch_bounds__(THREADS, 1)
     }
   }
 
+  if (p.sys_fence) __threadfence_system();   // peer stores performed before the kernel completes
   __syncthreads();
   if (warp == 2) {
     // All MMAs must have completed before the accumulators are released (they have, unless a wait ran out).
     mbar_wait(mma_done, 0, p.err);
     tc_fence_after();
     tmem_dealloc(tmem_base, TMEM_COLS);
+  }
+  if (threadIdx.x == 0) {
+    // Every CTA has finished claiming once all have counted themselves out; the last one re-zeroes the counter
+    // for the next launch on this stream (on every path, the ones that gave up included).
+    __threadfence();
+    if (atomicAdd(p.sched + 1, 1u) == gridDim.x - 1) {
+      atomicExch(p.sched, 0u);
+      atomicExch(p.sched + 1, 0u);
+    }
   }
 }
 
@@ -485,6 +538,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     }
   }
 
+  if (p.sys_fence) __threadfence_system();   // peer stores performed before the kernel completes
   __syncthreads();
   if (warp == 2) {
     mbar_wait(mma_done, 0, p.err);   // every pair MMA has completed (this CTA's TMEM included)
@@ -591,6 +645,30 @@ static int launch_pair_t(const CUtensorMap& ma, const CUtensorMap& mb, const Par
   return check_launch("gemm_tc2_kernel");
 }
 
+// Tile counters of the 1-SM kernel, one pair per (device, stream): launches on one stream run one after another,
+// and each leaves its counter at zero for the next.
+static unsigned* sched_counter(cudaStream_t st) {
+  static std::mutex mu;
+  static std::map<std::pair<int, cudaStream_t>, unsigned*> counters;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) {
+    fail("gemm: no current CUDA device");
+    return nullptr;
+  }
+  std::lock_guard<std::mutex> lock(mu);
+  const auto key = std::make_pair(dev, st);
+  const auto it = counters.find(key);
+  if (it != counters.end()) return it->second;
+  unsigned* c = nullptr;
+  if (cudaMalloc(&c, 2 * sizeof(unsigned)) != cudaSuccess ||
+      cudaMemsetAsync(c, 0, 2 * sizeof(unsigned), st) != cudaSuccess) {
+    fail("gemm: cannot set up the tile counter");
+    return nullptr;
+  }
+  counters[key] = c;
+  return c;
+}
+
 static int g_pair_mode = 1;   // 1: use the 2-SM kernel for M > 128; 0: always the 1-SM kernel
 
 int set_pair_mode(int on) {
@@ -599,7 +677,7 @@ int set_pair_mode(int on) {
 }
 
 int gemm_tc(const void* A, int64_t lda, const void* B, int64_t ldb, void* C, int64_t ldc, const void* R,
-            int64_t ldr, int64_t M, int64_t N, int64_t K, int64_t n_out, int epi, cudaStream_t stream) {
+            int64_t ldr, int64_t M, int64_t N, int64_t K, int64_t n_out, int epi, bool sys_fence, cudaStream_t stream) {
   if (M <= 0 || N <= 0 || n_out <= 0) return 0;
   if (M > INT32_MAX / 2 || N > INT32_MAX / 2 || K > INT32_MAX / 2) return fail("gemm: dimension too large");
   CUtensorMap ma, mb;
@@ -617,6 +695,8 @@ int gemm_tc(const void* A, int64_t lda, const void* B, int64_t ldb, void* C, int
   const int num_n_blocks = static_cast<int>((n_out + n_tile - 1) / n_tile);
   p.num_tiles = p.num_m_blocks * num_n_blocks;
   p.k_blocks = static_cast<int>((K + BK - 1) / BK);
+  p.sys_fence = sys_fence ? 1 : 0;
+  p.sched = nullptr;
   p.err = error_word();
   if (!p.err) return -1;
   if (g_pair_mode && M > BM) {
@@ -630,6 +710,8 @@ int gemm_tc(const void* A, int64_t lda, const void* B, int64_t ldb, void* C, int
       default: return fail("gemm: unknown epilogue");
     }
   }
+  p.sched = sched_counter(stream);
+  if (!p.sched) return -1;
   const int grid = p.num_tiles < sm_count() ? p.num_tiles : sm_count();
   switch (epi) {
     case EPI_STORE: return launch_t<EPI_STORE>(ma, mb, p, grid, stream);

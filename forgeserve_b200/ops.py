@@ -114,6 +114,50 @@ def linear(x: torch.Tensor, w: torch.Tensor, epilogue: int = L.FS_EPI_STORE, res
     return out
 
 
+def linear_to(x: torch.Tensor, w: torch.Tensor, c_ptr: int, ldc: int, system_fence: bool = False) -> None:
+    """x (..., K) @ w (N, K)^T stored at device address c_ptr, rows of ldc elements apart (no residual, no
+    SwiGLU). c_ptr may be another GPU's buffer mapped with ipc_open; system_fence=True then makes the kernel end
+    with a system-scope fence, so its stores are performed by the time the kernel completes."""
+    require_cuda(x, w)
+    if w.dtype != x.dtype or w.dim() != 2 or w.stride(1) != 1 or w.shape[1] != x.shape[-1]:
+        raise ValueError("linear_to: weight must be (N, K) with contiguous rows, in the input's dtype")
+    M, lda = _rows(x)
+    N, K = w.shape
+    if ldc < N:
+        raise ValueError("linear_to: output row stride smaller than N")
+    epi = L.FS_EPI_STORE | (L.FS_EPI_SYSTEM_FENCE if system_fence else 0)
+    ev = gemm_events
+    if ev is not None:
+        st = torch.cuda.current_stream(x.device)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(st)
+    L.check(L.load().fs_gemm(_p(x), lda, _p(w), w.stride(0), ctypes.c_void_p(c_ptr), ldc, None, 0, M, N, K, N, epi,
+                             dtype_code(x.dtype), _stream(x)), "fs_gemm")
+    if ev is not None:
+        e1.record(st)
+        ev.append((e0, e1, 2.0 * M * N * K))
+
+
+def ipc_handle(t: torch.Tensor) -> bytes:
+    """CUDA IPC handle of the allocation holding t, followed by t's byte offset in it (8 bytes, little-endian)."""
+    require_cuda(t)
+    h = (ctypes.c_char * L.FS_IPC_HANDLE_BYTES)()
+    off = ctypes.c_int64()
+    L.check(L.load().fs_ipc_handle(_p(t), h, ctypes.byref(off)), "fs_ipc_handle")
+    return bytes(h) + int(off.value).to_bytes(8, "little", signed=True)
+
+
+def ipc_open(handle: bytes) -> int:
+    """Map another process's allocation (the first FS_IPC_HANDLE_BYTES bytes of an ipc_handle); returns its base."""
+    base = ctypes.c_void_p()
+    L.check(L.load().fs_ipc_open(handle[: L.FS_IPC_HANDLE_BYTES], ctypes.byref(base)), "fs_ipc_open")
+    return int(base.value)
+
+
+def ipc_close(base: int) -> None:
+    L.check(L.load().fs_ipc_close(ctypes.c_void_p(base)), "fs_ipc_close")
+
+
 def rope_kv_write(qkv: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor, positions: torch.Tensor,
                   kv: L.KVCacheDesc, B: int, T: int, nh: int, nkv: int, hd: int, slot_base: int, slot_from_pos: bool,
                   apply_rope: bool = True) -> None:

@@ -42,6 +42,58 @@ def bubble_fraction(stages: int, microbatches: int) -> float:
     return (stages - 1) / (microbatches + stages - 1)
 
 
+HEAD_TILE = 256   # output columns of one GEMM tile: head slices start and end on tile edges
+
+
+def head_bounds(vocab: int, size: int) -> List[Tuple[int, int]]:
+    """Vocab range [lo, hi) of each stage's slice of a split output head: whole 256-column GEMM tiles, as even as
+    possible (earlier stages take the extra tiles); the ranges cover [0, vocab) in order."""
+    tiles = -(-vocab // HEAD_TILE)
+    base, extra = divmod(tiles, size)
+    bounds, at = [], 0
+    for r in range(size):
+        n = base + (r < extra)
+        bounds.append((min(at * HEAD_TILE, vocab), min((at + n) * HEAD_TILE, vocab)))
+        at += n
+    return bounds
+
+
+def split_head_program(rank: int, size: int, microbatches: int) -> List[Tuple[str, int]]:
+    """Host order of one stage's work in pipeline_forward when the output head is split over the stages.
+
+    ("recv", i) / ("send", i): post the receive of micro-batch i's activation from the previous stage / its send
+    to the next; ("bcast", j): post the broadcast of micro-batch j's normalised hidden state (the last stage
+    sends, the others receive); ("layers", i): the stage's layers on micro-batch i (the last stage then applies
+    the final norm); ("head", j): this stage's vocab slice of micro-batch j's logits.
+
+    Stage s runs micro-batch i in slot i + s of the GPipe schedule, so the last stage's broadcast of j (after its
+    layers on j, slot j + p - 1) arrives while stage s runs micro-batch j + p - 1 - s: stage s posts it before
+    that micro-batch and takes j's head slice after it; slices whose input comes after the stage's last
+    micro-batch run at the end, in the drain. Every rank posts its communication in one global order (a
+    stage's send of micro-batch i and the last stage's broadcast, ends of slots, ordered by slot and then by
+    stage from last to first), which NCCL needs when several communicators share a GPU: their kernels are not
+    guaranteed to run at the same time, so a rank that posted them in another order could wait forever."""
+    m, p, s = microbatches, size, rank
+    out: List[Tuple[str, int]] = []
+    for i in range(m):
+        if s > 0:
+            out.append(("recv", i))
+        j = i + s + 1 - p
+        if s < p - 1 and j >= 0:
+            out.append(("bcast", j))
+        out.append(("layers", i))
+        if s < p - 1:
+            out.append(("send", i))
+            if j >= 0:
+                out.append(("head", j))
+        else:
+            out += [("bcast", i), ("head", i)]
+    if s < p - 1:
+        for j in range(max(0, m + s + 1 - p), m):
+            out += [("bcast", j), ("head", j)]
+    return out
+
+
 def microbatch_sizes(batch: int, microbatches: int) -> List[int]:
     """Row counts of torch.arange(batch).tensor_split(microbatches): the first batch % m parts get one extra."""
     base, extra = divmod(batch, microbatches)
@@ -74,6 +126,7 @@ class PipelineStage(nn.Module):
         self.register_buffer("rope_sin", self._rope.sin.to(device), persistent=False)
         self.transport = transport if transport is not None else default_transport()
         self.trace: Optional[List] = None   # set to a list to record (mb, start, end) CUDA events per micro-batch
+        self.head_split: Optional[_HeadSplit] = None   # see split_head_
 
     @property
     def device(self) -> torch.device:
@@ -95,6 +148,32 @@ class PipelineStage(nn.Module):
                                                                   and self.is_last):
                 own[name] = w
         self.load_state_dict(own)
+        hs = self.head_split
+        if hs is not None and not self.is_last and "lm_head.weight" in full:
+            hs.weight.copy_(full["lm_head.weight"][hs.lo : hs.hi])
+
+    def split_head_(self) -> None:
+        """Spread the output head over all stages. Collective: every stage calls it once its weights are set.
+
+        Each stage then keeps the lm_head rows of its vocab range (head_bounds). In pipeline_forward with logits
+        for every position, the last stage broadcasts each micro-batch's normalised hidden state and every stage
+        computes its slice of the logits, the other stages storing it straight into the last stage's output over
+        NVLink. The logits are the same (bit for bit) as with the whole head on the last stage; they are still
+        returned on the last stage only. This evens out the stages: with the whole head, the last stage carries
+        the head GEMM (2 * d_model * vocab FLOP per token) on top of its layers and sets the pace of the pipeline.
+        Needs one process per GPU with an NCCL process group."""
+        import torch.distributed as dist
+        from .transport import DistTransport
+        if not (isinstance(self.transport, DistTransport) and dist.is_initialized()
+                and dist.get_backend() == "nccl" and self.size > 1):
+            raise RuntimeError("split_head_ needs one process per GPU and an NCCL process group of 2 or more ranks")
+        hs = _HeadSplit(self)
+        cfg = self.cfg
+        full = self.lm_head.weight.data if self.is_last else torch.empty(
+            cfg.vocab_size, cfg.d_model, dtype=self.dtype, device=self.device)
+        dist.broadcast(full, src=self.size - 1, group=hs.group)
+        hs.weight = full[hs.lo : hs.hi] if self.is_last else full[hs.lo : hs.hi].clone()
+        self.head_split = hs
 
     def _rope_tables(self):
         return self._rope.on(self.device)
@@ -117,6 +196,33 @@ class PipelineStage(nn.Module):
 
     def head(self, x: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
         return ops.linear(ops.rmsnorm(x, self.norm.weight, self.norm.eps), self.lm_head.weight, out=out)
+
+
+class _HeadSplit:
+    """A stage's part of the split output head: its vocab range and lm_head rows, the communicator the last stage
+    broadcasts on, and this process's mappings of the last stage's logits buffers."""
+
+    MAX_MAPS = 4
+
+    def __init__(self, stage: "PipelineStage"):
+        from .transport import head_group
+        self.group = head_group()
+        self.lo, self.hi = head_bounds(stage.cfg.vocab_size, stage.size)[stage.rank]
+        self.weight: Optional[torch.Tensor] = None
+        self.side = torch.cuda.Stream(stage.device)
+        self.maps: Dict[bytes, int] = {}   # IPC handle -> mapped base address, oldest first
+
+    def logits_address(self, handle: bytes) -> int:
+        key = bytes(handle[: ops.L.FS_IPC_HANDLE_BYTES])
+        base = self.maps.pop(key, None)
+        if base is None:
+            if len(self.maps) >= self.MAX_MAPS:   # drop the oldest mapping once no queued work can still use it
+                torch.cuda.synchronize(self.side.device)
+                old = next(iter(self.maps))
+                ops.ipc_close(self.maps.pop(old))
+            base = ops.ipc_open(key)
+        self.maps[key] = base
+        return base + int.from_bytes(bytes(handle[ops.L.FS_IPC_HANDLE_BYTES :]), "little", signed=True)
 
 
 class PipelineState:
@@ -163,7 +269,8 @@ def pipeline_forward(stage: PipelineStage, state: PipelineState, idx: Optional[t
     d = cfg.d_model
     act_dtype = stage.dtype
     recvs = {}
-    if not stage.is_first and all(state.sizes):
+    split = stage.head_split is not None and not last_only
+    if not stage.is_first and all(state.sizes) and not split:
         for mb, size in enumerate(state.sizes):
             buf = torch.empty(size, t, d, dtype=act_dtype, device=dev)
             recvs[mb] = (tr.irecv(buf, stage.rank - 1), buf)
@@ -182,6 +289,11 @@ def pipeline_forward(stage: PipelineStage, state: PipelineState, idx: Optional[t
         # The reference fails on a zero-row micro-batch (its attention reshapes an empty tensor,
         # forgeserve/model.py:77); refuse up front, on every stage, instead of part-way through.
         raise RuntimeError(f"more micro-batches ({len(state.sizes)}) than batch rows ({batch})")
+    if split:
+        _forward_split_head(stage, state, idx, t, start, out)
+        if not state.caches[0]:
+            state._length = start + t
+        return out
     sends, row = [], 0
     for mb, size in enumerate(state.sizes):
         if stage.is_first:
@@ -207,6 +319,91 @@ def pipeline_forward(stage: PipelineStage, state: PipelineState, idx: Optional[t
     if not state.caches[0]:
         state._length = start + t
     return out
+
+
+def _forward_split_head(stage: PipelineStage, state: PipelineState, idx: Optional[torch.Tensor], t: int,
+                        start: int, out: Optional[torch.Tensor]) -> None:
+    """pipeline_forward with the output head split over the stages (PipelineStage.split_head_), in the host order
+    of split_head_program."""
+    import torch.distributed as dist
+    cfg, hs, tr = stage.cfg, stage.head_split, stage.transport
+    dev, p, r = stage.device, stage.size, stage.rank
+    sizes = state.sizes
+    rows0 = [sum(sizes[:j]) for j in range(len(sizes))]
+    V, elt = cfg.vocab_size, torch.tensor([], dtype=stage.dtype).element_size()
+    stream = torch.cuda.current_stream(dev)
+    # Where the last stage's logits are: its IPC handle, broadcast on a side stream so that no queued compute is
+    # waited for (the receivers block on the host until it arrives).
+    with torch.cuda.stream(hs.side):
+        if stage.is_last:
+            hb = torch.frombuffer(bytearray(ops.ipc_handle(out)), dtype=torch.uint8).to(dev)
+        else:
+            hb = torch.empty(ops.L.FS_IPC_HANDLE_BYTES + 8, dtype=torch.uint8, device=dev)
+        dist.broadcast(hb, src=p - 1, group=hs.group)
+        logits_at = None if stage.is_last else hs.logits_address(bytes(hb.cpu().tolist()))
+    acts: Dict[int, Tuple] = {}
+    xn: Dict[int, Tuple] = {}
+    sends, keep = [], []
+
+    def mark():
+        if stage.trace is None:
+            return None
+        e = torch.cuda.Event(enable_timing=True)
+        e.record(stream)
+        return e
+
+    for kind, j in split_head_program(r, p, len(sizes)):
+        rows = slice(rows0[j], rows0[j] + sizes[j])
+        if kind == "recv":
+            # Posted from the side stream (the transfer does not wait for queued compute); the buffer comes from
+            # that stream's pool and is marked as used by the compute stream.
+            with torch.cuda.stream(hs.side):
+                buf = torch.empty(sizes[j], t, cfg.d_model, dtype=stage.dtype, device=dev)
+                acts[j] = (tr.irecv(buf, r - 1), buf)
+            buf.record_stream(stream)
+        elif kind == "layers":
+            if stage.is_first:
+                x = stage.embed(idx[rows])
+            else:
+                work, x = acts.pop(j)
+                work.wait()
+            e0 = mark()
+            stage.run_layers_(x, _positions(start, t, sizes[j], dev), state.caches[j])
+            if stage.is_last:
+                xn[j] = (None, ops.rmsnorm(x, stage.norm.weight, stage.norm.eps))
+            else:
+                acts[j] = (None, x)
+            if e0 is not None:
+                stage.trace.append((j, e0, mark()))
+        elif kind == "send":
+            sends.append(tr.isend(acts.pop(j)[1], r + 1))
+        elif kind == "bcast":
+            if stage.is_last:
+                h = xn[j][1]
+            else:
+                h = torch.empty(sizes[j], t, cfg.d_model, dtype=stage.dtype, device=dev)
+            xn[j] = (dist.broadcast(h, src=p - 1, group=hs.group, async_op=True), h)
+        else:
+            work, h = xn.pop(j)
+            if not stage.is_last:
+                work.wait()
+            keep.append(h)
+            if hs.hi > hs.lo:
+                e0 = mark()
+                if stage.is_last:
+                    ops.linear(h, hs.weight, out=out[rows, :, hs.lo : hs.hi])
+                else:
+                    ops.linear_to(h, hs.weight, logits_at + (rows0[j] * t * V + hs.lo) * elt, V, system_fence=True)
+                if e0 is not None:
+                    stage.trace.append((j, e0, mark()))
+    # Every stage reports once its slices are written; the last stage's stream waits for all of them before the
+    # logits are used.
+    done = torch.zeros(1, dtype=torch.float32, device=dev)
+    work = dist.all_reduce(done, group=hs.group, async_op=True)
+    if stage.is_last:
+        work.wait()
+    for w in sends:
+        w.wait()
 
 
 @torch.no_grad()

@@ -48,6 +48,24 @@ _PAIR_GROUPS: Dict[int, list] = {}
 COMM_SMS = int(os.environ.get("FORGESERVE_COMM_SMS", "12"))
 
 
+# The split output head (pipeline.py) uses one more communicator over all ranks: the last stage broadcasts each
+# micro-batch's normalised hidden state on it, and every stage reports there when its logits slices are written.
+# Its kernels are kept to a few CTAs, like the point-to-point ones, so they fit beside the persistent GEMM.
+_HEAD_GROUPS: Dict[int, object] = {}
+HEAD_CTAS = int(os.environ.get("FORGESERVE_HEAD_CTAS", "8"))
+
+
+def head_group():
+    world = dist.get_world_size()
+    if world not in _HEAD_GROUPS:
+        opts = None
+        if dist.get_backend() == "nccl":
+            opts = dist.ProcessGroupNCCL.Options()
+            opts.config.max_ctas = HEAD_CTAS
+        _HEAD_GROUPS[world] = dist.new_group(list(range(world)), pg_options=opts)
+    return _HEAD_GROUPS[world]
+
+
 def _pair_groups():
     world = dist.get_world_size()
     if world not in _PAIR_GROUPS:

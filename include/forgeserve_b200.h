@@ -21,6 +21,10 @@ extern "C" {
 
 enum { FS_F32 = 0, FS_BF16 = 1 };
 enum { FS_EPI_STORE = 0, FS_EPI_RESIDUAL = 1, FS_EPI_SWIGLU = 2 };
+/* ORed into fs_gemm's epilogue: C may be another GPU's memory (mapped with fs_ipc_open); every CTA of the
+ * tensor-core kernel ends with a system-scope fence, so the stores are performed before the kernel completes. */
+enum { FS_EPI_SYSTEM_FENCE = 0x100 };
+enum { FS_IPC_HANDLE_BYTES = 64 };
 enum { FS_ERR_WAIT_TIMEOUT = 1, FS_ERR_BAD_TOKEN = 2, FS_ERR_BAD_SLOT = 4, FS_ERR_BAD_POSITION = 8 };
 
 /* Library version (major*10000 + minor*100 + patch). */
@@ -43,6 +47,18 @@ int fs_set_persistent_sms(int n);
 /* on != 0 (default): bf16 GEMMs with M > 128 run on CTA pairs (tcgen05 cta_group::2, 256 x 256 tiles); 0: always on
  * single CTAs (128 x 256 tiles). Process-wide. For comparing the two kernels. No counterpart in the reference. */
 int fs_set_gemm_pair_mode(int on);
+
+/* Inter-process mapping of a device buffer, so that pipeline stages (one process per GPU) can write their vocab
+ * slice of the output head straight into the last stage's logits tensor over NVLink. No counterpart in the
+ * reference (its stages are CPU processes that exchange tensors through gloo; pipeline.py:112-118 computes the
+ * whole head on the last stage).
+ * fs_ipc_handle: the CUDA IPC handle (FS_IPC_HANDLE_BYTES bytes, written to `handle`) of the device allocation
+ *   that holds `ptr`, and ptr's byte offset inside that allocation.
+ * fs_ipc_open: maps another process's allocation into this one (peer access enabled); *base is the allocation's
+ *   start as seen from the current device. A process maps a given allocation once; fs_ipc_close unmaps it. */
+int fs_ipc_handle(const void* ptr, void* handle, int64_t* offset);
+int fs_ipc_open(const void* handle, void** base);
+int fs_ipc_close(void* base);
 
 /* RMSNorm over rows: y = T(T(x * rsqrt(mean(x^2) + eps)) * w), fp32 statistics.
  * Replaces RMSNorm.forward, forgeserve/model.py:29-31. y may alias x. */

@@ -88,6 +88,39 @@ def test_nccl_two_gpu_pipeline_matches_reference():
         assert torch.equal(out, g["generate"])
 
 
+def split_head_worker(rank, size, cfg_dict, batch, t, microbatches):
+    from forgeserve_b200 import _lib
+    from forgeserve_b200.weights import init_stage_
+    cfg = ModelConfig(**cfg_dict)
+    stage = PipelineStage(cfg, rank, size, dtype=torch.bfloat16).eval()
+    init_stage_(stage, seed=11, std=0.05)
+    idx = torch.randint(0, cfg.vocab_size, (batch, t), generator=torch.Generator().manual_seed(3))
+
+    def run():
+        state = PipelineState(stage, batch, microbatches)
+        out = pipeline_forward(stage, state, idx if rank == 0 else None, t)
+        return None if out is None else out.cpu()
+
+    whole = run()
+    stage.split_head_()
+    split, again = run(), run()   # the second call reuses the mapping of the last stage's logits
+    return whole, split, again, _lib.device_error(clear=True)
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+@pytest.mark.parametrize("microbatches", [1, 3])
+def test_nccl_split_head_matches_whole_head(microbatches):
+    """Head slices computed on every stage and stored into the last stage's logits over NVLink give the same
+    logits, bit for bit, as the whole head on the last stage (ragged last slice: vocab 1000 = 3 x 256 + 232)."""
+    cfg = dict(vocab_size=1000, d_model=256, n_layers=4, n_heads=4, n_kv_heads=2, max_seq_len=128)
+    res = run_distributed(split_head_worker, 2, cfg, 6, 64, microbatches, backend="nccl", timeout=300)
+    assert res[0][:3] == (None, None, None)
+    whole, split, again, err = res[1]
+    assert whole.shape == (6, 64, 1000) and torch.isfinite(whole.float()).all()
+    assert torch.equal(whole, split) and torch.equal(whole, again)
+    assert err == 0 and res[0][3] == 0
+
+
 def test_8b_shape_layer_bf16_against_oracle():
     """One 8B-shape decoder layer (d 4096, 32/8 heads, ffn 14336, theta 5e5) at B=1, T=1024 in bf16, against the
     oracle's fp32 layer on the same bf16 weights (run on the GPU with plain torch as the checker)."""
