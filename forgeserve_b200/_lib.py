@@ -47,6 +47,7 @@ SIGNATURES = {
     "fs_ipc_handle": (c_int, [c_vp, c_vp, ctypes.POINTER(c_i64)]),
     "fs_ipc_open": (c_int, [c_vp, ctypes.POINTER(c_vp)]),
     "fs_ipc_close": (c_int, [c_vp]),
+    "fs_copy_2d": (c_int, [c_vp, c_i64, c_vp, c_i64, c_i64, c_i64, c_vp]),
     "fs_rmsnorm": (c_int, [c_vp, c_i64, c_vp, c_vp, c_i64, c_i64, c_i64, c_float, c_int, c_vp]),
     "fs_gemm": (c_int, [c_vp, c_i64, c_vp, c_i64, c_vp, c_i64, c_vp, c_i64, c_i64, c_i64, c_i64, c_i64, c_int, c_int,
                         c_vp]),

@@ -148,6 +148,18 @@ int fs_ipc_open(const void* handle, void** base) {
   return 0;
 }
 
+int fs_copy_2d(void* dst, int64_t dpitch, const void* src, int64_t spitch, int64_t width, int64_t height,
+               void* stream) {
+  if (width <= 0 || height <= 0) return 0;
+  if (!dst || !src) return fail("fs_copy_2d: NULL pointer");
+  if (dpitch < width || spitch < width) return fail("fs_copy_2d: pitch smaller than the row width");
+  const cudaError_t e = cudaMemcpy2DAsync(dst, static_cast<size_t>(dpitch), src, static_cast<size_t>(spitch),
+                                          static_cast<size_t>(width), static_cast<size_t>(height), cudaMemcpyDefault,
+                                          static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return fail(std::string("fs_copy_2d: cudaMemcpy2DAsync: ") + cudaGetErrorString(e));
+  return 0;
+}
+
 int fs_ipc_close(void* base) {
   if (!base) return fail("fs_ipc_close: NULL pointer");
   const cudaError_t e = cudaIpcCloseMemHandle(base);

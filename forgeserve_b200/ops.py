@@ -154,6 +154,16 @@ def ipc_open(handle: bytes) -> int:
     return int(base.value)
 
 
+def copy_2d_to(dst_ptr: int, dpitch: int, src: torch.Tensor) -> None:
+    """Copy the rows of a 2-D view `src` (last dim contiguous) to device address dst_ptr, rows dpitch bytes apart,
+    on the current stream by the copy engine (dst_ptr may be another GPU's buffer mapped with ipc_open)."""
+    require_cuda(src)
+    rows, ld = _rows(src)
+    width = src.shape[-1] * src.element_size()
+    L.check(L.load().fs_copy_2d(ctypes.c_void_p(dst_ptr), int(dpitch), _p(src), ld * src.element_size(), width, rows,
+                                _stream(src)), "fs_copy_2d")
+
+
 def ipc_close(base: int) -> None:
     L.check(L.load().fs_ipc_close(ctypes.c_void_p(base)), "fs_ipc_close")
 

@@ -152,16 +152,23 @@ class PipelineStage(nn.Module):
         if hs is not None and not self.is_last and "lm_head.weight" in full:
             hs.weight.copy_(full["lm_head.weight"][hs.lo : hs.hi])
 
-    def split_head_(self) -> None:
+    def split_head_(self, transfer: str = "copy") -> None:
         """Spread the output head over all stages. Collective: every stage calls it once its weights are set.
 
         Each stage then keeps the lm_head rows of its vocab range (head_bounds). In pipeline_forward with logits
         for every position, the last stage broadcasts each micro-batch's normalised hidden state and every stage
-        computes its slice of the logits, the other stages storing it straight into the last stage's output over
-        NVLink. The logits are the same (bit for bit) as with the whole head on the last stage; they are still
-        returned on the last stage only. This evens out the stages: with the whole head, the last stage carries
-        the head GEMM (2 * d_model * vocab FLOP per token) on top of its layers and sets the pace of the pipeline.
-        Needs one process per GPU with an NCCL process group."""
+        computes its slice of the logits into the last stage's output over NVLink. The logits are the same (bit
+        for bit) as with the whole head on the last stage; they are still returned on the last stage only. This
+        evens out the stages: with the whole head, the last stage carries the head GEMM (2 * d_model * vocab FLOP
+        per token) on top of its layers and sets the pace of the pipeline.
+
+        transfer="copy": a stage computes its slice locally and the copy engine moves it (rows of the slice are
+        contiguous runs of the output) on a side stream, overlapped with the stage's next work. "store": the GEMM
+        epilogue stores the slice straight into the last stage's memory (fewer HBM bytes, but the SMs wait on
+        NVLink: every thread stores 64-byte pieces of different rows). Needs one process per GPU with an NCCL
+        process group."""
+        if transfer not in ("copy", "store"):
+            raise ValueError("transfer must be 'copy' or 'store'")
         import torch.distributed as dist
         from .transport import DistTransport
         if not (isinstance(self.transport, DistTransport) and dist.is_initialized()
@@ -173,6 +180,7 @@ class PipelineStage(nn.Module):
             cfg.vocab_size, cfg.d_model, dtype=self.dtype, device=self.device)
         dist.broadcast(full, src=self.size - 1, group=hs.group)
         hs.weight = full[hs.lo : hs.hi] if self.is_last else full[hs.lo : hs.hi].clone()
+        hs.peer_store = transfer == "store"
         self.head_split = hs
 
     def _rope_tables(self):
@@ -209,7 +217,9 @@ class _HeadSplit:
         self.group = head_group()
         self.lo, self.hi = head_bounds(stage.cfg.vocab_size, stage.size)[stage.rank]
         self.weight: Optional[torch.Tensor] = None
+        self.peer_store = False
         self.side = torch.cuda.Stream(stage.device)
+        self.copy = torch.cuda.Stream(stage.device)
         self.maps: Dict[bytes, int] = {}   # IPC handle -> mapped base address, oldest first
 
     def logits_address(self, handle: bytes) -> int:
@@ -390,14 +400,22 @@ def _forward_split_head(stage: PipelineStage, state: PipelineState, idx: Optiona
             keep.append(h)
             if hs.hi > hs.lo:
                 e0 = mark()
+                dst = None if stage.is_last else logits_at + (rows0[j] * t * V + hs.lo) * elt
                 if stage.is_last:
                     ops.linear(h, hs.weight, out=out[rows, :, hs.lo : hs.hi])
+                elif hs.peer_store:
+                    ops.linear_to(h, hs.weight, dst, V, system_fence=True)
                 else:
-                    ops.linear_to(h, hs.weight, logits_at + (rows0[j] * t * V + hs.lo) * elt, V, system_fence=True)
+                    part = ops.linear(h, hs.weight)
+                    hs.copy.wait_stream(stream)
+                    with torch.cuda.stream(hs.copy):
+                        ops.copy_2d_to(dst, V * elt, part)
+                    part.record_stream(hs.copy)
                 if e0 is not None:
                     stage.trace.append((j, e0, mark()))
-    # Every stage reports once its slices are written; the last stage's stream waits for all of them before the
-    # logits are used.
+    # Every stage reports once its slices are written (copies included); the last stage's stream waits for all of
+    # them before the logits are used.
+    stream.wait_stream(hs.copy)
     done = torch.zeros(1, dtype=torch.float32, device=dev)
     work = dist.all_reduce(done, group=hs.group, async_op=True)
     if stage.is_last:

@@ -60,6 +60,13 @@ int fs_ipc_handle(const void* ptr, void* handle, int64_t* offset);
 int fs_ipc_open(const void* handle, void** base);
 int fs_ipc_close(void* base);
 
+/* Copies `height` rows of `width` bytes from src (rows spitch bytes apart) to dst (rows dpitch bytes apart) on
+ * `stream`, by the copy engine (no SM takes part). Either side may be another GPU's memory mapped with
+ * fs_ipc_open: a stage moves its slice of the split head's logits into the last stage's output this way.
+ * No counterpart in the reference. */
+int fs_copy_2d(void* dst, int64_t dpitch, const void* src, int64_t spitch, int64_t width, int64_t height,
+               void* stream);
+
 /* RMSNorm over rows: y = T(T(x * rsqrt(mean(x^2) + eps)) * w), fp32 statistics.
  * Replaces RMSNorm.forward, forgeserve/model.py:29-31. y may alias x. */
 int fs_rmsnorm(const void* x, int64_t x_stride, const void* w, void* y, int64_t y_stride, int64_t rows, int64_t dim,

@@ -88,7 +88,7 @@ def test_nccl_two_gpu_pipeline_matches_reference():
         assert torch.equal(out, g["generate"])
 
 
-def split_head_worker(rank, size, cfg_dict, batch, t, microbatches):
+def split_head_worker(rank, size, cfg_dict, batch, t, microbatches, transfer):
     from forgeserve_b200 import _lib
     from forgeserve_b200.weights import init_stage_
     cfg = ModelConfig(**cfg_dict)
@@ -102,18 +102,19 @@ def split_head_worker(rank, size, cfg_dict, batch, t, microbatches):
         return None if out is None else out.cpu()
 
     whole = run()
-    stage.split_head_()
+    stage.split_head_(transfer)
     split, again = run(), run()   # the second call reuses the mapping of the last stage's logits
     return whole, split, again, _lib.device_error(clear=True)
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-@pytest.mark.parametrize("microbatches", [1, 3])
-def test_nccl_split_head_matches_whole_head(microbatches):
-    """Head slices computed on every stage and stored into the last stage's logits over NVLink give the same
-    logits, bit for bit, as the whole head on the last stage (ragged last slice: vocab 1000 = 3 x 256 + 232)."""
+@pytest.mark.parametrize("microbatches,transfer", [(1, "copy"), (3, "copy"), (3, "store")])
+def test_nccl_split_head_matches_whole_head(microbatches, transfer):
+    """Head slices computed on every stage and moved into the last stage's logits over NVLink (by the copy
+    engine, or stored by the GEMM epilogue) give the same logits, bit for bit, as the whole head on the last
+    stage (ragged last slice: vocab 1000 = 3 x 256 + 232)."""
     cfg = dict(vocab_size=1000, d_model=256, n_layers=4, n_heads=4, n_kv_heads=2, max_seq_len=128)
-    res = run_distributed(split_head_worker, 2, cfg, 6, 64, microbatches, backend="nccl", timeout=300)
+    res = run_distributed(split_head_worker, 2, cfg, 6, 64, microbatches, transfer, backend="nccl", timeout=300)
     assert res[0][:3] == (None, None, None)
     whole, split, again, err = res[1]
     assert whole.shape == (6, 64, 1000) and torch.isfinite(whole.float()).all()
