@@ -10,9 +10,10 @@
 //   warp 5      MMA issuer (one thread): S_j = Q K_j^T into one of two TMEM buffers; O += P_{j-1} V_{j-1} with
 //               P read from TMEM and V from shared memory (MN-major operand)
 //   warps 0-3   softmax, one thread per query row: S row from TMEM, causal mask, running max in the log2
-//               domain, P = exp2(S - m) packed to bf16 into TMEM; O rescaled in TMEM only when the running max
-//               grows by more than 2^8 (otherwise the stale max is kept, bounding P by 2^8); final O / l to global
-// TMEM: S0 [0,128) S1 [128,256) P [256,320) O [384, 384+hd). Every wait is bounded (common.cuh).
+//               domain, P = exp2(S - m) packed to bf16 into TMEM (two P buffers, so P_j is written while
+//               P_{j-1} V_{j-1} runs); O rescaled in TMEM only when the running max grows by more than 2^8
+//               (otherwise the stale max is kept, bounding P by 2^8); final O / l to global
+// TMEM: S0 [0,128) S1 [128,256) P0 [256,320) P1 [320,384) O [384, 384+hd). Every wait is bounded (common.cuh).
 // No TMA multicast (the kernel also runs in multi-GPU jobs).
 #include <cudaTypedefs.h>
 
@@ -99,6 +100,13 @@ __device__ __forceinline__ uint64_t sw128_mnmajor_desc(uint32_t smem_addr, uint3
   d |= static_cast<uint64_t>(1u) << 46;
   d |= static_cast<uint64_t>(2u) << 61;
   return d;
+}
+
+// 2^x by the MUFU instruction (ex2.approx, flushes subnormal results to zero); x <= 8 here.
+__device__ __forceinline__ float exp2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
 }
 
 __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
@@ -289,7 +297,7 @@ __global__ void __launch_bounds__(THREADS, 1)
 #pragma unroll
         for (int kk = 0; kk < BN / 16; ++kk) {
           const uint64_t bdesc = sw128_mnmajor_desc(v_addr + kk * 2048u, G::KV_PANEL);
-          mma_ts(tmem + O_COL, tmem + P_COL + kk * 8, bdesc, G::IDESC_O, (j | kk) != 0);
+          mma_ts(tmem + O_COL, tmem + P_COL + (j & 1) * (BN / 2) + kk * 8, bdesc, G::IDESC_O, (j | kk) != 0);
         }
         tc_commit(pv_done);
         tc_commit(&v_empty[vs]);
@@ -306,8 +314,12 @@ __global__ void __launch_bounds__(THREADS, 1)
     }
   } else {
     // ------------------------------------------------------------------------------------------ softmax
+    // One thread per query row. S_j is read from TMEM twice, 32 columns at a time (pass 1: row max; pass 2:
+    // P = exp2(S * scale - m), stored to P buffer j & 1 chunk by chunk), so the loops stay rolled and short and
+    // the max and the sum run in four independent chains each.
     const int row = warp * 32 + lane;
     const uint32_t lane_base = static_cast<uint32_t>(warp * 32) << 16;
+    const int64_t last_vis = my_pos < p.n_slots - 1 ? my_pos : p.n_slots - 1;
     float m_ref = -INFINITY, l = 0.f;
     bool ok = true;
     for (int j = 0; j < n_tiles; ++j) {
@@ -315,53 +327,64 @@ __global__ void __launch_bounds__(THREADS, 1)
       ok = __all_sync(0xffffffffu, mbar_wait(&s_full[sb], (j >> 1) & 1, p.err));
       if (!ok) break;
       tc_fence_after();
-      float v[BN];
-      {
-        uint32_t t[BN / 32][32];
-#pragma unroll
-        for (int c = 0; c < BN / 32; ++c) tmem_ld_32x32b_x32(tmem + lane_base + S_COL + sb * 128 + c * 32, t[c]);
-        tc_wait_ld();
-#pragma unroll
-        for (int c = 0; c < BN / 32; ++c)
-#pragma unroll
-          for (int i = 0; i < 32; ++i) v[c * 32 + i] = __uint_as_float(t[c][i]);
-      }
-      tc_fence_before();
-      mbar_arrive(&s_empty[sb]);
       const int64_t key0 = static_cast<int64_t>(j) * BN;
-      float mx = -INFINITY;
-      const int64_t last_vis = my_pos < p.n_slots - 1 ? my_pos : p.n_slots - 1;
-      if (key0 + BN - 1 <= last_vis) {            // every key of the tile is visible to this row
+      const bool whole = key0 + BN - 1 <= last_vis;   // every key of the tile is visible to this row
+      const uint32_t s_addr = tmem + lane_base + S_COL + sb * 128;
+      float m4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+#pragma unroll 1
+      for (int c = 0; c < BN / 32; ++c) {
+        uint32_t t[32];
+        tmem_ld_32x32b_x32(s_addr + c * 32, t);
+        tc_wait_ld();
+        tmem_regs_ready(t);
+        if (whole) {
 #pragma unroll
-        for (int c = 0; c < BN; ++c) mx = fmaxf(mx, v[c]);
-      } else {
+          for (int i = 0; i < 32; ++i) m4[i & 3] = fmaxf(m4[i & 3], __uint_as_float(t[i]));
+        } else {
+          const int64_t k0 = key0 + c * 32;
 #pragma unroll
-        for (int c = 0; c < BN; ++c) {
-          v[c] = key0 + c <= last_vis ? v[c] : -INFINITY;
-          mx = fmaxf(mx, v[c]);
+          for (int i = 0; i < 32; ++i) m4[i & 3] = fmaxf(m4[i & 3], k0 + i <= last_vis ? __uint_as_float(t[i]) : -INFINITY);
         }
       }
-      mx *= p.scale_log2;                          // max in the log2 domain (the scale is positive)
+      const float mx = fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3])) * p.scale_log2;   // log2 domain
       const float m_new = fmaxf(m_ref, mx);
       // Whether a row moves its reference max is decided per row, but the TMEM accesses that rescale O are
       // .sync.aligned warp instructions: the warp takes the rescale path if any of its rows needs it, and rows that
       // do not need it multiply by 1.
       const bool need = m_ref == -INFINITY || m_new > m_ref + RESCALE_THRESHOLD;
-      const float corr = (need && m_ref != -INFINITY) ? exp2f(m_ref - m_new) : 1.f;
+      const float corr = (need && m_ref != -INFINITY) ? exp2_approx(m_ref - m_new) : 1.f;
       if (need) m_ref = m_new;
       const float sub = m_ref == -INFINITY ? 0.f : m_ref;
-      // P for this tile, in registers, before waiting for the previous P V product
-      uint32_t pk[BN / 2];
-      float sum = 0.f;
+      const uint32_t p_addr = tmem + lane_base + P_COL + sb * (BN / 2);
+      float s4[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll 1
+      for (int c = 0; c < BN / 32; ++c) {
+        uint32_t t[32], q16[16];
+        tmem_ld_32x32b_x32(s_addr + c * 32, t);
+        tc_wait_ld();
+        tmem_regs_ready(t);
+        const int64_t k0 = key0 + c * 32;
 #pragma unroll
-      for (int i = 0; i < BN / 2; ++i) {
-        const float p0 = exp2f(fmaf(v[2 * i], p.scale_log2, -sub));
-        const float p1 = exp2f(fmaf(v[2 * i + 1], p.scale_log2, -sub));
-        sum += p0 + p1;
-        pk[i] = pack_bf16x2(p0, p1);
+        for (int i = 0; i < 16; ++i) {
+          float x0 = __uint_as_float(t[2 * i]), x1 = __uint_as_float(t[2 * i + 1]);
+          if (!whole) {
+            x0 = k0 + 2 * i <= last_vis ? x0 : -INFINITY;
+            x1 = k0 + 2 * i + 1 <= last_vis ? x1 : -INFINITY;
+          }
+          const float p0 = exp2_approx(fmaf(x0, p.scale_log2, -sub));
+          const float p1 = exp2_approx(fmaf(x1, p.scale_log2, -sub));
+          s4[i & 3] += p0 + p1;
+          q16[i] = pack_bf16x2(p0, p1);
+        }
+        tmem_st_32x32b_x16(p_addr + c * 16, q16);
       }
-      l = l * corr + sum;
+      tc_wait_st();
+      tc_fence_before();
+      mbar_arrive(&s_empty[sb]);                   // S_j is no longer read
+      l = l * corr + ((s4[0] + s4[1]) + (s4[2] + s4[3]));
       if (j >= 1) {
+        // P V_{j-1} has completed (waited for in order, tile by tile, so the barrier's phase is never ambiguous)
+        // before O is rescaled and before P V_j may start.
         ok = __all_sync(0xffffffffu, mbar_wait(pv_done, (j - 1) & 1, p.err));
         if (!ok) break;
         tc_fence_after();
@@ -372,20 +395,14 @@ __global__ void __launch_bounds__(THREADS, 1)
             const uint32_t addr = tmem + lane_base + O_COL + c * 32;
             tmem_ld_32x32b_x32(addr, t);
             tc_wait_ld();
+            tmem_regs_ready(t);
 #pragma unroll
             for (int i = 0; i < 32; ++i) t[i] = __float_as_uint(__uint_as_float(t[i]) * corr);
             tmem_st_32x32b_x32(addr, t);
           }
+          tc_wait_st();
         }
       }
-#pragma unroll
-      for (int c = 0; c < BN / 32; ++c) {
-        uint32_t q16[16];
-#pragma unroll
-        for (int i = 0; i < 16; ++i) q16[i] = pk[c * 16 + i];
-        tmem_st_32x32b_x16(tmem + lane_base + P_COL + c * 16, q16);
-      }
-      tc_wait_st();
       if (key0 + BN > n_keys) {                    // the tile with the last key: same for every row
         // V rows past the last key hold stale data; P is 0 there but 0 * NaN is not, so zero them. V_j is waited
         // for first (softmax j follows S_j, which only waited for K_j).
@@ -413,6 +430,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         uint32_t t[32];
         tmem_ld_32x32b_x32(tmem + lane_base + O_COL + c * 32, t);
         tc_wait_ld();
+        tmem_regs_ready(t);
         if (row < valid_rows) {
           uint4* dst = reinterpret_cast<uint4*>(orow + c * 32);
 #pragma unroll

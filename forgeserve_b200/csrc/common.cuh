@@ -166,6 +166,14 @@ __device__ __forceinline__ void tc_commit(uint64_t* bar) {
                : "memory");
 }
 __device__ __forceinline__ void tc_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+// tcgen05.ld writes its registers asynchronously; they are valid after tcgen05.wait::ld. The compiler only sees
+// the ld as their producer, so after the wait, pass them through an empty volatile asm: every later use then
+// depends on an instruction that cannot move above the wait.
+template <int N>
+__device__ __forceinline__ void tmem_regs_ready(uint32_t (&r)[N]) {
+#pragma unroll
+  for (int i = 0; i < N; ++i) asm volatile("" : "+r"(r[i]));
+}
 
 // 32 lanes x 32 columns of 32-bit TMEM -> 32 registers per thread (thread i reads lane base+i).
 __device__ __forceinline__ void tmem_ld_32x32b_x32(uint32_t taddr, uint32_t (&r)[32]) {

@@ -55,11 +55,25 @@ struct Params {
 
 constexpr int TQ = 4;   // tile-queue entries (claimed tiles handed from the producer to the MMA and epilogue warps)
 
-__device__ __forceinline__ void tile_coords(int tile, int num_m_blocks, int& m_blk, int& n_blk) {
-  // M-fastest order: the CTAs resident at one time share a few B (weight) tiles and stream all of A,
-  // which for the prefill shapes (M <= 8192, K <= 14336) stays resident in the 126 MB L2.
-  m_blk = tile % num_m_blocks;
-  n_blk = tile / num_m_blocks;
+// Tile order. Tiles are numbered so that the CTAs working at one time share operands in L2: M fastest inside
+// groups of GROUP_M m-blocks, groups in N order (GROUP_M = 0: M fastest over the whole matrix).
+#ifndef FS_GEMM_GROUP_M
+#define FS_GEMM_GROUP_M 8
+#endif
+constexpr int GROUP_M = FS_GEMM_GROUP_M;
+
+__device__ __forceinline__ void tile_coords(int tile, int num_m, int num_n, int& m_blk, int& n_blk) {
+  if (GROUP_M <= 0 || num_m <= GROUP_M) {
+    m_blk = tile % num_m;
+    n_blk = tile / num_m;
+    return;
+  }
+  const int per_group = GROUP_M * num_n;
+  const int first = (tile / per_group) * GROUP_M;
+  const int gm = num_m - first < GROUP_M ? num_m - first : GROUP_M;
+  const int local = tile - (tile / per_group) * per_group;
+  m_blk = first + local % gm;
+  n_blk = local / gm;
 }
 
 __device__ __forceinline__ float bf16_lo(uint32_t v) { return __uint_as_float(v << 16); }
@@ -113,6 +127,8 @@ __device__ __forceinline__ void epilogue_tile(const Params& p, uint32_t tmem_bas
       tmem_ld_32x32b_x32(taddr + c * 32, g);
       tmem_ld_32x32b_x32(taddr + BN / 2 + c * 32, u);
       tc_wait_ld();
+      tmem_regs_ready(g);
+      tmem_regs_ready(u);
       float v[32];
 #pragma unroll
       for (int i = 0; i < 32; ++i) {
@@ -128,6 +144,7 @@ __device__ __forceinline__ void epilogue_tile(const Params& p, uint32_t tmem_bas
       uint32_t r[32];
       tmem_ld_32x32b_x32(taddr + c * 32, r);
       tc_wait_ld();
+      tmem_regs_ready(r);
       const int col0 = n_blk * BN + c * 32;
       float v[32];
 #pragma unroll
@@ -233,7 +250,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         mbar_arrive(&tq_full[slot]);
         if (tile < 0) break;
         int m_blk, n_blk;
-        tile_coords(tile, p.num_m_blocks, m_blk, n_blk);
+        tile_coords(tile, p.num_m_blocks, p.num_tiles / p.num_m_blocks, m_blk, n_blk);
         const int b_row0 = EPI == EPI_SWIGLU ? n_blk * (BN / 2) : n_blk * BN;
         const int b_row1 = EPI == EPI_SWIGLU ? p.n_out + n_blk * (BN / 2) : n_blk * BN + BN / 2;
         for (int kb = 0; kb < p.k_blocks; ++kb) {
@@ -319,7 +336,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       if (!warp_wait(&tfull[acc], acc_ph, p.err)) break;
       tc_fence_after();
       int m_blk, n_blk;
-      tile_coords(tile, p.num_m_blocks, m_blk, n_blk);
+      tile_coords(tile, p.num_m_blocks, p.num_tiles / p.num_m_blocks, m_blk, n_blk);
       epilogue_tile<EPI>(p, tmem_base, acc, q, lane, m_blk * BM + q * 32 + lane, n_blk, vec_ok);
       tc_fence_before();
       mbar_arrive(&tempty[acc]);
@@ -352,7 +369,10 @@ __global__ void __launch_bounds__(THREADS, 1)
 // traffic per FLOP drops by a third against the 1-SM kernel, and 6 stages fit. The leader CTA (rank 0) issues
 // the MMAs; every copy completes on the leader's barrier; the leader signals both CTAs' barriers; both CTAs'
 // epilogues read their own TMEM (their 128 rows) and report to the leader's accumulator-free barrier.
-constexpr int STAGES2 = 6;
+#ifndef FS_GEMM_PAIR_STAGES
+#define FS_GEMM_PAIR_STAGES 6
+#endif
+constexpr int STAGES2 = FS_GEMM_PAIR_STAGES;
 constexpr int STAGE2_BYTES = A_BYTES + BH_BYTES;  // 32 KiB per CTA per k-block
 constexpr int SMEM2_BYTES = STAGES2 * STAGE2_BYTES + 1024 + BAR_BYTES;
 constexpr uint32_t IDESC2 = idesc_bf16_f32(2 * BM, BN);
@@ -459,7 +479,8 @@ __global__ void __launch_bounds__(THREADS, 1)
       uint32_t ph = 0;
       bool ok = true;
       for (int tile = pair; tile < p.num_tiles && ok; tile += num_pairs) {
-        const int m_pair = tile % num_m_pairs, n_blk = tile / num_m_pairs;
+        int m_pair, n_blk;
+        tile_coords(tile, num_m_pairs, p.num_tiles / num_m_pairs, m_pair, n_blk);
         const int a_row = m_pair * 2 * BM + static_cast<int>(cta) * BM;
         const int b_row = EPI == EPI_SWIGLU ? (cta == 0 ? n_blk * (BN / 2) : p.n_out + n_blk * (BN / 2))
                                             : n_blk * BN + static_cast<int>(cta) * (BN / 2);
@@ -527,7 +548,8 @@ __global__ void __launch_bounds__(THREADS, 1)
     for (int tile = pair; tile < p.num_tiles; tile += num_pairs) {
       if (!warp_wait(&tfull[acc], acc_ph, p.err)) break;
       tc_fence_after();
-      const int m_pair = tile % num_m_pairs, n_blk = tile / num_m_pairs;
+      int m_pair, n_blk;
+      tile_coords(tile, num_m_pairs, p.num_tiles / num_m_pairs, m_pair, n_blk);
       const int row = m_pair * 2 * BM + static_cast<int>(cta) * BM + q * 32 + lane;
       epilogue_tile<EPI>(p, tmem_base, acc, q, lane, row, n_blk, vec_ok);
       tc_fence_before();
