@@ -242,6 +242,136 @@ def run_ours(args):
     return result
 
 
+# --------------------------------------------------------------------------------------- config 4 (decode)
+C4 = dict(requests=64, new_tokens=256, prompt_lo=512, prompt_hi=4096, num_blocks=16384, block_size=16)
+C4_WORKLOAD = ("C4: 8B-shape continuous-batching decode over a paged KV cache (block size 16, 16384 blocks per "
+               "GPU, free list shuffled by a seed), 64 requests, prompts uniform in [512, 4096], 256 greedy new "
+               "tokens each, one pipeline stage per GPU")
+
+
+def run_c4(args):
+    """Config 4 through the Engine (1 GPU) or PipelineEngine (one stage per GPU): one step is the whole batch of
+    64 requests from submission to the last token. Reports generated tokens/s over the run and over the decode
+    phase (every request prefilled), and the decode steps' HBM bytes against the measured bandwidth."""
+    import random
+    import torch.distributed as dist
+
+    from forgeserve_b200 import Engine, ForgeModel, ModelConfig, PipelineStage, _lib
+    from forgeserve_b200.pipeline_engine import PipelineEngine
+    from forgeserve_b200.weights import init_model_, init_stage_
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=600))
+    cfg = ModelConfig(**CFG)
+    if world == 1:
+        model = ForgeModel(cfg, device=dev, dtype=torch.bfloat16).eval()
+        init_model_(model, seed=1234, std=0.02)
+        engine = Engine(model, C4["num_blocks"], C4["block_size"], max_batch=C4["requests"], seed=0,
+                        cuda_graphs=not args.no_graphs)
+        weight_bytes = sum(p.numel() * p.element_size() for p in model.parameters())
+    else:
+        stage = PipelineStage(cfg, rank, world, device=dev, dtype=torch.bfloat16).eval()
+        init_stage_(stage, seed=1234, std=0.02)
+        engine = PipelineEngine(stage, C4["num_blocks"], C4["block_size"], max_batch=C4["requests"], seed=0,
+                                microbatches=args.microbatches or world)
+        weight_bytes = sum(p.numel() * p.element_size() for p in stage.parameters())
+    rng = random.Random(11)
+    lengths = [rng.randint(C4["prompt_lo"], C4["prompt_hi"]) for _ in range(C4["requests"])]
+    g = torch.Generator().manual_seed(12)
+    prompts = [torch.randint(0, cfg.vocab_size, (n,), generator=g).tolist() for n in lengths]
+    stream = torch.cuda.current_stream(dev)
+
+    def one_run(prompts, new_tokens):
+        random.Random(5).shuffle(engine.pool.allocator._free)   # non-contiguous block tables
+        for pr in prompts:
+            engine.add_request(pr, new_tokens)
+        e0 = torch.cuda.Event(enable_timing=True)
+        e_dec = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        decode_steps, marked = 0, False
+        while engine.has_work():
+            if not engine.waiting and not marked:
+                e_dec.record(stream)
+                marked = True
+            decoding = not engine.waiting
+            engine.step()
+            decode_steps += decoding
+        e1.record(stream)
+        torch.cuda.synchronize()
+        outs = {rid: r.output for rid, r in engine.requests.items()}
+        engine.requests.clear()
+        return e0.elapsed_time(e1), (e_dec.elapsed_time(e1) if marked else 0.0), decode_steps, outs
+
+    for _ in range(max(args.warmup, 1)):
+        one_run(prompts[:8], 16)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    launches0 = _lib.launch_count()
+    sampler = ClockSampler([local] if world == 1 else range(world))
+    total_ms = dec_ms = 0.0
+    steps_dec = 0
+    with sampler:
+        for _ in range(args.steps):
+            t, td, nd, outs = one_run(prompts, C4["new_tokens"])
+            total_ms, dec_ms, steps_dec = total_ms + t, dec_ms + td, steps_dec + nd
+    launches = _lib.launch_count() - launches0
+
+    def red(x, op):
+        t = torch.tensor([float(x)], device=dev, dtype=torch.float64)
+        if world > 1:
+            dist.all_reduce(t, op=op)
+        return float(t)
+
+    total_ms = red(total_ms, dist.ReduceOp.MAX if world > 1 else None)
+    dec_ms = red(dec_ms, dist.ReduceOp.MAX if world > 1 else None)
+    weight_bytes = red(weight_bytes, dist.ReduceOp.SUM if world > 1 else None)
+    launches = red(launches, dist.ReduceOp.SUM if world > 1 else None)
+    clocks = sampler.summary()
+    result = None
+    if rank == 0:
+        n_req, n_new = C4["requests"], C4["new_tokens"]
+        generated = n_req * n_new * args.steps
+        dec_tokens = n_req * (n_new - 1) * args.steps
+        # bytes a decode step must move: every weight once (all stages) and the K/V of every cached token of
+        # every layer; the mean context over the decode phase is prompt + half the generated tokens
+        kv_token = cfg.n_layers * cfg.n_kv_heads * cfg.head_dim * 2 * 2
+        mean_ctx = sum(lengths) / n_req + n_new / 2
+        step_bytes = weight_bytes + n_req * mean_ctx * kv_token
+        step_ms = dec_ms / max(steps_dec, 1)
+        hbm, src = (json.loads((ROOT / "MEASURED_PEAKS.json").read_text())["hbm_gbs"], "measured") \
+            if (ROOT / "MEASURED_PEAKS.json").exists() else (6650.0, "fallback")
+        achieved = step_bytes / (step_ms / 1e3) / 1e9
+        result = {
+            "metric": "continuous-batching decode tokens/s, 8B-shape bf16 (config 4)",
+            "value": round(generated / (total_ms / 1e3), 1), "unit": "tokens/s", "n_gpus": world,
+            "steps": args.steps, "warmup": max(args.warmup, 1), "ms_per_step": round(total_ms / args.steps, 1),
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic: seeded prompt lengths and token ids, seeded N(0, 0.02) weights",
+            "config": {"workload": C4_WORKLOAD, "stages": world, "parallelism": f"pp{world}",
+                       "microbatches": 1 if world == 1 else (args.microbatches or world),
+                       "decode_cuda_graphs": world == 1 and not args.no_graphs},
+            "decode": {"tokens_per_s": round(dec_tokens / (dec_ms / 1e3), 1), "steps": steps_dec,
+                       "ms_per_step": round(step_ms, 3)},
+            "roofline": {"bound": "hbm", "kernel": "whole decode step (weights + K/V of every cached token)",
+                         "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s",
+                         "frac": round(achieved / hbm, 4), "peak_source": src,
+                         "bytes_per_step": int(step_bytes)},
+            "gpu_launches": int(launches), "clocks": clocks,
+        }
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return result
+
+
 def gemm_traffic():
     """DRAM bytes per launch of the profiled gate/up GEMM launch, from the committed ncu summary (or None)."""
     p = ROOT / "profiles" / "gemm_tc_8b_gateup.txt"
@@ -420,6 +550,10 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--whole-head", action="store_true", help="N > 1: keep the whole output head on the last stage")
+    ap.add_argument("--workload", choices=["c3", "c4"], default="c3",
+                    help="c3: pipeline prefill (the headline metric); c4: continuous-batching decode")
+    ap.add_argument("--microbatches", type=int, default=0, help="c4 with N > 1: micro-batches per engine step")
+    ap.add_argument("--no-graphs", action="store_true", help="c4: launch every decode kernel from Python")
     ap.add_argument("--profile-case", default=None, help="run a few launches of one kernel (for ncu) and exit")
     ap.add_argument("--reps", type=int, default=3)
     ap.add_argument("--timed", action="store_true", help="with --profile-case: also time cold-L2 launches")
@@ -429,7 +563,14 @@ def main():
         return
     if args.warmup < 3 and args.impl == "ours":
         print("warning: fewer than 3 warm-up steps", file=sys.stderr)
-    if args.impl == "reference":
+    if args.workload == "c4":
+        if args.impl == "reference":
+            res = None if int(os.environ.get("RANK", "0")) else {
+                "impl": "reference", "metric": "continuous-batching decode tokens/s, 8B-shape bf16 (config 4)",
+                "unavailable": "config 4 is not run on the CPU (the reference's Engine is fp32 on the host cores)"}
+        else:
+            res = run_c4(args)
+    elif args.impl == "reference":
         res = run_reference(args)
     else:
         res = run_ours(args)

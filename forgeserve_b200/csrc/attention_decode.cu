@@ -31,7 +31,15 @@
 namespace fs {
 namespace decode {
 
-constexpr int THREADS = 128, CHUNK = 64, MAX_REP = 8, MAX_SPLITS = 64;
+constexpr int THREADS = 128, CHUNK = 64, MAX_REP = 8, MAX_SPLITS = 64, SPLIT_KEYS = 512;
+
+// Key slots per split: SPLIT_KEYS, wider (a multiple of CHUNK) only when n_slots exceeds MAX_SPLITS of them.
+// Split s covers slots [s * per, (s + 1) * per); a split at or past a row's last visible key is empty.
+__host__ __device__ __forceinline__ int64_t split_keys(int64_t n_slots, int splits) {
+  return splits * static_cast<int64_t>(SPLIT_KEYS) >= n_slots
+             ? SPLIT_KEYS
+             : ((n_slots + splits - 1) / splits + CHUNK - 1) / CHUNK * CHUNK;
+}
 
 __device__ __forceinline__ int64_t key_row_offset(const KVCache& kv, int r, int64_t s, int g, int hd, bool& ok) {
   const int64_t bi = s / kv.block_size;
@@ -78,9 +86,10 @@ __global__ void __launch_bounds__(THREADS)
   int64_t pos = positions[r];
   if (pos < 0) pos = 0;
   const int64_t n_vis = pos + 1 < n_slots ? pos + 1 : n_slots;
-  const int64_t per = ((n_vis + splits - 1) / splits + CHUNK - 1) / CHUNK * CHUNK;
+  const int64_t per = split_keys(n_slots, splits);
   const int64_t k_begin = static_cast<int64_t>(split) * per;
   const int64_t k_end = k_begin + per < n_vis ? k_begin + per : n_vis;
+  if (k_begin >= n_vis) return;   // empty split: nothing to write (the combine does not read it)
 
   for (int i = tid; i < rep * HD; i += THREADS)
     qs[i] = to_f(q[static_cast<int64_t>(r) * ldq + static_cast<int64_t>(g * rep + i / HD) * HD + i % HD]);
@@ -176,7 +185,7 @@ __global__ void __launch_bounds__(THREADS)
         out[static_cast<int64_t>(r) * ldo + static_cast<int64_t>(hh) * HD + d] = from_f<T>(l > 0.f ? acc[h] / l : 0.f);
       } else {
         const int64_t slot = (static_cast<int64_t>(r) * nh + hh) * splits + split;
-        ws[slot * HD + d] = acc[h];
+        if (m_s[h] != -INFINITY) ws[slot * HD + d] = acc[h];   // an empty split is skipped by the combine
       }
     }
   }
@@ -190,16 +199,23 @@ __global__ void __launch_bounds__(THREADS)
 
 template <typename T, int HD>
 __global__ void __launch_bounds__(THREADS)
-    attn_combine_kernel(const float* __restrict__ ws, int B, int nh, int splits, T* __restrict__ out, int64_t ldo) {
+    attn_combine_kernel(const float* __restrict__ ws, int B, int nh, int splits, const int64_t* __restrict__ positions,
+                        int64_t n_slots, T* __restrict__ out, int64_t ldo) {
   const int r = blockIdx.x, h = blockIdx.y, d = threadIdx.x;
   const int64_t base = (static_cast<int64_t>(r) * nh + h) * splits;
   const float* ml = ws + static_cast<int64_t>(B) * nh * splits * HD;
+  int64_t pos = positions[r];
+  if (pos < 0) pos = 0;
+  const int64_t n_vis = pos + 1 < n_slots ? pos + 1 : n_slots;
+  const int64_t per = split_keys(n_slots, splits);
+  const int used = static_cast<int>((n_vis + per - 1) / per < splits ? (n_vis + per - 1) / per : splits);
   float M = -INFINITY;
-  for (int s = 0; s < splits; ++s) M = fmaxf(M, ml[2 * (base + s)]);
+  for (int s = 0; s < used; ++s) M = fmaxf(M, ml[2 * (base + s)]);
   float L = 0.f, o = 0.f;
-  for (int s = 0; s < splits; ++s) {
+  for (int s = 0; s < used; ++s) {
     const float m = ml[2 * (base + s)];
-    const float w = m == -INFINITY ? 0.f : expf(m - M);
+    if (m == -INFINITY) continue;   // no visible key in this split (its O partial is not written)
+    const float w = expf(m - M);
     L += w * ml[2 * (base + s) + 1];
     if (d < HD) o += w * ws[(base + s) * HD + d];
   }
@@ -297,7 +313,8 @@ __global__ void __launch_bounds__(THREADS_TC)
   const int64_t n_vis = pos + 1 < p.n_slots ? pos + 1 : p.n_slots;
   const int64_t k_begin = static_cast<int64_t>(split) * p.per;
   const int64_t k_end = k_begin + p.per < n_vis ? k_begin + p.per : n_vis;
-  const int n_tiles = k_end > k_begin ? static_cast<int>((k_end - k_begin + TILE - 1) / TILE) : 0;
+  if (k_begin >= n_vis) return;   // empty split: the whole CTA leaves before any set-up (the combine skips it)
+  const int n_tiles = static_cast<int>((k_end - k_begin + TILE - 1) / TILE);
   const int my_n = n_tiles > warp ? (n_tiles - warp + WARPS - 1) / WARPS : 0;   // tiles warp, warp+4, ...
 
   if (threadIdx.x == 0) {
@@ -475,7 +492,7 @@ __global__ void __launch_bounds__(THREADS_TC)
           __float2bfloat16_rn(L > 0.f ? o / L : 0.f);
     } else {
       const int64_t slot = (static_cast<int64_t>(r) * p.nh + hh) * p.splits + split;
-      p.ws[slot * HD + d] = o;
+      if (M != -INFINITY) p.ws[slot * HD + d] = o;   // an empty split is skipped by the combine
       if (d == 0) {
         float* ml = p.ws + static_cast<int64_t>(gridDim.z) * p.nh * p.splits * HD;
         ml[2 * slot] = M == -INFINITY ? -INFINITY : M * 0.6931471805599453f;   // log2 -> natural-log domain
@@ -520,8 +537,7 @@ int launch_t(const void* q, int64_t ldq, const KVCache& kv, int64_t n_slots, con
   p.nh = static_cast<int>(nh);
   p.rep = static_cast<int>(nh / nkv);
   p.splits = splits;
-  const int64_t per = (n_slots + splits - 1) / splits;
-  p.per = static_cast<int>((per + TILE - 1) / TILE * TILE);
+  p.per = static_cast<int>(split_keys(n_slots, splits));
   p.scale_log2 = scale * 1.4426950408889634f;
   p.ws = ws;
   p.err = err;
@@ -563,21 +579,22 @@ int launch_t(const void* q, int64_t ldq, const KVCache& kv, int64_t n_slots, con
 }
 
 template <typename T, int HD>
-int combine_t(float* ws, int64_t B, int64_t nh, int splits, void* out, int64_t ldo, cudaStream_t st) {
+int combine_t(float* ws, int64_t B, int64_t nh, int splits, const int64_t* positions, int64_t n_slots, void* out,
+              int64_t ldo, cudaStream_t st) {
   attn_combine_kernel<T, HD><<<dim3(static_cast<unsigned>(B), static_cast<unsigned>(nh)), THREADS, 0, st>>>(
-      ws, static_cast<int>(B), static_cast<int>(nh), splits, static_cast<T*>(out), ldo);
+      ws, static_cast<int>(B), static_cast<int>(nh), splits, positions, n_slots, static_cast<T*>(out), ldo);
   return check_launch("attn_combine_kernel");
 }
 
 int choose_splits(int64_t B, int64_t nkv, int64_t n_slots, int sms) {
-  // Keys per split: the batch's key slots (B * nkv * n_slots, an upper bound) over ~8 CTAs per SM, between 128
-  // and 512 slots, a multiple of 64; more only when that would exceed MAX_SPLITS.
-  if (sms <= 0) sms = 148;
-  int64_t per = (B * nkv * n_slots + 8 * static_cast<int64_t>(sms) - 1) / (8 * static_cast<int64_t>(sms));
-  per = (per + 63) / 64 * 64;
-  if (per < 2 * CHUNK) per = 2 * CHUNK;
-  if (per > 8 * CHUNK) per = 8 * CHUNK;
-  int64_t s = (n_slots + per - 1) / per;
+  // A split covers a fixed number of key slots (SPLIT_KEYS), more only past MAX_SPLITS: the partition of a row's
+  // keys, and so the order of the sums, is the same whatever the batch size and the width of the block table
+  // (splits past a row's context end at once and add exact zeros), so a step gives the same result in a CUDA
+  // graph (tables padded to the longest possible row), eagerly, or split into micro-batches.
+  (void)B;
+  (void)nkv;
+  (void)sms;
+  int64_t s = (n_slots + SPLIT_KEYS - 1) / SPLIT_KEYS;
   if (s > MAX_SPLITS) s = MAX_SPLITS;
   return s < 1 ? 1 : static_cast<int>(s);
 }
@@ -617,10 +634,10 @@ int launch(int dtype, const void* q, int64_t ldq, const KVCache& kv, int64_t n_s
   }
   if (rc || splits == 1) return rc;
   if (dtype == BF16)
-    return hd == 128 ? combine_t<__nv_bfloat16, 128>(ws, B, nh, splits, out, ldo, st)
-                     : combine_t<__nv_bfloat16, 64>(ws, B, nh, splits, out, ldo, st);
-  return hd == 128 ? combine_t<float, 128>(ws, B, nh, splits, out, ldo, st)
-                   : combine_t<float, 64>(ws, B, nh, splits, out, ldo, st);
+    return hd == 128 ? combine_t<__nv_bfloat16, 128>(ws, B, nh, splits, positions, n_slots, out, ldo, st)
+                     : combine_t<__nv_bfloat16, 64>(ws, B, nh, splits, positions, n_slots, out, ldo, st);
+  return hd == 128 ? combine_t<float, 128>(ws, B, nh, splits, positions, n_slots, out, ldo, st)
+                   : combine_t<float, 64>(ws, B, nh, splits, positions, n_slots, out, ldo, st);
 }
 
 }  // namespace decode

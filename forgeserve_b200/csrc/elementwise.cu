@@ -141,7 +141,7 @@ __global__ void rope_kv_kernel(T* __restrict__ qkv, int64_t ld, const float* __r
 
 // Vectorised bf16 variant for head_dim % 16 == 0: each work item moves 8 elements (16 bytes) of x1 and the
 // matching 8 of x2 (rotation) or 8 values of v (copy); same arithmetic and rounding as rope_kv_kernel.
-__global__ void __launch_bounds__(256)
+__global__ void __launch_bounds__(128)
     rope_kv_vec_kernel(__nv_bfloat16* __restrict__ qkv, int64_t ld, const float* __restrict__ cos_t,
                        const float* __restrict__ sin_t, int rope_rows, const int64_t* __restrict__ positions,
                        KVCache kv, int T_new, int nh, int nkv, int hd, int64_t slot_base, int slot_from_pos,
@@ -315,6 +315,56 @@ __global__ void argmax_kernel(const T* __restrict__ x, int64_t row_stride, int64
   }
 }
 
+// bf16 rows of dim = 256 * VPL: one warp per row (8 rows per CTA), lanes reading consecutive 16-byte vectors.
+// Pass 1 accumulates the sum of squares (a shuffle reduction, no block barrier); pass 2 reads the row again (now
+// in L1/L2) with w and writes y. Few registers, so every warp slot of an SM can hold a row in flight. Same
+// rounding points as rmsnorm_kernel.
+template <int VPL>
+__global__ void __launch_bounds__(256)
+    rmsnorm_warp_kernel(const __nv_bfloat16* __restrict__ x, int64_t xs, const __nv_bfloat16* __restrict__ w,
+                        __nv_bfloat16* __restrict__ y, int64_t ys, int64_t rows, float eps) {
+  using bf = __nv_bfloat16;
+  const int64_t row = static_cast<int64_t>(blockIdx.x) * 8 + (threadIdx.x >> 5);
+  if (row >= rows) return;
+  const int lane = threadIdx.x & 31;
+  const uint4* xr = reinterpret_cast<const uint4*>(x + row * xs);
+  float ss = 0.f;
+#pragma unroll 4
+  for (int i = 0; i < VPL; ++i) {
+    const uint4 u = xr[i * 32 + lane];
+    const bf* e = reinterpret_cast<const bf*>(&u);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const float f = __bfloat162float(e[j]);
+      ss = fmaf(f, f, ss);
+    }
+  }
+  ss = warp_sum(ss);
+  const float r = rsqrtf(ss / static_cast<float>(VPL * 256) + eps);
+  const uint4* wr = reinterpret_cast<const uint4*>(w);
+  uint4* yr = reinterpret_cast<uint4*>(y + row * ys);
+#pragma unroll 4
+  for (int i = 0; i < VPL; ++i) {
+    const uint4 u = xr[i * 32 + lane];
+    const uint4 wu = wr[i * 32 + lane];
+    const bf* e = reinterpret_cast<const bf*>(&u);
+    const bf* we = reinterpret_cast<const bf*>(&wu);
+    uint4 o;
+    bf* oe = reinterpret_cast<bf*>(&o);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) oe[j] = from_f<bf>(rnd<bf>(__bfloat162float(e[j]) * r) * __bfloat162float(we[j]));
+    yr[i * 32 + lane] = o;
+  }
+}
+
+template <int VPL>
+static void launch_rmsnorm_warp(const void* x, int64_t xs, const void* w, void* y, int64_t ys, int64_t rows, float eps,
+                                cudaStream_t st) {
+  rmsnorm_warp_kernel<VPL><<<static_cast<unsigned>((rows + 7) / 8), 256, 0, st>>>(
+      static_cast<const __nv_bfloat16*>(x), xs, static_cast<const __nv_bfloat16*>(w), static_cast<__nv_bfloat16*>(y),
+      ys, rows, eps);
+}
+
 }  // namespace
 
 // ================================================================================================ host
@@ -325,6 +375,19 @@ int rmsnorm(int dtype, const void* x, int64_t xs, const void* w, void* y, int64_
   if (dim <= 0 || dim > (1 << 24)) return fail("rmsnorm: bad dim");
   if (rows > INT32_MAX) return fail("rmsnorm: too many rows");
   constexpr int TH = 256;
+  const bool aligned = ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(y) |
+                         reinterpret_cast<uintptr_t>(w)) & 15) == 0 && xs % 8 == 0 && ys % 8 == 0;
+  if (dtype == BF16 && aligned && dim % 256 == 0) {
+    switch (dim / 256) {
+      case 1: launch_rmsnorm_warp<1>(x, xs, w, y, ys, rows, eps, st); return check_launch("rmsnorm_warp_kernel");
+      case 2: launch_rmsnorm_warp<2>(x, xs, w, y, ys, rows, eps, st); return check_launch("rmsnorm_warp_kernel");
+      case 4: launch_rmsnorm_warp<4>(x, xs, w, y, ys, rows, eps, st); return check_launch("rmsnorm_warp_kernel");
+      case 8: launch_rmsnorm_warp<8>(x, xs, w, y, ys, rows, eps, st); return check_launch("rmsnorm_warp_kernel");
+      case 16: launch_rmsnorm_warp<16>(x, xs, w, y, ys, rows, eps, st); return check_launch("rmsnorm_warp_kernel");
+      case 32: launch_rmsnorm_warp<32>(x, xs, w, y, ys, rows, eps, st); return check_launch("rmsnorm_warp_kernel");
+      default: break;
+    }
+  }
   if (dtype == F32)
     rmsnorm_kernel<float, TH><<<static_cast<unsigned>(rows), TH, 0, st>>>(
         static_cast<const float*>(x), xs, static_cast<const float*>(w), static_cast<float*>(y), ys, static_cast<int>(dim), eps);
@@ -350,7 +413,7 @@ int rope_kv_write(int dtype, void* qkv, int64_t ld, const float* cos_t, const fl
                    ((reinterpret_cast<uintptr_t>(qkv) | reinterpret_cast<uintptr_t>(kv.k) |
                      reinterpret_cast<uintptr_t>(kv.v)) & 15) == 0;
   if (vec) {
-    rope_kv_vec_kernel<<<static_cast<unsigned>(tokens), 256, 0, st>>>(
+    rope_kv_vec_kernel<<<static_cast<unsigned>(tokens), 128, 0, st>>>(
         static_cast<__nv_bfloat16*>(qkv), ld, cos_t, sin_t, static_cast<int>(rope_rows), positions, kv,
         static_cast<int>(T_new), static_cast<int>(nh), static_cast<int>(nkv), static_cast<int>(hd), slot_base,
         slot_from_pos, error_word());

@@ -50,6 +50,12 @@ struct Params {
   int num_m_blocks, num_tiles, k_blocks;
   int sys_fence;   // C may be another GPU's memory: end every epilogue thread with a system-scope fence
   unsigned* sched; // 1-SM kernel: [next tile, CTAs finished], zero at launch; the last CTA to finish re-zeroes it
+  // Split K (1-SM kernel, one m-block): work unit u = (tile u / k_split, K chunk u % k_split of kb_per k-blocks);
+  // each unit stores its fp32 partial of the B rows it covers to ws[(chunk * M + row) * ldw + B row], and
+  // splitk_reduce_kernel applies the epilogue to the sums. k_split = 1: whole K, fused epilogue.
+  int k_split, kb_per;
+  float* ws;
+  int64_t ldw;
   unsigned* err;
 };
 
@@ -174,6 +180,72 @@ __device__ __forceinline__ void epilogue_tile(const Params& p, uint32_t tmem_bas
   }
 }
 
+// Split-K epilogue: this unit's fp32 partial sums (no rounding) to the workspace, by B row.
+template <int EPI>
+__device__ __forceinline__ void epilogue_partial(const Params& p, uint32_t tmem_base, int acc, int q, int lane, int row,
+                                                 int n_blk, int chunk) {
+  const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(acc * BN);
+  float* wrow = p.ws + (static_cast<int64_t>(chunk) * p.M + row) * p.ldw;
+  const int n_b = EPI == EPI_SWIGLU ? 2 * p.n_out : p.n_out;   // B rows
+  const bool row_ok = row < p.M;
+#pragma unroll 1
+  for (int c = 0; c < BN / 32; ++c) {
+    uint32_t r[32];
+    __syncwarp();   // the whole warp takes part in the collective TMEM load
+    tmem_ld_32x32b_x32(taddr + c * 32, r);
+    tc_wait_ld();
+    tmem_regs_ready(r);
+    int brow0, lim;   // first B row of these 32 accumulator columns, and the end of their half (or of B)
+    if constexpr (EPI == EPI_SWIGLU) {
+      const int half_col = (c * 32) % (BN / 2);
+      brow0 = (c * 32 < BN / 2 ? 0 : p.n_out) + n_blk * (BN / 2) + half_col;
+      lim = (c * 32 < BN / 2 ? 0 : p.n_out) + p.n_out;
+    } else {
+      brow0 = n_blk * BN + c * 32;
+      lim = n_b;
+    }
+    if (!row_ok) {
+    } else if (brow0 + 32 <= lim && ((p.ldw | brow0) & 3) == 0) {
+      float4* dst = reinterpret_cast<float4*>(wrow + brow0);
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+        dst[i] = make_float4(__uint_as_float(r[4 * i]), __uint_as_float(r[4 * i + 1]), __uint_as_float(r[4 * i + 2]),
+                             __uint_as_float(r[4 * i + 3]));
+    } else {
+#pragma unroll
+      for (int i = 0; i < 32; ++i)
+        if (brow0 + i < lim) wrow[brow0 + i] = __uint_as_float(r[i]);
+    }
+  }
+}
+
+// Sums the split-K partials and applies the epilogue with the fused kernel's rounding points.
+template <int EPI>
+__global__ void __launch_bounds__(256)
+    splitk_reduce_kernel(const float* __restrict__ ws, int64_t ldw, int k_split, int M, int n_out,
+                         __nv_bfloat16* __restrict__ C, int64_t ldc, const __nv_bfloat16* __restrict__ R, int64_t ldr) {
+  const int64_t total = static_cast<int64_t>(M) * n_out;
+  const int64_t plane = static_cast<int64_t>(M) * ldw;
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int row = static_cast<int>(i / n_out), j = static_cast<int>(i % n_out);
+    const float* w = ws + static_cast<int64_t>(row) * ldw;
+    float a = 0.f, b = 0.f;
+    for (int k = 0; k < k_split; ++k) {
+      a += w[k * plane + j];
+      if constexpr (EPI == EPI_SWIGLU) b += w[k * plane + n_out + j];
+    }
+    float v;
+    if constexpr (EPI == EPI_SWIGLU) {
+      v = rnd<__nv_bfloat16>(silu_f(rnd<__nv_bfloat16>(a))) * rnd<__nv_bfloat16>(b);
+    } else {
+      v = rnd<__nv_bfloat16>(a);
+      if constexpr (EPI == EPI_RESIDUAL) v += __bfloat162float(R[static_cast<int64_t>(row) * ldr + j]);
+    }
+    C[static_cast<int64_t>(row) * ldc + j] = __float2bfloat16_rn(v);
+  }
+}
+
 template <int EPI>
 __global__ void __launch_bounds__(THREADS, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, Params p) {
@@ -244,16 +316,18 @@ __global__ void __launch_bounds__(THREADS, 1)
           ok = false;
           break;
         }
-        int tile = static_cast<int>(atomicAdd(p.sched, 1u));
-        if (tile >= p.num_tiles) tile = -1;
-        tq[slot] = tile;
+        int unit = static_cast<int>(atomicAdd(p.sched, 1u));
+        if (unit >= p.num_tiles * p.k_split) unit = -1;
+        tq[slot] = unit;
         mbar_arrive(&tq_full[slot]);
-        if (tile < 0) break;
+        if (unit < 0) break;
+        const int tile = unit / p.k_split, kb0 = (unit % p.k_split) * p.kb_per;
+        const int kb1 = kb0 + p.kb_per < p.k_blocks ? kb0 + p.kb_per : p.k_blocks;
         int m_blk, n_blk;
         tile_coords(tile, p.num_m_blocks, p.num_tiles / p.num_m_blocks, m_blk, n_blk);
         const int b_row0 = EPI == EPI_SWIGLU ? n_blk * (BN / 2) : n_blk * BN;
         const int b_row1 = EPI == EPI_SWIGLU ? p.n_out + n_blk * (BN / 2) : n_blk * BN + BN / 2;
-        for (int kb = 0; kb < p.k_blocks; ++kb) {
+        for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait(&empty[s], ph ^ 1u, p.err) || *abort_flag) {
             ok = false;
             break;
@@ -286,16 +360,18 @@ __global__ void __launch_bounds__(THREADS, 1)
           ok = false;
           break;
         }
-        const int tile = tq[slot];
+        const int unit = tq[slot];
         mbar_arrive(&tq_empty[slot]);
-        if (tile < 0) break;
+        if (unit < 0) break;
+        const int kb0 = (unit % p.k_split) * p.kb_per;
+        const int kb1 = kb0 + p.kb_per < p.k_blocks ? kb0 + p.kb_per : p.k_blocks;
         if (!mbar_wait(&tempty[acc], acc_ph ^ 1u, p.err) || *abort_flag) {
           ok = false;
           break;
         }
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
-        for (int kb = 0; kb < p.k_blocks; ++kb) {
+        for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait(&full[s], ph, p.err) || *abort_flag) {
             ok = false;
             break;
@@ -307,7 +383,7 @@ __global__ void __launch_bounds__(THREADS, 1)
 #pragma unroll
           for (int k = 0; k < BK / 16; ++k) {
             // +32 bytes along K inside the 128-byte swizzle row = +2 in the descriptor's address field
-            tc_mma_f16(d_tmem, adesc + 2u * k, bdesc + 2u * k, IDESC, (kb | k) != 0);
+            tc_mma_f16(d_tmem, adesc + 2u * k, bdesc + 2u * k, IDESC, (kb != kb0 || k != 0) ? 1u : 0u);
           }
           tc_commit(&empty[s]);  // the smem stage is free once these MMAs have read it
           if (++s == STAGES) s = 0, ph ^= 1u;
@@ -329,15 +405,18 @@ __global__ void __launch_bounds__(THREADS, 1)
     for (int i = 0;; ++i) {
       const int slot = i & (TQ - 1);
       if (!warp_wait(&tq_full[slot], static_cast<uint32_t>((i / TQ) & 1), p.err)) break;
-      const int tile = tq[slot];
+      const int unit = tq[slot];
       __syncwarp();
       if (lane == 0) mbar_arrive(&tq_empty[slot]);
-      if (tile < 0) break;
+      if (unit < 0) break;
       if (!warp_wait(&tfull[acc], acc_ph, p.err)) break;
       tc_fence_after();
       int m_blk, n_blk;
-      tile_coords(tile, p.num_m_blocks, p.num_tiles / p.num_m_blocks, m_blk, n_blk);
-      epilogue_tile<EPI>(p, tmem_base, acc, q, lane, m_blk * BM + q * 32 + lane, n_blk, vec_ok);
+      tile_coords(unit / p.k_split, p.num_m_blocks, p.num_tiles / p.num_m_blocks, m_blk, n_blk);
+      if (p.k_split > 1)
+        epilogue_partial<EPI>(p, tmem_base, acc, q, lane, m_blk * BM + q * 32 + lane, n_blk, unit % p.k_split);
+      else
+        epilogue_tile<EPI>(p, tmem_base, acc, q, lane, m_blk * BM + q * 32 + lane, n_blk, vec_ok);
       tc_fence_before();
       mbar_arrive(&tempty[acc]);
       if (++acc == NUM_ACC) acc = 0, acc_ph ^= 1u;
@@ -691,6 +770,41 @@ static unsigned* sched_counter(cudaStream_t st) {
   return c;
 }
 
+// Split-K partial sums, one growing buffer per (device, stream). An outgrown buffer is kept (not freed): a CUDA
+// graph captured on that stream may still address it.
+static float* splitk_workspace(cudaStream_t st, int64_t bytes) {
+  static std::mutex mu;
+  static std::map<std::pair<int, cudaStream_t>, std::pair<float*, int64_t>> bufs;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) {
+    fail("gemm: no current CUDA device");
+    return nullptr;
+  }
+  std::lock_guard<std::mutex> lock(mu);
+  auto& b = bufs[std::make_pair(dev, st)];
+  if (b.second < bytes) {
+    b = {nullptr, 0};
+    const int64_t want = (bytes + (int64_t(1) << 20) - 1) >> 20 << 20;
+    if (cudaMalloc(&b.first, static_cast<size_t>(want)) != cudaSuccess) {
+      b = {nullptr, 0};
+      fail("gemm: cannot allocate the split-K workspace");
+      return nullptr;
+    }
+    b.second = want;
+  }
+  return b.first;
+}
+
+template <int EPI>
+static int launch_reduce_t(const Params& p, int64_t M, int64_t n_out, cudaStream_t st) {
+  const int64_t total = M * n_out;
+  int64_t blocks = (total + 255) / 256;
+  if (blocks > 4 * sm_count()) blocks = 4 * sm_count();
+  splitk_reduce_kernel<EPI><<<static_cast<unsigned>(blocks), 256, 0, st>>>(
+      p.ws, p.ldw, p.k_split, static_cast<int>(M), static_cast<int>(n_out), p.C, p.ldc, p.R, p.ldr);
+  return check_launch("splitk_reduce_kernel");
+}
+
 static int g_pair_mode = 1;   // 1: use the 2-SM kernel for M > 128; 0: always the 1-SM kernel
 
 int set_pair_mode(int on) {
@@ -719,6 +833,10 @@ int gemm_tc(const void* A, int64_t lda, const void* B, int64_t ldb, void* C, int
   p.k_blocks = static_cast<int>((K + BK - 1) / BK);
   p.sys_fence = sys_fence ? 1 : 0;
   p.sched = nullptr;
+  p.k_split = 1;
+  p.kb_per = p.k_blocks;
+  p.ws = nullptr;
+  p.ldw = 0;
   p.err = error_word();
   if (!p.err) return -1;
   if (g_pair_mode && M > BM) {
@@ -734,12 +852,40 @@ int gemm_tc(const void* A, int64_t lda, const void* B, int64_t ldb, void* C, int
   }
   p.sched = sched_counter(stream);
   if (!p.sched) return -1;
-  const int grid = p.num_tiles < sm_count() ? p.num_tiles : sm_count();
+  const int sms = sm_count();
+  // Few rows (a decode step): with one m-block there are fewer tiles than SMs, so fewer CTAs than SMs would
+  // stream the weights. Split K into chunks of at least KB_MIN k-blocks until there are ~2 units per CTA; the
+  // partial sums (M rows x the tile's columns, fp32) are small next to the weight bytes.
+  constexpr int KB_MIN = 8;
+  if (!sys_fence && p.num_m_blocks == 1 && p.num_tiles < sms && p.k_blocks >= 2 * KB_MIN) {
+    int split = (2 * sms + p.num_tiles - 1) / p.num_tiles;
+    if (split > p.k_blocks / KB_MIN) split = p.k_blocks / KB_MIN;
+    if (split >= 2) {
+      p.kb_per = (p.k_blocks + split - 1) / split;
+      split = (p.k_blocks + p.kb_per - 1) / p.kb_per;
+      const int64_t n_b = epi == EPI_SWIGLU ? 2 * n_out : n_out;
+      p.ldw = (n_b + 3) / 4 * 4;
+      p.ws = splitk_workspace(stream, static_cast<int64_t>(split) * M * p.ldw * static_cast<int64_t>(sizeof(float)));
+      if (!p.ws) return -1;
+      p.k_split = split;
+    } else {
+      p.kb_per = p.k_blocks;
+    }
+  }
+  const int units = p.num_tiles * p.k_split;
+  const int grid = units < sms ? units : sms;
+  int rc;
   switch (epi) {
-    case EPI_STORE: return launch_t<EPI_STORE>(ma, mb, p, grid, stream);
-    case EPI_RESIDUAL: return launch_t<EPI_RESIDUAL>(ma, mb, p, grid, stream);
-    case EPI_SWIGLU: return launch_t<EPI_SWIGLU>(ma, mb, p, grid, stream);
+    case EPI_STORE: rc = launch_t<EPI_STORE>(ma, mb, p, grid, stream); break;
+    case EPI_RESIDUAL: rc = launch_t<EPI_RESIDUAL>(ma, mb, p, grid, stream); break;
+    case EPI_SWIGLU: rc = launch_t<EPI_SWIGLU>(ma, mb, p, grid, stream); break;
     default: return fail("gemm: unknown epilogue");
+  }
+  if (rc || p.k_split == 1) return rc;
+  switch (epi) {
+    case EPI_STORE: return launch_reduce_t<EPI_STORE>(p, M, n_out, stream);
+    case EPI_RESIDUAL: return launch_reduce_t<EPI_RESIDUAL>(p, M, n_out, stream);
+    default: return launch_reduce_t<EPI_SWIGLU>(p, M, n_out, stream);
   }
 }
 

@@ -166,14 +166,92 @@ class Scheduler:
             req.blocks = []
 
 
-class Engine(Scheduler):
-    """Continuous batching of one model on one GPU (forgeserve/engine.py:36-45)."""
+class _DecodeGraph:
+    """One decode step of `rows` greedy rows (one new token each) captured as a CUDA graph: embedding, every layer,
+    final norm, head of the last position and argmax, over static device buffers for the token ids, positions and
+    block tables (tables padded with block 0 to max_seq_len / block_size columns, as the reference pads them,
+    engine.py:122). The kernels read positions from device memory, so one graph serves every step with that
+    many rows; a step costs one host-to-device copy, one replay and one 8-byte-per-row copy back.
 
-    def __init__(self, model, num_blocks: int, block_size: int = 16, max_batch: int = 8, seed: int = 0):
+    The first step runs eagerly on the graph's stream (it is a real step, and it sets up that stream's GEMM tile
+    counter and split-K workspace), then the same work is captured without running it."""
+
+    def __init__(self, model, pool: PagedKVPool, rows: int):
+        self.model, self.pool, self.rows = model, pool, rows
+        self.width = -(-model.cfg.max_seq_len // pool.block_size)
+        dev = model.device
+        n = rows * (2 + self.width)
+        self.host = torch.zeros(n, dtype=torch.int64).pin_memory()
+        self.inp = torch.zeros(n, dtype=torch.int64, device=dev)
+        self.idx = self.inp[:rows].view(rows, 1)
+        self.pos = self.inp[rows : 2 * rows].view(rows, 1)
+        self.tab = self.inp[2 * rows :].view(rows, self.width)
+        self.out_host = torch.empty(rows, dtype=torch.int64).pin_memory()
+        self.stream = torch.cuda.Stream(dev)
+        self.graph: Optional[torch.cuda.CUDAGraph] = None
+        self.tokens: Optional[torch.Tensor] = None
+
+    def _step(self) -> torch.Tensor:
+        from .model import layer_forward_
+        m = self.model
+        cos, sin = m._rope.on(m.device)
+        x = ops.embed(self.idx, m.tok_emb.weight)
+        for layer, view in zip(m.layers, self.pool.views(self.tab, self.pos)):
+            layer_forward_(layer, x, self.pos, view, cos, sin)
+        return ops.argmax(m.head(x)[:, -1])
+
+    def run(self, idx: torch.Tensor, positions: torch.Tensor, tables: torch.Tensor) -> List[int]:
+        r = self.rows
+        self.host.zero_()
+        self.host[:r].copy_(idx.reshape(-1))
+        self.host[r : 2 * r].copy_(positions.reshape(-1))
+        self.host[2 * r :].view(r, self.width)[:, : tables.shape[1]].copy_(tables)
+        cur = torch.cuda.current_stream(self.model.device)
+        self.stream.wait_stream(cur)
+        with torch.cuda.stream(self.stream):
+            self.inp.copy_(self.host, non_blocking=True)
+            if self.graph is None:
+                out = self._step()
+                self.stream.synchronize()
+                g = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(g, stream=self.stream):
+                    self.tokens = self._step()
+                self.graph = g
+            else:
+                self.graph.replay()
+                out = self.tokens
+            self.out_host.copy_(out, non_blocking=True)
+        self.stream.synchronize()
+        cur.wait_stream(self.stream)
+        return self.out_host.tolist()
+
+
+class Engine(Scheduler):
+    """Continuous batching of one model on one GPU (forgeserve/engine.py:36-45).
+
+    cuda_graphs=True (extra): decode steps whose rows are all greedy replay a captured CUDA graph per row count
+    (_DecodeGraph) instead of launching every kernel from Python; the tokens are the same."""
+
+    MAX_GRAPHS = 4
+
+    def __init__(self, model, num_blocks: int, block_size: int = 16, max_batch: int = 8, seed: int = 0,
+                 cuda_graphs: bool = True):
         self.model, self.cfg = model, model.cfg
         self.pool = PagedKVPool(self.cfg, num_blocks, block_size, tp=model.tp, dtype=model.dtype, device=model.device)
+        self.cuda_graphs = cuda_graphs
+        self._graphs: Dict[int, _DecodeGraph] = {}
         self._init_scheduler(max_batch, seed)
 
     def _forward_rows(self, reqs, idx, positions, tables):
+        if (self.cuda_graphs and self.pool.device.type == "cuda" and idx.shape[1] == 1
+                and all(r.temperature == 0 for r in reqs)
+                and tables.shape[1] * self.pool.block_size <= self.cfg.max_seq_len + self.pool.block_size):
+            g = self._graphs.pop(idx.shape[0], None)
+            if g is None:
+                if len(self._graphs) >= self.MAX_GRAPHS:
+                    self._graphs.pop(next(iter(self._graphs)))
+                g = _DecodeGraph(self.model, self.pool, idx.shape[0])
+            self._graphs[idx.shape[0]] = g
+            return g.run(idx, positions, tables)
         logits = self.model(idx, positions, self.pool.views(tables, positions), last_only=True)
         return self._sample_rows(logits[:, -1], reqs)

@@ -191,14 +191,18 @@ def attention(q: torch.Tensor, kv: L.KVCacheDesc, n_slots: int, positions: torch
 
 
 _DECODE_WS = {}
+_DECODE_WS_RETIRED: List[torch.Tensor] = []
 
 
 def decode_workspace(device: torch.device, nbytes: int) -> torch.Tensor:
-    """A per-device scratch buffer for split decode attention, grown on demand and reused across calls (calls are
-    ordered on one stream; concurrent streams would need their own)."""
-    key = str(device)
+    """A scratch buffer for split decode attention per (device, current stream), grown on demand and reused by the
+    calls on that stream (which run one after another). A buffer that is outgrown stays allocated: a CUDA graph
+    captured earlier may still address it."""
+    key = (str(device), torch.cuda.current_stream(device).cuda_stream)
     ws = _DECODE_WS.get(key)
     if ws is None or ws.numel() < nbytes:
+        if ws is not None:
+            _DECODE_WS_RETIRED.append(ws)
         ws = torch.empty(max(nbytes, 1 << 20), dtype=torch.uint8, device=device)
         _DECODE_WS[key] = ws
     return ws

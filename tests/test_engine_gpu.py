@@ -124,3 +124,27 @@ def test_pipeline_engine_bf16_decode_kernel_matches_single_engine():
             agree = sum(a == b for a, b in zip(got, want[rid]))
             assert agree >= 18, (got, want[rid])          # bf16: micro-batched rows may flip a near-tie
         assert steps == single.steps
+
+
+def test_engine_decode_graph_matches_eager_launches():
+    """bf16, head_dim 128, block size 16 (tensor-core decode attention, split-K GEMMs): decode steps replayed from
+    captured CUDA graphs give exactly the tokens of launching every kernel eagerly. Requests of different lengths
+    finish at different steps, so several row counts (several graphs) are exercised, and a sampled request keeps
+    its steps on the eager path."""
+    cfg = ModelConfig(vocab_size=1000, d_model=512, n_layers=3, n_heads=8, n_kv_heads=2, max_seq_len=640)
+    sd = O.test_model_weights(O.Cfg(**cfg.to_dict()), seed=21, scale=0.05)
+    m = ForgeModel(cfg, device="cuda")
+    m.load_state_dict(sd)
+    m = m.to(torch.bfloat16).eval()
+    gen = torch.Generator().manual_seed(9)
+    requests = [(torch.randint(0, 1000, (n,), generator=gen).tolist(), k)
+                for n, k in ((9, 30), (300, 12), (40, 25), (170, 30), (1, 7))]
+    outs = []
+    for graphs in (False, True):
+        eng = Engine(m, num_blocks=256, block_size=16, max_batch=5, cuda_graphs=graphs)
+        ids = [eng.add_request(p, k) for p, k in requests]
+        out = eng.run()
+        outs.append([out[i] for i in ids])
+        if graphs:
+            assert len(eng._graphs) >= 2
+    assert outs[0] == outs[1]

@@ -66,6 +66,29 @@ def test_gemm_tcgen05_swiglu(M, F, K):
     bf16_close(got, want, rel=2 ** -6)
 
 
+@pytest.mark.parametrize("epi", [L.FS_EPI_STORE, L.FS_EPI_RESIDUAL, L.FS_EPI_SWIGLU])
+@pytest.mark.parametrize("M,N,K", [(64, 6144, 4096), (1, 512, 4096), (100, 768, 2048), (64, 4096, 14336),
+                                   (33, 1002, 1024)])
+def test_gemm_split_k_small_m(epi, M, N, K):
+    """Few rows (decode steps): K is split over more CTAs and a second kernel sums the partials and applies the
+    epilogue (ragged N, N/2 not a multiple of 4 for SwiGLU, a single row)."""
+    a = torch.randn(M, K, device=DEV).bfloat16()
+    w = (torch.randn(N, K, device=DEV) / math.sqrt(K)).bfloat16()
+    if epi == L.FS_EPI_SWIGLU:
+        F = N // 2
+        got = ops.linear(a, w, epi)
+        g = (a.float() @ w[:F].float().t()).bfloat16()
+        u = (a.float() @ w[F:].float().t()).bfloat16()
+        bf16_close(got, torch.nn.functional.silu(g) * u, rel=2 ** -6)
+    elif epi == L.FS_EPI_RESIDUAL:
+        x = torch.randn(M, N, device=DEV).bfloat16()
+        want = x.float() + (a.float() @ w.float().t()).bfloat16().float()
+        ops.linear(a, w, epi, residual=x, out=x)
+        bf16_close(x, want)
+    else:
+        bf16_close(ops.linear(a, w), (a.double() @ w.double().t()).float())
+
+
 def test_gemm_tcgen05_strided_rows():
     """A operand that is a column slice of a wider buffer (row stride > K), as the q part of a qkv buffer."""
     buf = torch.randn(200, 384, device=DEV).bfloat16()
@@ -108,7 +131,7 @@ def rmsnorm_ref(x, w, eps):
 
 
 @pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
-@pytest.mark.parametrize("rows,dim", [(1, 64), (7, 128), (300, 4096), (5, 100)])
+@pytest.mark.parametrize("rows,dim", [(1, 64), (7, 128), (300, 4096), (5, 100), (33, 256), (17, 8192), (9, 768)])
 def test_rmsnorm(dtype, rows, dim):
     x = torch.randn(rows, dim, device=DEV).to(dtype) * 3
     w = (torch.rand(dim, device=DEV) + 0.5).to(dtype)
