@@ -3,17 +3,19 @@
 // Same semantics as attention.cu (forgeserve/model.py:69-76): GQA (query head h reads KV head h / rep), key slot s
 // visible to a query at position p iff s <= p and s < n_slots, scale 1/sqrt(hd), output bf16.
 //
-// One CTA computes 128 queries of one head against the keys 0 .. min(n_slots, max position + 1) - 1, 128 keys per
-// step:
+// One CTA computes 128 queries of one head against the keys 0 .. min(n_slots, max position + 1) - 1, 64 keys per
+// step; two CTAs share an SM (256 TMEM columns and ~97 KB of shared memory each), so one CTA's MMAs run during the
+// other's softmax:
 //   warp 4      TMA producer: the Q tile once; per step the K and V tiles, fetched in 16-key boxes through the
-//               block table (a paged pool's blocks or a contiguous cache's one block per row), 2-stage ring
+//               block table (a paged pool's blocks or a contiguous cache's one block per row), 2-stage rings
 //   warp 5      MMA issuer (one thread): S_j = Q K_j^T into one of two TMEM buffers; O += P_{j-1} V_{j-1} with
-//               P read from TMEM and V from shared memory (MN-major operand)
+//               P read from TMEM and V from shared memory (MN-major operand); S_j's buffer is released by the
+//               commit that follows P_j V_j
 //   warps 0-3   softmax, one thread per query row: S row from TMEM, causal mask, running max in the log2
-//               domain, P = exp2(S - m) packed to bf16 into TMEM (two P buffers, so P_j is written while
-//               P_{j-1} V_{j-1} runs); O rescaled in TMEM only when the running max grows by more than 2^8
-//               (otherwise the stale max is kept, bounding P by 2^8); final O / l to global
-// TMEM: S0 [0,128) S1 [128,256) P0 [256,320) P1 [320,384) O [384, 384+hd). Every wait is bounded (common.cuh).
+//               domain, P = exp2(S - m) packed to bf16 over the first half of S_j's columns; O rescaled in TMEM
+//               only when the running max grows by more than 2^8 (otherwise the stale max is kept, bounding P by
+//               2^8); final O / l to global
+// TMEM: S_0 [0,64) S_1 [64,128), P_j over the first half of S_j, O [128, 128+hd). Every wait is bounded (common.cuh).
 // No TMA multicast (the kernel also runs in multi-GPU jobs).
 #include <cudaTypedefs.h>
 
@@ -23,8 +25,10 @@
 namespace fs {
 namespace attn_tc {
 
-constexpr int BM = 128, BN = 128, CHUNK = 16, K_STAGES = 3, V_STAGES = 2, THREADS = 192;
-constexpr int S_COL = 0, P_COL = 256, O_COL = 384, TMEM_COLS = 512;
+constexpr int BM = 128, BN = 64, CHUNK = 16, K_STAGES = 2, V_STAGES = 2, THREADS = 192;
+// TMEM: S_0 [0, 64), S_1 [64, 128); P_j (bf16 pairs, 32 columns) is written over the first half of S_j's own
+// columns; O [128, 128 + hd). 256 columns, ~97 KB of shared memory: two CTAs share an SM.
+constexpr int S_COL = 0, O_COL = 2 * BN, TMEM_COLS = 256;
 constexpr float RESCALE_THRESHOLD = 8.0f;   // log2 units
 
 template <int HD>
@@ -115,7 +119,7 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
 }
 
 template <int HD>
-__global__ void __launch_bounds__(THREADS, 1)
+__global__ void __launch_bounds__(THREADS, 2)
     attn_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                    const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmK128,
                    const __grid_constant__ CUtensorMap tmV128, Params p) {
@@ -173,7 +177,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     }
     for (int s = 0; s < 2; ++s) {
       mbar_init(&s_full[s], 1);
-      mbar_init(&s_empty[s], BM);
+      mbar_init(&s_empty[s], 1);   // released by the commit after P_j V_j, which reads P_j from S_j's columns
     }
     mbar_init(p_full, BM);
     mbar_init(pv_done, 1);
@@ -281,7 +285,7 @@ __global__ void __launch_bounds__(THREADS, 1)
           const int hf = kk / 4, kq = kk % 4;
           const uint64_t adesc = sw128_kmajor_desc(q_addr + hf * G::Q_PANEL) + 2u * kq;
           const uint64_t bdesc = sw128_kmajor_desc(k_addr + hf * G::KV_PANEL) + 2u * kq;
-          tc_mma_f16(tmem + S_COL + (j & 1) * 128, adesc, bdesc, G::IDESC_S, kk != 0);
+          tc_mma_f16(tmem + S_COL + (j & 1) * BN, adesc, bdesc, G::IDESC_S, kk != 0);
         }
         tc_commit(&s_full[j & 1]);
         tc_commit(&k_empty[ks]);
@@ -297,10 +301,11 @@ __global__ void __launch_bounds__(THREADS, 1)
 #pragma unroll
         for (int kk = 0; kk < BN / 16; ++kk) {
           const uint64_t bdesc = sw128_mnmajor_desc(v_addr + kk * 2048u, G::KV_PANEL);
-          mma_ts(tmem + O_COL, tmem + P_COL + (j & 1) * (BN / 2) + kk * 8, bdesc, G::IDESC_O, (j | kk) != 0);
+          mma_ts(tmem + O_COL, tmem + S_COL + (j & 1) * BN + kk * 8, bdesc, G::IDESC_O, (j | kk) != 0);
         }
         tc_commit(pv_done);
         tc_commit(&v_empty[vs]);
+        tc_commit(&s_empty[j & 1]);   // S_j's columns (P_j) are free once P_j V_j has completed
         return true;
       };
       if (ok) ok = issue_s(0);
@@ -329,7 +334,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       tc_fence_after();
       const int64_t key0 = static_cast<int64_t>(j) * BN;
       const bool whole = key0 + BN - 1 <= last_vis;   // every key of the tile is visible to this row
-      const uint32_t s_addr = tmem + lane_base + S_COL + sb * 128;
+      const uint32_t s_addr = tmem + lane_base + S_COL + sb * BN;
       float m4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll 1
       for (int c = 0; c < BN / 32; ++c) {
@@ -355,7 +360,9 @@ __global__ void __launch_bounds__(THREADS, 1)
       const float corr = (need && m_ref != -INFINITY) ? exp2_approx(m_ref - m_new) : 1.f;
       if (need) m_ref = m_new;
       const float sub = m_ref == -INFINITY ? 0.f : m_ref;
-      const uint32_t p_addr = tmem + lane_base + P_COL + sb * (BN / 2);
+      // P chunk c goes to columns [16c, 16c + 16) of S_j: chunk c's scores (columns [32c, 32c + 32)) and every
+      // earlier chunk were read before it is stored
+      const uint32_t p_addr = s_addr;
       float s4[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll 1
       for (int c = 0; c < BN / 32; ++c) {
@@ -379,8 +386,6 @@ __global__ void __launch_bounds__(THREADS, 1)
         tmem_st_32x32b_x16(p_addr + c * 16, q16);
       }
       tc_wait_st();
-      tc_fence_before();
-      mbar_arrive(&s_empty[sb]);                   // S_j is no longer read
       l = l * corr + ((s4[0] + s4[1]) + (s4[2] + s4[3]));
       if (j >= 1) {
         // P V_{j-1} has completed (waited for in order, tile by tile, so the barrier's phase is never ambiguous)
@@ -408,7 +413,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         // for first (softmax j follows S_j, which only waited for K_j).
         ok = __all_sync(0xffffffffu, mbar_wait(&v_full[j % V_STAGES], (j / V_STAGES) & 1, p.err));
         if (!ok) break;
-        if (key0 + row >= n_keys) {
+        if (row < BN && key0 + row >= n_keys) {
           uint4* vrow = reinterpret_cast<uint4*>(smem + G::V_OFF + (j % V_STAGES) * G::KV_BYTES + row * 128);
 #pragma unroll
           for (int hf = 0; hf < G::HALVES; ++hf)
