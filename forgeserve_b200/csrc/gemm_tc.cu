@@ -30,11 +30,19 @@
 namespace fs {
 namespace tcg {
 
-constexpr int BM = 128, BN = 256, BK = 64, STAGES = 4;
+// A stage of the 1-SM kernel holds KP1 64-wide K panels of A and B (one k-block = 64 * KP1 of K).
+#ifndef FS_GEMM_KPANELS
+#define FS_GEMM_KPANELS 1
+#endif
+#ifndef FS_GEMM_STAGES
+#define FS_GEMM_STAGES (4 / FS_GEMM_KPANELS)
+#endif
+constexpr int KP1 = FS_GEMM_KPANELS;
+constexpr int BM = 128, BN = 256, BK = 64, STAGES = FS_GEMM_STAGES;
 constexpr int A_BYTES = BM * BK * 2;  // 16 KiB
 constexpr int B_BYTES = BN * BK * 2;  // 32 KiB (two 128-row halves)
 constexpr int BH_BYTES = B_BYTES / 2;
-constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+constexpr int STAGE_BYTES = KP1 * (A_BYTES + B_BYTES);
 constexpr int NUM_ACC = 2;
 constexpr int TMEM_COLS = NUM_ACC * BN;  // 512
 constexpr int THREADS = 256;
@@ -333,9 +341,14 @@ __global__ void __launch_bounds__(THREADS, 1)
             break;
           }
           mbar_arrive_expect_tx(&full[s], STAGE_BYTES);
-          tma_load_2d(tiles + s * STAGE_BYTES, &tmA, &full[s], kb * BK, m_blk * BM);
-          tma_load_2d(tiles + s * STAGE_BYTES + A_BYTES, &tmB, &full[s], kb * BK, b_row0);
-          tma_load_2d(tiles + s * STAGE_BYTES + A_BYTES + BH_BYTES, &tmB, &full[s], kb * BK, b_row1);
+#pragma unroll
+          for (int pk = 0; pk < KP1; ++pk) {
+            const int kx = (kb * KP1 + pk) * BK;
+            uint8_t* st = tiles + s * STAGE_BYTES;
+            tma_load_2d(st + pk * A_BYTES, &tmA, &full[s], kx, m_blk * BM);
+            tma_load_2d(st + KP1 * A_BYTES + pk * B_BYTES, &tmB, &full[s], kx, b_row0);
+            tma_load_2d(st + KP1 * A_BYTES + pk * B_BYTES + BH_BYTES, &tmB, &full[s], kx, b_row1);
+          }
           issued[s] = true;
           last_ph[s] = ph;
           if (++s == STAGES) s = 0, ph ^= 1u;
@@ -378,12 +391,15 @@ __global__ void __launch_bounds__(THREADS, 1)
           }
           tc_fence_after();
           const uint32_t a_addr = smem_u32(tiles + s * STAGE_BYTES);
-          const uint64_t adesc = sw128_kmajor_desc(a_addr);
-          const uint64_t bdesc = sw128_kmajor_desc(a_addr + A_BYTES);
 #pragma unroll
-          for (int k = 0; k < BK / 16; ++k) {
-            // +32 bytes along K inside the 128-byte swizzle row = +2 in the descriptor's address field
-            tc_mma_f16(d_tmem, adesc + 2u * k, bdesc + 2u * k, IDESC, (kb != kb0 || k != 0) ? 1u : 0u);
+          for (int pk = 0; pk < KP1; ++pk) {
+            const uint64_t adesc = sw128_kmajor_desc(a_addr + pk * A_BYTES);
+            const uint64_t bdesc = sw128_kmajor_desc(a_addr + KP1 * A_BYTES + pk * B_BYTES);
+#pragma unroll
+            for (int k = 0; k < BK / 16; ++k) {
+              // +32 bytes along K inside the 128-byte swizzle row = +2 in the descriptor's address field
+              tc_mma_f16(d_tmem, adesc + 2u * k, bdesc + 2u * k, IDESC, (kb != kb0 || pk != 0 || k != 0) ? 1u : 0u);
+            }
           }
           tc_commit(&empty[s]);  // the smem stage is free once these MMAs have read it
           if (++s == STAGES) s = 0, ph ^= 1u;
@@ -448,11 +464,17 @@ __global__ void __launch_bounds__(THREADS, 1)
 // traffic per FLOP drops by a third against the 1-SM kernel, and 6 stages fit. The leader CTA (rank 0) issues
 // the MMAs; every copy completes on the leader's barrier; the leader signals both CTAs' barriers; both CTAs'
 // epilogues read their own TMEM (their 128 rows) and report to the leader's accumulator-free barrier.
-#ifndef FS_GEMM_PAIR_STAGES
-#define FS_GEMM_PAIR_STAGES 6
+// A stage of the pair kernel holds KP 64-wide K panels of A and B (one k-block = 64 * KP of K); the ring keeps
+// ~192 KB of stages either way.
+#ifndef FS_GEMM_PAIR_KPANELS
+#define FS_GEMM_PAIR_KPANELS 2
 #endif
+#ifndef FS_GEMM_PAIR_STAGES
+#define FS_GEMM_PAIR_STAGES (6 / FS_GEMM_PAIR_KPANELS)
+#endif
+constexpr int KP = FS_GEMM_PAIR_KPANELS;
 constexpr int STAGES2 = FS_GEMM_PAIR_STAGES;
-constexpr int STAGE2_BYTES = A_BYTES + BH_BYTES;  // 32 KiB per CTA per k-block
+constexpr int STAGE2_BYTES = KP * (A_BYTES + BH_BYTES);  // 32 KiB per CTA per 64 of K
 constexpr int SMEM2_BYTES = STAGES2 * STAGE2_BYTES + 1024 + BAR_BYTES;
 constexpr uint32_t IDESC2 = idesc_bf16_f32(2 * BM, BN);
 
@@ -570,8 +592,12 @@ __global__ void __launch_bounds__(THREADS, 1)
           }
           const uint32_t leader_full = map_to_cta(smem_u32(&full[s]), 0);
           if (cta == 0) mbar_arrive_expect_tx(&full[s], 2 * STAGE2_BYTES);
-          tma_load_2d_pair(tiles + s * STAGE2_BYTES, &tmA, leader_full, kb * BK, a_row);
-          tma_load_2d_pair(tiles + s * STAGE2_BYTES + A_BYTES, &tmB, leader_full, kb * BK, b_row);
+#pragma unroll
+          for (int pk = 0; pk < KP; ++pk) {
+            tma_load_2d_pair(tiles + s * STAGE2_BYTES + pk * A_BYTES, &tmA, leader_full, (kb * KP + pk) * BK, a_row);
+            tma_load_2d_pair(tiles + s * STAGE2_BYTES + KP * A_BYTES + pk * BH_BYTES, &tmB, leader_full,
+                             (kb * KP + pk) * BK, b_row);
+          }
           if (++s == STAGES2) s = 0, ph ^= 1u;
         }
       }
@@ -597,10 +623,14 @@ __global__ void __launch_bounds__(THREADS, 1)
           }
           tc_fence_after();
           const uint32_t a_addr = smem_u32(tiles + s * STAGE2_BYTES);
-          const uint64_t adesc = sw128_kmajor_desc(a_addr);
-          const uint64_t bdesc = sw128_kmajor_desc(a_addr + A_BYTES);
 #pragma unroll
-          for (int k = 0; k < BK / 16; ++k) tc_mma_f16_pair(d_tmem, adesc + 2u * k, bdesc + 2u * k, IDESC2, (kb | k) != 0);
+          for (int pk = 0; pk < KP; ++pk) {
+            const uint64_t adesc = sw128_kmajor_desc(a_addr + pk * A_BYTES);
+            const uint64_t bdesc = sw128_kmajor_desc(a_addr + KP * A_BYTES + pk * BH_BYTES);
+#pragma unroll
+            for (int k = 0; k < BK / 16; ++k)
+              tc_mma_f16_pair(d_tmem, adesc + 2u * k, bdesc + 2u * k, IDESC2, (kb | pk | k) != 0);
+          }
           const uint32_t e = smem_u32(&empty[s]);
           tc_commit_pair(map_to_cta(e, 0));
           tc_commit_pair(map_to_cta(e, 1));
@@ -830,7 +860,7 @@ int gemm_tc(const void* A, int64_t lda, const void* B, int64_t ldb, void* C, int
   const int n_tile = epi == EPI_SWIGLU ? BN / 2 : BN;  // output columns per tile
   const int num_n_blocks = static_cast<int>((n_out + n_tile - 1) / n_tile);
   p.num_tiles = p.num_m_blocks * num_n_blocks;
-  p.k_blocks = static_cast<int>((K + BK - 1) / BK);
+  p.k_blocks = static_cast<int>((K + BK * KP1 - 1) / (BK * KP1));   // k-blocks of the 1-SM kernel
   p.sys_fence = sys_fence ? 1 : 0;
   p.sched = nullptr;
   p.k_split = 1;
@@ -840,6 +870,7 @@ int gemm_tc(const void* A, int64_t lda, const void* B, int64_t ldb, void* C, int
   p.err = error_word();
   if (!p.err) return -1;
   if (g_pair_mode && M > BM) {
+    p.k_blocks = static_cast<int>((K + BK * KP - 1) / (BK * KP));   // k-blocks of 64 * KP
     const int num_m_pairs = (p.num_m_blocks + 1) / 2;
     p.num_tiles = num_m_pairs * num_n_blocks;
     const int pairs = p.num_tiles < sm_count() / 2 ? p.num_tiles : sm_count() / 2;
