@@ -495,6 +495,33 @@ __device__ __forceinline__ void cluster_sync_all() {
 __device__ __forceinline__ void mbar_arrive_remote(uint32_t cluster_addr) {
   asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
 }
+__device__ __forceinline__ void st_cluster_u32(uint32_t cluster_addr, uint32_t v) {
+  asm volatile("st.shared::cluster.u32 [%0], %1;" ::"r"(cluster_addr), "r"(v) : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait_cluster(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// Bounded wait whose acquire covers writes the other CTA of the pair made before its release-arrive.
+__device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity, unsigned* err) {
+  if (mbar_try_wait_cluster(bar, parity)) return true;
+  const uint64_t t0 = globaltimer_ns();
+  uint32_t spins = 0;
+  while (true) {
+    if (mbar_try_wait_cluster(bar, parity)) return true;
+    if ((++spins & 255u) == 0 && globaltimer_ns() - t0 > kWaitLimitNs) {
+      flag_error(err, ERR_WAIT_TIMEOUT);
+      return false;
+    }
+  }
+}
 // 2-D TMA load into this CTA's shared memory whose completion is counted on a barrier of either CTA of the pair.
 __device__ __forceinline__ void tma_load_2d_pair(void* smem_dst, const CUtensorMap* map, uint32_t bar_cluster_addr,
                                                  int x, int y) {
@@ -544,10 +571,12 @@ __global__ void __launch_bounds__(THREADS, 1)
   uint64_t* mma_done = bars + 2 * STAGES2 + 2 * NUM_ACC;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  uint64_t* tq_full = reinterpret_cast<uint64_t*>(smem + STAGES2 * STAGE2_BYTES + 128);   // each CTA's own
+  uint64_t* tq_empty = tq_full + TQ;                                                     // the leader's is used
+  volatile int* tq = reinterpret_cast<volatile int*>(tq_empty + TQ);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t cta = cluster_ctarank();
-  const int pair = blockIdx.x >> 1, num_pairs = gridDim.x >> 1;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES2; ++s) {
@@ -557,6 +586,10 @@ __global__ void __launch_bounds__(THREADS, 1)
     for (int a = 0; a < NUM_ACC; ++a) {
       mbar_init(&tfull[a], 1);
       mbar_init(&tempty[a], 2 * 128);
+    }
+    for (int i = 0; i < TQ; ++i) {
+      mbar_init(&tq_full[i], 1);
+      mbar_init(&tq_empty[i], 2 + 1 + 2 * 4);   // both producers, the MMA thread, both CTAs' epilogue warps
     }
     mbar_init(mma_done, 1);
     *abort_flag = 0;
@@ -572,6 +605,14 @@ __global__ void __launch_bounds__(THREADS, 1)
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
   const int num_m_pairs = (p.num_m_blocks + 1) >> 1;
+  // Tile queue: the leader's producer claims a tile from the grid's counter and publishes it in both CTAs' queue
+  // slot (the peer's by a store to its shared memory and a release-arrive on its barrier); every consumer of the
+  // slot (both producers, the MMA thread, both CTAs' epilogue warps) releases it on the leader's tq_empty.
+  const uint32_t leader_tq_empty = map_to_cta(smem_u32(tq_empty), 0);
+  auto release_slot = [&](int slot) {
+    if (cta == 0) mbar_arrive(&tq_empty[slot]);
+    else mbar_arrive_remote(leader_tq_empty + 8u * static_cast<uint32_t>(slot));
+  };
 
   if (warp == 0) {
     // -------------------------------------------------------------------------------- TMA producer (both CTAs)
@@ -579,7 +620,28 @@ __global__ void __launch_bounds__(THREADS, 1)
       int s = 0;
       uint32_t ph = 0;
       bool ok = true;
-      for (int tile = pair; tile < p.num_tiles && ok; tile += num_pairs) {
+      for (int i = 0; ok; ++i) {
+        const int slot = i & (TQ - 1);
+        const uint32_t qph = static_cast<uint32_t>((i / TQ) & 1);
+        if (cta == 0) {
+          if (!mbar_wait_cluster(&tq_empty[slot], qph ^ 1u, p.err) || *abort_flag) {
+            ok = false;
+            break;
+          }
+          int claim = static_cast<int>(atomicAdd(p.sched, 1u));
+          if (claim >= p.num_tiles) claim = -1;
+          tq[slot] = claim;
+          st_cluster_u32(map_to_cta(smem_u32(const_cast<int*>(&tq[slot])), 1), static_cast<uint32_t>(claim));
+          mbar_arrive(&tq_full[slot]);
+          mbar_arrive_remote(map_to_cta(smem_u32(&tq_full[slot]), 1));
+        }
+        if (!mbar_wait_cluster(&tq_full[slot], qph, p.err) || *abort_flag) {
+          ok = false;
+          break;
+        }
+        const int tile = tq[slot];
+        release_slot(slot);
+        if (tile < 0) break;
         int m_pair, n_blk;
         tile_coords(tile, num_m_pairs, p.num_tiles / num_m_pairs, m_pair, n_blk);
         const int a_row = m_pair * 2 * BM + static_cast<int>(cta) * BM;
@@ -609,7 +671,15 @@ __global__ void __launch_bounds__(THREADS, 1)
       int s = 0, acc = 0;
       uint32_t ph = 0, acc_ph = 0;
       bool ok = true;
-      for (int tile = pair; tile < p.num_tiles && ok; tile += num_pairs) {
+      for (int i = 0; ok; ++i) {
+        const int slot = i & (TQ - 1);
+        if (!mbar_wait_cluster(&tq_full[slot], static_cast<uint32_t>((i / TQ) & 1), p.err) || *abort_flag) {
+          ok = false;
+          break;
+        }
+        const int tile = tq[slot];
+        release_slot(slot);
+        if (tile < 0) break;
         if (!mbar_wait(&tempty[acc], acc_ph ^ 1u, p.err) || *abort_flag) {
           ok = false;
           break;
@@ -654,7 +724,14 @@ __global__ void __launch_bounds__(THREADS, 1)
                         (EPI != EPI_RESIDUAL || (((p.ldr & 7) == 0) && ((reinterpret_cast<uintptr_t>(p.R) & 15) == 0)));
     int acc = 0;
     uint32_t acc_ph = 0;
-    for (int tile = pair; tile < p.num_tiles; tile += num_pairs) {
+    for (int i = 0;; ++i) {
+      const int slot = i & (TQ - 1);
+      if (!__all_sync(0xffffffffu, mbar_wait_cluster(&tq_full[slot], static_cast<uint32_t>((i / TQ) & 1), p.err)))
+        break;
+      const int tile = tq[slot];
+      __syncwarp();
+      if (lane == 0) release_slot(slot);
+      if (tile < 0) break;
       if (!warp_wait(&tfull[acc], acc_ph, p.err)) break;
       tc_fence_after();
       int m_pair, n_blk;
@@ -677,6 +754,14 @@ __global__ void __launch_bounds__(THREADS, 1)
     tmem_dealloc_pair(tmem_base, TMEM_COLS);
   }
   cluster_sync_all();   // neither CTA leaves while the other may still signal its barriers
+  if (threadIdx.x == 0) {
+    // every CTA has finished claiming once all have counted themselves out; the last one re-zeroes the counter
+    __threadfence();
+    if (atomicAdd(p.sched + 1, 1u) == gridDim.x - 1) {
+      atomicExch(p.sched, 0u);
+      atomicExch(p.sched + 1, 0u);
+    }
+  }
 }
 
 // ------------------------------------------------------------------------------------------------ host
@@ -871,6 +956,8 @@ int gemm_tc(const void* A, int64_t lda, const void* B, int64_t ldb, void* C, int
   if (!p.err) return -1;
   if (g_pair_mode && M > BM) {
     p.k_blocks = static_cast<int>((K + BK * KP - 1) / (BK * KP));   // k-blocks of 64 * KP
+    p.sched = sched_counter(stream);
+    if (!p.sched) return -1;
     const int num_m_pairs = (p.num_m_blocks + 1) / 2;
     p.num_tiles = num_m_pairs * num_n_blocks;
     const int pairs = p.num_tiles < sm_count() / 2 ? p.num_tiles : sm_count() / 2;

@@ -46,6 +46,7 @@ _PAIR_GROUPS: Dict[int, list] = {}
 # NCCL kernels stay resident on the SMs they run on while a receive waits for its data. Pipeline stages keep a
 # few SMs out of the persistent GEMM grid for them, and cap NCCL's point-to-point channels to match.
 COMM_SMS = int(os.environ.get("FORGESERVE_COMM_SMS", "12"))
+PAIR_GEMM = os.environ.get("FORGESERVE_PAIR_GEMM", "1") != "0"
 
 
 # The split output head (pipeline.py) uses one more communicator over all ranks: the last stage broadcasts each
@@ -85,9 +86,10 @@ class DistTransport:
                 from . import ops
                 sms = torch.cuda.get_device_properties(torch.cuda.current_device()).multi_processor_count
                 ops.set_persistent_sms(max(sms - COMM_SMS, 1))
-                # A CTA pair needs two free SMs of one GPC; NCCL kernels resident on scattered SMs break pairs up
-                # (measured on 4 GPUs: 830-910 TFLOP/s per middle stage against ~1200 for single-CTA tiles).
-                ops.set_gemm_pair_mode(False)
+                # A CTA pair needs two free SMs of one GPC, and NCCL kernels resident on scattered SMs delay some
+                # pairs; the GEMMs claim their tiles at run time, so a late pair just takes fewer tiles.
+                # FORGESERVE_PAIR_GEMM=0 keeps stages on single-CTA tiles.
+                ops.set_gemm_pair_mode(PAIR_GEMM)
 
     def _group_with(self, peer: int):
         if self.pairs is None:
