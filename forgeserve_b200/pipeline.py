@@ -94,6 +94,37 @@ def split_head_program(rank: int, size: int, microbatches: int) -> List[Tuple[st
     return out
 
 
+def ring_program(rank: int, size: int, microbatches: int, items: int) -> List[Tuple[str, int]]:
+    """Host order of one stage's work in overlapped greedy decoding (pipeline_generate with overlap).
+
+    Item k = (t - 1) * m + j feeds token t-1 of micro-batch j through the stages and yields token t. Ops:
+    ("tok_recv", k) on stage 0 / ("tok_send", k) on the last stage: token k (item k's input) over the ring
+    link last -> first; ("act_recv", k) / ("act_send", k): item k's activation from / to the neighbour;
+    ("compute", k): the stage's part of item k (stage 0 embeds, the last stage applies the head and takes the
+    argmax). With m >= p micro-batches, stage s runs item k in slot k + s: token k is ready at the end of the last
+    stage's slot k - m + p - 1 <= k - 1, so stage 0 never waits for it. Every rank posts its communication in one
+    global order (the slot boundary, then the sending stage), which NCCL needs across communicators."""
+    m, p, s = microbatches, size, rank
+    if m < p:
+        raise ValueError("overlapped decoding needs at least as many micro-batches as stages")
+    ops: List[Tuple[int, int, str, int]] = []   # (time, sending stage, op, item)
+    if s == p - 1:
+        for k in range(min(m, items)):             # the prefill's tokens start the ring
+            ops.append((0, p - 1, "tok_send", k))
+    for k in range(items):
+        if s == 0:
+            ops.append((0 if k < m else k - m + p, p - 1, "tok_recv", k))
+        else:
+            ops.append((k + s, s - 1, "act_recv", k))
+        ops.append((k + s, p + 1, "compute", k))     # after the slot's receives, before its sends
+        if s < p - 1:
+            ops.append((k + s + 1, s, "act_send", k))
+        elif k + m < items:
+            ops.append((k + s + 1, p - 1, "tok_send", k + m))
+    ops.sort()
+    return [(op, k) for _, _, op, k in ops]
+
+
 def microbatch_sizes(batch: int, microbatches: int) -> List[int]:
     """Row counts of torch.arange(batch).tensor_split(microbatches): the first batch % m parts get one extra."""
     base, extra = divmod(batch, microbatches)
@@ -424,13 +455,87 @@ def _forward_split_head(stage: PipelineStage, state: PipelineState, idx: Optiona
         w.wait()
 
 
+def _overlap_possible(stage: PipelineStage, microbatches: int, temperature: float) -> bool:
+    import torch.distributed as dist
+    from .transport import DistTransport
+    return (temperature == 0 and stage.size > 1 and microbatches >= stage.size
+            and isinstance(stage.transport, DistTransport) and dist.is_initialized()
+            and dist.get_backend() == "nccl")
+
+
+@torch.no_grad()
+def _generate_overlapped(stage: PipelineStage, prompt: torch.Tensor, n: int, microbatches: int) -> torch.Tensor:
+    """Greedy generation without draining the pipeline after every token (ring_program): after the prefill, the
+    last stage sends each micro-batch's new tokens straight to the first stage, which starts that micro-batch's
+    next step while the other stages still work on the other micro-batches. Same tokens as the step-by-step
+    loop; the full token matrix is broadcast from the last stage once, at the end."""
+    import torch.distributed as dist
+    from .transport import ring_group
+    p, r = stage.size, stage.rank
+    b, T = prompt.shape
+    dev, tr = stage.device, stage.transport
+    state = PipelineState(stage, b, microbatches)
+    sizes = state.sizes
+    m = len(sizes)
+    rows0 = [sum(sizes[:j]) for j in range(m)]
+    toks = torch.zeros(b, T + n, dtype=torch.int64, device=dev)
+    toks[:, :T].copy_(prompt.to(dev))
+    logits = pipeline_forward(stage, state, toks[:, :T] if stage.is_first else None, T, last_only=True)
+    if stage.is_last:
+        toks[:, T].copy_(ops.argmax(logits[:, -1]))
+    del logits
+    items = (n - 1) * m   # item k feeds token k // m of micro-batch k % m and yields the next one
+    ring = ring_group()
+    tok_in, act_in, act_out, sends = {}, {}, {}, []
+    for op, k in ring_program(r, p, m, items):
+        j, t = k % m, k // m
+        rows = slice(rows0[j], rows0[j] + sizes[j])
+        if op == "tok_send":
+            buf = toks[rows, T + t].contiguous()
+            sends.append((dist.isend(buf, dst=0, group=ring), buf))
+        elif op == "tok_recv":
+            buf = torch.empty(sizes[j], dtype=torch.int64, device=dev)
+            tok_in[k] = (dist.irecv(buf, src=p - 1, group=ring), buf)
+        elif op == "act_recv":
+            buf = torch.empty(sizes[j], 1, stage.cfg.d_model, dtype=stage.dtype, device=dev)
+            act_in[k] = (tr.irecv(buf, r - 1), buf)
+        elif op == "act_send":
+            sends.append((tr.isend(act_out.pop(k), r + 1), None))
+        else:
+            if stage.is_first:
+                work, tb = tok_in.pop(k)
+                work.wait()
+                x = stage.embed(tb.view(-1, 1))
+            else:
+                work, x = act_in.pop(k)
+                work.wait()
+            stage.run_layers_(x, _positions(T + t, 1, sizes[j], dev), state.caches[j])
+            if stage.is_last:
+                toks[rows, T + t + 1].copy_(ops.argmax(stage.head(x)[:, -1]))
+            else:
+                act_out[k] = x
+    for work, _ in sends:
+        work.wait()
+    tr.broadcast(toks, src=p - 1)
+    return toks
+
+
 @torch.no_grad()
 def pipeline_generate(stage: PipelineStage, prompt: torch.Tensor, max_new_tokens: int, microbatches: int = 1,
-                      temperature: float = 0.0, generator=None) -> torch.Tensor:
+                      temperature: float = 0.0, generator=None, overlap: Optional[bool] = None) -> torch.Tensor:
     """Generate with the pipeline. Every stage calls this with the same `prompt` (B, T) and gets the same result
-    (on the prompt's device). The last stage samples; the tokens are broadcast from it (pipeline.py:121-137)."""
+    (on the prompt's device). The last stage samples; the tokens are broadcast from it (pipeline.py:121-137).
+
+    overlap (extra): greedy decoding with at least as many micro-batches as stages, one process per GPU over
+    NCCL, can overlap successive steps (_generate_overlapped) instead of draining the pipeline after every token;
+    None picks it whenever it applies. The tokens are the same either way."""
     b, t = prompt.shape
     max_new_tokens = min(max_new_tokens, stage.cfg.max_seq_len - t)
+    possible = _overlap_possible(stage, microbatches, temperature)
+    if overlap and not possible:
+        raise ValueError("overlapped decoding needs temperature 0, micro-batches >= stages >= 2, and NCCL ranks")
+    if (overlap is None or overlap) and possible and max_new_tokens > 0:
+        return _generate_overlapped(stage, prompt, max_new_tokens, microbatches).to(prompt.device)
     state = PipelineState(stage, b, microbatches)
     dev = stage.device
     toks = torch.empty(b, t + max(max_new_tokens, 0), dtype=torch.int64, device=dev)

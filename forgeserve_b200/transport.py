@@ -67,6 +67,18 @@ def head_group():
     return _HEAD_GROUPS[world]
 
 
+# Overlapped greedy decoding (pipeline.py) sends each new token from the last stage straight to the first over a
+# communicator of its own (with two stages this is a second communicator between the same two ranks).
+_RING_GROUPS: Dict[int, object] = {}
+
+
+def ring_group():
+    world = dist.get_world_size()
+    if world not in _RING_GROUPS:
+        _RING_GROUPS[world] = dist.new_group([0, world - 1])
+    return _RING_GROUPS[world]
+
+
 def _pair_groups():
     world = dist.get_world_size()
     if world not in _PAIR_GROUPS:

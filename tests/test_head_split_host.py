@@ -81,3 +81,64 @@ def test_receives_posted_up_front_deadlock_in_the_model():
     last = progs[-1]
     progs[-1] = [op for op in last if op[0] == "recv"] + [op for op in last if op[0] != "recv"]
     assert not run_serialised(progs)
+
+
+# ------------------------------------------------------------------------ overlapped decoding (token ring)
+from forgeserve_b200.pipeline import ring_program
+
+
+def _ring_op(kind, k, rank, size):
+    if kind in ("tok_send", "tok_recv"):
+        return ("T", k)
+    if kind == "act_send":
+        return ("A", rank, k)
+    if kind == "act_recv":
+        return ("A", rank - 1, k)
+    return None
+
+
+def run_ring_serialised(size, progs):
+    pc = [0] * size
+    while True:
+        for r in range(size):
+            while pc[r] < len(progs[r]) and _ring_op(*progs[r][pc[r]], r, size) is None:
+                pc[r] += 1
+        if all(pc[r] == len(progs[r]) for r in range(size)):
+            return True
+        waiting = {}
+        for r in range(size):
+            if pc[r] < len(progs[r]):
+                waiting.setdefault(_ring_op(*progs[r][pc[r]], r, size), []).append(r)
+        fired = [op for op, ranks in waiting.items() if len(ranks) == 2]
+        if not fired:
+            return False
+        for op in fired:
+            for r in waiting[op]:
+                pc[r] += 1
+
+
+@pytest.mark.parametrize("size,m", [(2, 2), (2, 3), (2, 5), (3, 3), (3, 4), (4, 4), (4, 7), (8, 8), (8, 16)])
+@pytest.mark.parametrize("steps", [1, 2, 5])
+def test_ring_program_is_complete_ordered_and_completes_serialised(size, m, steps):
+    items = steps * m
+    progs = [ring_program(r, size, m, items) for r in range(size)]
+    for r, prog in enumerate(progs):
+        assert [k for op, k in prog if op == "compute"] == list(range(items))
+        for k in range(items):
+            c = prog.index(("compute", k))
+            if r == 0:
+                assert prog.index(("tok_recv", k)) < c
+            else:
+                assert prog.index(("act_recv", k)) < c
+            if r < size - 1:
+                assert c < prog.index(("act_send", k))
+            elif k + m < items:
+                assert c < prog.index(("tok_send", k + m))
+    sends = [k for op, k in progs[-1] if op == "tok_send"]
+    assert sorted(sends) == list(range(items)) and [k for op, k in progs[0] if op == "tok_recv"] == sends
+    assert run_ring_serialised(size, progs)
+
+
+def test_ring_program_needs_enough_microbatches():
+    with pytest.raises(ValueError):
+        ring_program(0, 4, 3, 10)
