@@ -225,7 +225,8 @@ def run_ours(args):
             "bubble": {"measured": round(1.0 - busy_sum / (world * ms_max), 4),
                        "analytic": round(bubble_fraction(world, MICROBATCHES), 4)},
             "model_tflops": round(step_flops * args.steps / (ms_max / 1e3) / 1e12, 1),
-            "roofline": {"bound": "tensor", "kernel": "gemm_tc_kernel (every projection GEMM of the timed region)",
+            "roofline": {"bound": "tensor",
+                         "kernel": "gemm_tc2_kernel, the 2-SM tcgen05 GEMM (every projection GEMM of the timed region)",
                          "achieved": round(achieved, 1) if achieved else None, "peak": peak, "unit": "TFLOP/s",
                          "frac": round(achieved / peak, 4) if achieved else None, "peak_source": peak_src,
                          "launches": int(gemm_n), "traffic": gemm_traffic()},
