@@ -91,6 +91,13 @@ __device__ __forceinline__ void tmem_st_32x32b_x32(uint32_t taddr, const uint32_
       "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
       : "memory");
 }
+// 32 lanes x 64 columns of 32-bit TMEM -> 64 registers per thread (thread i reads lane base + i).
+__device__ __forceinline__ void tmem_ld_32x32b_x64(uint32_t taddr, uint32_t (&r)[64]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x64.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32,%33,%34,%35,%36,%37,%38,%39,%40,%41,%42,%43,%44,%45,%46,%47,%48,%49,%50,%51,%52,%53,%54,%55,%56,%57,%58,%59,%60,%61,%62,%63}, [%64];"
+      : "=r"(r[0]),"=r"(r[1]),"=r"(r[2]),"=r"(r[3]),"=r"(r[4]),"=r"(r[5]),"=r"(r[6]),"=r"(r[7]),"=r"(r[8]),"=r"(r[9]),"=r"(r[10]),"=r"(r[11]),"=r"(r[12]),"=r"(r[13]),"=r"(r[14]),"=r"(r[15]),"=r"(r[16]),"=r"(r[17]),"=r"(r[18]),"=r"(r[19]),"=r"(r[20]),"=r"(r[21]),"=r"(r[22]),"=r"(r[23]),"=r"(r[24]),"=r"(r[25]),"=r"(r[26]),"=r"(r[27]),"=r"(r[28]),"=r"(r[29]),"=r"(r[30]),"=r"(r[31]),"=r"(r[32]),"=r"(r[33]),"=r"(r[34]),"=r"(r[35]),"=r"(r[36]),"=r"(r[37]),"=r"(r[38]),"=r"(r[39]),"=r"(r[40]),"=r"(r[41]),"=r"(r[42]),"=r"(r[43]),"=r"(r[44]),"=r"(r[45]),"=r"(r[46]),"=r"(r[47]),"=r"(r[48]),"=r"(r[49]),"=r"(r[50]),"=r"(r[51]),"=r"(r[52]),"=r"(r[53]),"=r"(r[54]),"=r"(r[55]),"=r"(r[56]),"=r"(r[57]),"=r"(r[58]),"=r"(r[59]),"=r"(r[60]),"=r"(r[61]),"=r"(r[62]),"=r"(r[63])
+      : "r"(taddr));
+}
 __device__ __forceinline__ void tc_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 __device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 
@@ -335,22 +342,19 @@ __global__ void __launch_bounds__(THREADS, 2)
       const int64_t key0 = static_cast<int64_t>(j) * BN;
       const bool whole = key0 + BN - 1 <= last_vis;   // every key of the tile is visible to this row
       const uint32_t s_addr = tmem + lane_base + S_COL + sb * BN;
-      float m4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
-#pragma unroll 1
-      for (int c = 0; c < BN / 32; ++c) {
-        uint32_t t[32];
-        tmem_ld_32x32b_x32(s_addr + c * 32, t);
-        tc_wait_ld();
-        tmem_regs_ready(t);
-        if (whole) {
+      static_assert(BN == 64, "the softmax holds one 64-column S row in registers");
+      uint32_t t[BN];   // the row's scores: one TMEM load serves both passes
+      tmem_ld_32x32b_x64(s_addr, t);
+      tc_wait_ld();
+      tmem_regs_ready(t);
+      if (!whole) {
 #pragma unroll
-          for (int i = 0; i < 32; ++i) m4[i & 3] = fmaxf(m4[i & 3], __uint_as_float(t[i]));
-        } else {
-          const int64_t k0 = key0 + c * 32;
-#pragma unroll
-          for (int i = 0; i < 32; ++i) m4[i & 3] = fmaxf(m4[i & 3], k0 + i <= last_vis ? __uint_as_float(t[i]) : -INFINITY);
-        }
+        for (int i = 0; i < BN; ++i)
+          if (key0 + i > last_vis) t[i] = __float_as_uint(-INFINITY);
       }
+      float m4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+#pragma unroll
+      for (int i = 0; i < BN; ++i) m4[i & 3] = fmaxf(m4[i & 3], __uint_as_float(t[i]));
       const float mx = fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3])) * p.scale_log2;   // log2 domain
       const float m_new = fmaxf(m_ref, mx);
       // Whether a row moves its reference max is decided per row, but the TMEM accesses that rescale O are
@@ -360,31 +364,17 @@ __global__ void __launch_bounds__(THREADS, 2)
       const float corr = (need && m_ref != -INFINITY) ? exp2_approx(m_ref - m_new) : 1.f;
       if (need) m_ref = m_new;
       const float sub = m_ref == -INFINITY ? 0.f : m_ref;
-      // P chunk c goes to columns [16c, 16c + 16) of S_j: chunk c's scores (columns [32c, 32c + 32)) and every
-      // earlier chunk were read before it is stored
-      const uint32_t p_addr = s_addr;
+      // P (bf16 pairs, 32 columns) over the first half of S_j's columns: the whole row is in registers already
       float s4[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll 1
-      for (int c = 0; c < BN / 32; ++c) {
-        uint32_t t[32], q16[16];
-        tmem_ld_32x32b_x32(s_addr + c * 32, t);
-        tc_wait_ld();
-        tmem_regs_ready(t);
-        const int64_t k0 = key0 + c * 32;
+      uint32_t pk[BN / 2];
 #pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          float x0 = __uint_as_float(t[2 * i]), x1 = __uint_as_float(t[2 * i + 1]);
-          if (!whole) {
-            x0 = k0 + 2 * i <= last_vis ? x0 : -INFINITY;
-            x1 = k0 + 2 * i + 1 <= last_vis ? x1 : -INFINITY;
-          }
-          const float p0 = exp2_approx(fmaf(x0, p.scale_log2, -sub));
-          const float p1 = exp2_approx(fmaf(x1, p.scale_log2, -sub));
-          s4[i & 3] += p0 + p1;
-          q16[i] = pack_bf16x2(p0, p1);
-        }
-        tmem_st_32x32b_x16(p_addr + c * 16, q16);
+      for (int i = 0; i < BN / 2; ++i) {
+        const float p0 = exp2_approx(fmaf(__uint_as_float(t[2 * i]), p.scale_log2, -sub));
+        const float p1 = exp2_approx(fmaf(__uint_as_float(t[2 * i + 1]), p.scale_log2, -sub));
+        s4[i & 3] += p0 + p1;
+        pk[i] = pack_bf16x2(p0, p1);
       }
+      tmem_st_32x32b_x32(s_addr, pk);
       tc_wait_st();
       l = l * corr + ((s4[0] + s4[1]) + (s4[2] + s4[3]));
       if (j >= 1) {
