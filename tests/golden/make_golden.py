@@ -20,9 +20,12 @@ import torch
 
 HERE = Path(__file__).resolve().parent
 ROOT = HERE.parents[1]
-REF = os.environ.get("FORGESERVE_REFERENCE", "/root/reference")
+# The reference checkout to import (its `forgeserve` package): --reference <dir> or FORGESERVE_REFERENCE.
+REF = os.environ.get("FORGESERVE_REFERENCE")
 if "--reference" in sys.argv:
     REF = sys.argv[sys.argv.index("--reference") + 1]
+if not REF:
+    raise SystemExit("make_golden.py: pass --reference <reference checkout> or set FORGESERVE_REFERENCE")
 sys.path.insert(0, REF)
 sys.path.insert(0, str(ROOT))
 
