@@ -24,6 +24,7 @@ from .model import Block, RMSNorm, RopeTables, layer_forward_
 from .parallel import SINGLE
 from .sampling import sample
 from .transport import default_transport
+from .weights import open_state_dict
 
 
 def stage_layers(n_layers: int, size: int) -> List[Tuple[int, int]]:
@@ -182,6 +183,11 @@ class PipelineStage(nn.Module):
         hs = self.head_split
         if hs is not None and not self.is_last and "lm_head.weight" in full:
             hs.weight.copy_(full["lm_head.weight"][hs.lo : hs.hi])
+
+    def load_from_file(self, path) -> None:
+        """load_from_full on a state dict saved with torch.save, memory-mapped (weights.open_state_dict): only
+        this stage's tensors are read from the file, so no process holds the whole model in host memory."""
+        self.load_from_full(open_state_dict(path))
 
     def split_head_(self, transfer: str = "copy") -> None:
         """Spread the output head over all stages. Collective: every stage calls it once its weights are set.

@@ -1,9 +1,14 @@
-"""Seeded weights in the reference's state-dict format, generated per tensor.
+"""Weights in the reference's state-dict format: seeded per tensor, or memory-mapped from a saved state dict.
 
 Every tensor is drawn from its own generator, seeded from (seed, tensor name), so a pipeline stage can build
 exactly its own layers — on its GPU, without materialising the full model — and still hold the same values
 as a single-process model built from the same seed. Names are the reference's state-dict keys
 (forgeserve/model.py:109-138; `lm_head.weight` equals `tok_emb.weight`, as ForgeModel ties them).
+
+A saved model is a `torch.save` of `ForgeModel.state_dict()` (the reference's format; any subset of its keys
+works too). `open_state_dict` maps such a file instead of reading it, so a stage that loads from it with
+`PipelineStage.load_from_full` reads only its own tensors' pages: at the 70B shape the full fp32 dict is about
+274 GB, more than a host holds, while one of 8 stages needs about 35 GB of it.
 """
 
 import hashlib
@@ -61,6 +66,13 @@ def seeded_state_dict(cfg: ModelConfig, seed: int = 0, std: float = 0.02, names:
     shapes = model_shapes(cfg)
     keys = list(shapes) if names is None else list(names)
     return {k: seeded_tensor(k, shapes[k], seed, std, device, dtype) for k in keys}
+
+
+def open_state_dict(path) -> Dict[str, torch.Tensor]:
+    """The state dict saved at `path`, memory-mapped: CPU tensors that are views of the file's pages (tied
+    tensors, such as the reference's `lm_head.weight` and `tok_emb.weight`, stay one storage). Nothing is read
+    until a tensor's elements are used."""
+    return torch.load(path, map_location="cpu", mmap=True, weights_only=True)
 
 
 @torch.no_grad()

@@ -1,6 +1,8 @@
 """Host-side logic of forgeserve_b200 that needs no GPU: configuration, stage split, micro-batch rows, block
 allocation, stage construction and weight loading, the fused-weight views, the export list."""
 
+import os
+
 import pytest
 import torch
 
@@ -141,3 +143,48 @@ def test_out_of_scope_names_refuse():
         fs.speculative_generate(None, None, None, 1)
     with pytest.raises(NotImplementedError):
         fs.ForgeModel(small_cfg(), fs.TPContext(0, 2))
+
+
+def _mapped_ranges(path):
+    """Address ranges of this process's mappings of `path` (Linux /proc/self/maps)."""
+    real = os.path.realpath(path)
+    out = []
+    with open("/proc/self/maps") as f:
+        for line in f:
+            parts = line.split()
+            if len(parts) >= 6 and parts[5] == real:
+                lo, hi = (int(x, 16) for x in parts[0].split("-"))
+                out.append((lo, hi))
+    return out
+
+
+def test_stages_load_from_a_mapped_state_dict_file(tmp_path):
+    """Per-stage loading from the reference's saved format (torch.save of the state dict, tied head): the file is
+    mapped, not read, and each stage ends up with the same weights as load_from_full of the in-memory dict."""
+    from forgeserve_b200.weights import open_state_dict
+    cfg = small_cfg(n_layers=5)
+    full = O.test_model_weights(O.Cfg(**cfg.to_dict()), seed=6)
+    assert full["lm_head.weight"] is full["tok_emb.weight"]
+    path = tmp_path / "model.pt"
+    torch.save(full, path)
+    mapped = open_state_dict(path)
+    assert set(mapped) == set(full)
+    ranges = _mapped_ranges(path)
+    assert ranges, "the state dict file is not memory-mapped"
+    for k, t in mapped.items():
+        assert any(lo <= t.data_ptr() < hi for lo, hi in ranges), k      # a view of the file, not a host copy
+    assert mapped["lm_head.weight"].data_ptr() == mapped["tok_emb.weight"].data_ptr()
+    for rank in range(3):
+        a = PipelineStage(cfg, rank, 3, device="cpu")
+        a.load_from_file(path)
+        b = PipelineStage(cfg, rank, 3, device="cpu")
+        b.load_from_full(full)
+        sa, sb = a.state_dict(), b.state_dict()
+        assert set(sa) == set(sb)
+        for k in sa:
+            assert torch.equal(sa[k], sb[k]), (rank, k)
+    # a stage built in bf16 takes the fp32 file's tensors rounded, as load_from_full does
+    c = PipelineStage(cfg, 1, 3, device="cpu", dtype=torch.bfloat16)
+    c.load_from_file(path)
+    lo = c.lo
+    assert torch.equal(c.layers[0].mlp.w_down.weight, full[f"layers.{lo}.mlp.w_down.weight"].to(torch.bfloat16))
