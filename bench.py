@@ -280,7 +280,7 @@ def run_c4(args):
         stage = PipelineStage(cfg, rank, world, device=dev, dtype=torch.bfloat16).eval()
         init_stage_(stage, seed=1234, std=0.02)
         engine = PipelineEngine(stage, C4["num_blocks"], C4["block_size"], max_batch=C4["requests"], seed=0,
-                                microbatches=args.microbatches or world)
+                                microbatches=args.microbatches or world, overlap=False if args.no_windows else None)
         weight_bytes = sum(p.numel() * p.element_size() for p in stage.parameters())
     rng = random.Random(11)
     lengths = [rng.randint(C4["prompt_lo"], C4["prompt_hi"]) for _ in range(C4["requests"])]
@@ -296,19 +296,17 @@ def run_c4(args):
         e_dec = torch.cuda.Event(enable_timing=True)
         e1 = torch.cuda.Event(enable_timing=True)
         e0.record(stream)
-        decode_steps, marked = 0, False
-        while engine.has_work():
-            if not engine.waiting and not marked:
-                e_dec.record(stream)
-                marked = True
-            decoding = not engine.waiting
+        while engine.waiting:            # prefill phase: one request per step (decodes only while blocks lack)
             engine.step()
-            decode_steps += decoding
+        e_dec.record(stream)
+        steps0 = engine.steps
+        engine.run()                     # decode phase (on a pipeline: decode windows, unless --no-windows)
+        decode_steps = engine.steps - steps0
         e1.record(stream)
         torch.cuda.synchronize()
         outs = {rid: r.output for rid, r in engine.requests.items()}
         engine.requests.clear()
-        return e0.elapsed_time(e1), (e_dec.elapsed_time(e1) if marked else 0.0), decode_steps, outs
+        return e0.elapsed_time(e1), e_dec.elapsed_time(e1), decode_steps, outs
 
     for _ in range(max(args.warmup, 1)):
         one_run(prompts[:8], 16)
@@ -358,7 +356,8 @@ def run_c4(args):
             "data": "synthetic: seeded prompt lengths and token ids, seeded N(0, 0.02) weights",
             "config": {"workload": C4_WORKLOAD, "stages": world, "parallelism": f"pp{world}",
                        "microbatches": 1 if world == 1 else (args.microbatches or world),
-                       "decode_cuda_graphs": world == 1 and not args.no_graphs},
+                       "decode_cuda_graphs": world == 1 and not args.no_graphs,
+                       "decode_windows": getattr(engine, "windows", 0)},
             "decode": {"tokens_per_s": round(dec_tokens / (dec_ms / 1e3), 1), "steps": steps_dec,
                        "ms_per_step": round(step_ms, 3)},
             "roofline": {"bound": "hbm", "kernel": "whole decode step (weights + K/V of every cached token)",
@@ -555,6 +554,7 @@ def main():
                     help="c3: pipeline prefill (the headline metric); c4: continuous-batching decode")
     ap.add_argument("--microbatches", type=int, default=0, help="c4 with N > 1: micro-batches per engine step")
     ap.add_argument("--no-graphs", action="store_true", help="c4: launch every decode kernel from Python")
+    ap.add_argument("--no-windows", action="store_true", help="c4 with N > 1: drain the pipeline after every step")
     ap.add_argument("--profile-case", default=None, help="run a few launches of one kernel (for ncu) and exit")
     ap.add_argument("--reps", type=int, default=3)
     ap.add_argument("--timed", action="store_true", help="with --profile-case: also time cold-L2 launches")

@@ -68,9 +68,17 @@ class Scheduler:
         return bool(self.waiting or self.running)
 
     def run(self) -> Dict[int, List[int]]:
-        """Step until every request is finished. Returns the generated tokens of each request."""
+        """Step until every request is finished. Returns the generated tokens of each request.
+
+        A subclass that can run several decode steps without waiting for each step's tokens (`_windowed`,
+        `_decode_window`: PipelineEngine over NCCL ranks) takes them a window at a time; the outputs, block
+        tables and counters are those of stepping one by one."""
         while self.has_work():
-            self.step()
+            w = self._window_steps() if self._windowed() else 0
+            if w >= 2:
+                self._decode_window(w)
+            else:
+                self.step()
         return {rid: r.output for rid, r in self.requests.items()}
 
     def step(self) -> None:
@@ -81,9 +89,7 @@ class Scheduler:
             self._decode()
         elif self.waiting:
             raise RuntimeError("the head request cannot be scheduled: the block pool is too small")
-        used = self.pool.allocator.num_blocks - self.pool.allocator.num_free
-        self.peak_running = max(self.peak_running, len(self.running))
-        self.peak_blocks = max(self.peak_blocks, used)
+        self._record_peaks()
 
     # ---- scheduling ------------------------------------------------------------------------------------
     def _try_prefill(self) -> bool:
@@ -144,10 +150,82 @@ class Scheduler:
                       tables: torch.Tensor) -> List[int]:
         raise NotImplementedError
 
+    # ---- decode windows ----------------------------------------------------------------------------------
+    def _windowed(self) -> bool:
+        """Whether `_decode_window` can run now (the subclass's execution conditions)."""
+        return False
+
+    def _decode_window(self, w: int) -> None:
+        raise NotImplementedError
+
+    def _window_steps(self) -> int:
+        """How many decode steps, from the next one on, the scheduler takes over the current running rows whatever
+        tokens they sample; 0 if the next step is not a decode of rows that are all greedy with no eos.
+
+        Without eos, a row finishes when its length says so (max_new_tokens, max_seq_len), and the block grants
+        (_grant_blocks) depend on lengths only; a prefill that cannot get its blocks now cannot later in the window,
+        since grants only take blocks. The window ends at the first step where a row finishes, or before the first
+        step whose grants would find the pool empty (the step-by-step scheduler preempts there)."""
+        if not self.running or any(r.temperature != 0 or r.eos_id is not None for r in self.running):
+            return 0
+        if self.waiting and len(self.running) < self.max_batch:
+            head = self.waiting[0]
+            if self.pool.blocks_for(len(head.prompt) + len(head.output)) <= self.pool.allocator.num_free:
+                return 0                                 # the next step prefills
+        w = min(min(r.max_new_tokens - len(r.output), self.cfg.max_seq_len - len(r.prompt) - len(r.output))
+                for r in self.running)
+        bs, free = self.pool.block_size, self.pool.allocator.num_free
+        nblocks = [len(r.blocks) for r in self.running]
+        for t in range(w):
+            for i, r in enumerate(self.running):
+                pos = r.cached + t
+                if pos % bs == 0 and pos // bs == nblocks[i]:
+                    if free == 0:
+                        return t
+                    free -= 1
+                    nblocks[i] += 1
+        return w
+
+    def _window_step(self, rows: List[Request], cached: List[int], t: int, last: bool):
+        """Step t of a decode window over `rows` (their cache lengths `cached` at the window's start): the step's
+        block grants in row order, as _grant_blocks makes them (none preempts inside a window), its counters, and
+        the (block tables, positions) that _decode would pass for it."""
+        self.steps += 1
+        bs = self.pool.block_size
+        for req, c in zip(rows, cached):
+            if (c + t) % bs == 0 and (c + t) // bs == len(req.blocks):
+                req.blocks += self.pool.allocator.allocate(1)
+        if not last:                                     # as step() records them after a decode with no finish
+            self._record_peaks()
+        width = max(len(r.blocks) for r in rows)
+        tables = torch.tensor([r.blocks + [0] * (width - len(r.blocks)) for r in rows])
+        positions = torch.tensor([[c + t] for c in cached])
+        return tables, positions
+
+    def _window_end(self, rows: List[Request], tokens: List[List[int]]) -> None:
+        """Append a window's tokens (tokens[t][i]: step t, row i) as _decode appends them step by step."""
+        for t, step_tokens in enumerate(tokens):
+            for req, tok in zip(rows, step_tokens):
+                req.cached += 1
+                self._append(req, tok)
+                if req.finished:
+                    if t != len(tokens) - 1:
+                        raise RuntimeError("a row finished inside a decode window")
+                    self.running.remove(req)
+        self._record_peaks()
+
+    def _record_peaks(self) -> None:
+        used = self.pool.allocator.num_blocks - self.pool.allocator.num_free
+        self.peak_running = max(self.peak_running, len(self.running))
+        self.peak_blocks = max(self.peak_blocks, used)
+
+    def _argmax(self, logits: torch.Tensor) -> torch.Tensor:
+        return ops.argmax(logits)
+
     def _sample_rows(self, logits: torch.Tensor, reqs: List[Request]) -> List[int]:
         """One token per row of logits (R, V): greedy rows by one argmax kernel, the others from the engine's
         generator in row order."""
-        greedy = ops.argmax(logits).cpu().tolist()
+        greedy = self._argmax(logits).cpu().tolist()
         out = []
         for r, req in enumerate(reqs):
             if req.temperature == 0:

@@ -9,25 +9,40 @@ layers (`PagedKVPool(..., n_layers=len(stage.layers))`), indexed by the same blo
 One step (a prefill of one request, or one decode token for every running request) goes through the stages in
 `microbatches` groups of rows: stage s runs group i while stage s+1 runs group i-1, and the last stage computes the
 head for the last position only and samples.
+
+Decode windows (`run`, one process per stage over torch.distributed): while the running rows are all greedy with
+no eos, the scheduler's next steps do not depend on the tokens (Scheduler._window_steps), so every stage plans
+them ahead and the rows' groups go round the pipeline without a drain after each step: the last stage sends each
+group's new tokens straight to the first (ring_program, as pipeline_generate's overlapped loop), and stage s works
+on step t's group j while the first stage already runs step t+1's earlier groups. With at least as many groups as
+stages no stage waits for a token. The tokens reach every stage with one broadcast at the end of the window.
 """
 
-from typing import List
+from typing import List, Optional
 
 import torch
+import torch.distributed as dist
 
-from . import ops
 from .engine import Request, Scheduler
 from .paged import PagedKVPool
-from .pipeline import microbatch_sizes
+from .pipeline import microbatch_sizes, ring_program
+from .transport import DistTransport, ring_group
 
 
 class PipelineEngine(Scheduler):
+    """overlap (extra): None or True takes decode windows whenever they apply (the tokens, block tables and
+    counters are those of stepping one by one); False steps one by one, draining the pipeline every step."""
+
+    MAX_WINDOW = 64     # decode steps per window: bounds what the host enqueues ahead of the GPUs
+
     def __init__(self, stage, num_blocks: int, block_size: int = 16, max_batch: int = 8, seed: int = 0,
-                 microbatches: int = 1):
+                 microbatches: int = 1, overlap: Optional[bool] = None):
         self.stage, self.cfg = stage, stage.cfg
         self.pool = PagedKVPool(self.cfg, num_blocks, block_size, dtype=stage.dtype, device=stage.device,
                                 n_layers=len(stage.layers))
         self.microbatches = max(1, microbatches)
+        self.overlap = overlap
+        self.windows = 0          # decode windows taken by run()
         self._init_scheduler(max_batch, seed)
 
     def _forward_rows(self, reqs: List[Request], idx: torch.Tensor, positions: torch.Tensor,
@@ -70,3 +85,73 @@ class PipelineEngine(Scheduler):
             tokens = torch.empty(R, dtype=torch.int64, device=dev)
         tr.broadcast(tokens, src=st.size - 1)
         return tokens.cpu().tolist()
+
+    # ---- decode windows ----------------------------------------------------------------------------------
+    def _windowed(self) -> bool:
+        st = self.stage
+        if self.overlap is False or st.size < 2 or min(self.microbatches, len(self.running)) < st.size:
+            return False
+        if not (isinstance(st.transport, DistTransport) and st.transport.group is None and dist.is_initialized()):
+            return False
+        backend = dist.get_backend()
+        return backend == "nccl" or (backend == "gloo" and st.device.type == "cpu")
+
+    def _window_steps(self) -> int:
+        return min(super()._window_steps(), self.MAX_WINDOW)
+
+    @torch.no_grad()
+    def _decode_window(self, w: int) -> None:
+        """w decode steps of the running rows, in groups, over ring_program's order (item k = step k // m of
+        group k % m). Every stage makes each step's block grants, tables and positions (Scheduler._window_step)
+        when it first computes a group of that step, in step order on every stage; the first stage takes a
+        group's input tokens from the ring (for the first step, the known last tokens, sent by the last stage at
+        the start like the prefill's tokens in pipeline_generate)."""
+        st = self.stage
+        p, r, dev, tr = st.size, st.rank, st.device, st.transport
+        rows = list(self.running)
+        sizes = microbatch_sizes(len(rows), min(self.microbatches, len(rows)))
+        m = len(sizes)
+        starts = [sum(sizes[:j]) for j in range(m)]
+        cached = [req.cached for req in rows]
+        toks = torch.empty(w + 1, len(rows), dtype=torch.int64, device=dev)   # toks[t]: step t's input tokens
+        toks[0].copy_(torch.tensor([req.output[-1] for req in rows]))
+        ring = ring_group()
+        plan, plan_t = None, -1
+        tok_in, act_in, act_out, sends = {}, {}, {}, []
+        for op, k in ring_program(r, p, m, w * m):
+            j, t = k % m, k // m
+            grp = slice(starts[j], starts[j] + sizes[j])
+            if op == "tok_send":
+                buf = toks[t, grp]
+                sends.append((dist.isend(buf, dst=0, group=ring), buf))
+            elif op == "tok_recv":
+                buf = torch.empty(sizes[j], dtype=torch.int64, device=dev)
+                tok_in[k] = (dist.irecv(buf, src=p - 1, group=ring), buf)
+            elif op == "act_recv":
+                buf = torch.empty(sizes[j], 1, self.cfg.d_model, dtype=st.dtype, device=dev)
+                act_in[k] = (tr.irecv(buf, r - 1), buf)
+            elif op == "act_send":
+                sends.append((tr.isend(act_out.pop(k), r + 1), None))
+            else:
+                if t != plan_t:
+                    plan, plan_t = self._window_step(rows, cached, t, last=t == w - 1), t
+                tables, positions = plan
+                views = self.pool.views(tables[grp], positions[grp])
+                pos = views[0].positions if views else positions[grp].to(dev)
+                if st.is_first:
+                    work, tb = tok_in.pop(k)
+                    work.wait()
+                    x = st.embed(tb.view(-1, 1))
+                else:
+                    work, x = act_in.pop(k)
+                    work.wait()
+                st.run_layers_(x, pos, views)
+                if st.is_last:
+                    toks[t + 1, grp].copy_(self._argmax(st.head(x[:, -1:])[:, -1]))
+                else:
+                    act_out[k] = x
+        for work, _ in sends:
+            work.wait()
+        tr.broadcast(toks, src=p - 1)
+        self._window_end(rows, toks[1:].cpu().tolist())
+        self.windows += 1
