@@ -469,6 +469,22 @@ def profile_case(name: str, reps: int, timed: bool = False):
         out = torch.empty(M, V, device=dev, dtype=torch.bfloat16)
         fn = lambda: ops.linear(a, w, out=out)
         work = (2.0 * M * V * d, "FLOP")
+    elif name.startswith("gemm_decode_"):   # a C4 decode step's projections (gemm_decode_<proj>[@rows], 64 rows)
+        proj, _, r = name[len("gemm_decode_"):].partition("@")
+        rows = int(r) if r else 64
+        n_k = {"qkv": ((nh + 2 * nkv) * hd, d), "o": (d, nh * hd), "gateup": (2 * F, d), "down": (d, F)}
+        if proj not in n_k:
+            raise SystemExit(f"unknown profile case {name}")
+        n, k = n_k[proj]
+        a, w = rnd(rows, k), rnd(n, k, scale=0.02)
+        if proj in ("o", "down"):
+            x = rnd(rows, n)
+            fn = lambda: ops.linear(a, w, L.FS_EPI_RESIDUAL, residual=x, out=x)
+        elif proj == "gateup":
+            fn = lambda: ops.linear(a, w, L.FS_EPI_SWIGLU)
+        else:
+            fn = lambda: ops.linear(a, w)
+        work = (2.0 * n * k + 2.0 * rows * (k + n), "B")    # the weights once, the rows in and out
     elif name == "attention":          # one micro-batch's causal prefill attention: 4 x 2048 queries, 32/8 heads
         kc, vc = rnd(MB_ROWS, nkv, SEQ, hd), rnd(MB_ROWS, nkv, SEQ, hd)
         q = rnd(M, (nh + 2 * nkv) * hd)
@@ -555,12 +571,14 @@ def main():
     ap.add_argument("--microbatches", type=int, default=0, help="c4 with N > 1: micro-batches per engine step")
     ap.add_argument("--no-graphs", action="store_true", help="c4: launch every decode kernel from Python")
     ap.add_argument("--no-windows", action="store_true", help="c4 with N > 1: drain the pipeline after every step")
-    ap.add_argument("--profile-case", default=None, help="run a few launches of one kernel (for ncu) and exit")
+    ap.add_argument("--profile-case", default=None,
+                    help="run a few launches of one kernel (for ncu) and exit; a comma-separated list runs several")
     ap.add_argument("--reps", type=int, default=3)
     ap.add_argument("--timed", action="store_true", help="with --profile-case: also time cold-L2 launches")
     args = ap.parse_args()
     if args.profile_case:
-        profile_case(args.profile_case, args.reps, args.timed)
+        for name in args.profile_case.split(","):
+            profile_case(name, args.reps, args.timed)
         return
     if args.warmup < 3 and args.impl == "ours":
         print("warning: fewer than 3 warm-up steps", file=sys.stderr)

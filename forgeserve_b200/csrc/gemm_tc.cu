@@ -254,6 +254,57 @@ __global__ void __launch_bounds__(256)
   }
 }
 
+// The same sums and epilogue, four consecutive outputs of one row per thread: grid (column groups, rows), float4
+// loads of the partials, each output summed over the chunks in the same order as above (the same bits). Needs
+// n_out % 4 == 0 and 8-byte aligned rows of C (and R); the workspace rows are 16-byte aligned (ldw % 4 == 0). C may
+// be R (an in-place residual): every thread reads its own four residuals before it stores them.
+template <int EPI>
+__global__ void __launch_bounds__(256)
+    splitk_reduce_vec_kernel(const float* __restrict__ ws, int64_t ldw, int k_split, int M, int n_out,
+                             __nv_bfloat16* C, int64_t ldc, const __nv_bfloat16* R, int64_t ldr) {
+  const int row = blockIdx.y;
+  const int j = (blockIdx.x * 256 + threadIdx.x) * 4;
+  if (j >= n_out) return;
+  const int64_t plane = static_cast<int64_t>(M) * ldw;
+  const float* w = ws + static_cast<int64_t>(row) * ldw + j;
+  float a[4] = {0.f, 0.f, 0.f, 0.f}, b[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll 4
+  for (int k = 0; k < k_split; ++k) {
+    const float4 x = *reinterpret_cast<const float4*>(w + k * plane);
+    a[0] += x.x;
+    a[1] += x.y;
+    a[2] += x.z;
+    a[3] += x.w;
+    if constexpr (EPI == EPI_SWIGLU) {
+      const float4 y = *reinterpret_cast<const float4*>(w + k * plane + n_out);
+      b[0] += y.x;
+      b[1] += y.y;
+      b[2] += y.z;
+      b[3] += y.w;
+    }
+  }
+  float v[4];
+  if constexpr (EPI == EPI_RESIDUAL) {
+    const uint2 rr = *reinterpret_cast<const uint2*>(R + static_cast<int64_t>(row) * ldr + j);
+    v[0] = rnd<__nv_bfloat16>(a[0]) + bf16_lo(rr.x);
+    v[1] = rnd<__nv_bfloat16>(a[1]) + bf16_hi(rr.x);
+    v[2] = rnd<__nv_bfloat16>(a[2]) + bf16_lo(rr.y);
+    v[3] = rnd<__nv_bfloat16>(a[3]) + bf16_hi(rr.y);
+  } else {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      if constexpr (EPI == EPI_SWIGLU)
+        v[i] = rnd<__nv_bfloat16>(silu_f(rnd<__nv_bfloat16>(a[i]))) * rnd<__nv_bfloat16>(b[i]);
+      else
+        v[i] = rnd<__nv_bfloat16>(a[i]);
+    }
+  }
+  uint2 out;
+  out.x = pack_bf16(v[0], v[1]);
+  out.y = pack_bf16(v[2], v[3]);
+  *reinterpret_cast<uint2*>(C + static_cast<int64_t>(row) * ldc + j) = out;
+}
+
 template <int EPI>
 __global__ void __launch_bounds__(THREADS, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, Params p) {
@@ -912,6 +963,14 @@ static float* splitk_workspace(cudaStream_t st, int64_t bytes) {
 
 template <int EPI>
 static int launch_reduce_t(const Params& p, int64_t M, int64_t n_out, cudaStream_t st) {
+  const bool vec = n_out % 4 == 0 && p.ldc % 4 == 0 && (reinterpret_cast<uintptr_t>(p.C) & 7) == 0 &&
+                   (EPI != EPI_RESIDUAL || (p.ldr % 4 == 0 && (reinterpret_cast<uintptr_t>(p.R) & 7) == 0));
+  if (vec && M <= 65535) {
+    const dim3 grid(static_cast<unsigned>((n_out / 4 + 255) / 256), static_cast<unsigned>(M));
+    splitk_reduce_vec_kernel<EPI><<<grid, 256, 0, st>>>(p.ws, p.ldw, p.k_split, static_cast<int>(M),
+                                                       static_cast<int>(n_out), p.C, p.ldc, p.R, p.ldr);
+    return check_launch("splitk_reduce_vec_kernel");
+  }
   const int64_t total = M * n_out;
   int64_t blocks = (total + 255) / 256;
   if (blocks > 4 * sm_count()) blocks = 4 * sm_count();

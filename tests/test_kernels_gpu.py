@@ -89,6 +89,28 @@ def test_gemm_split_k_small_m(epi, M, N, K):
         bf16_close(ops.linear(a, w), (a.double() @ w.double().t()).float())
 
 
+@pytest.mark.parametrize("epi", [L.FS_EPI_STORE, L.FS_EPI_RESIDUAL, L.FS_EPI_SWIGLU])
+def test_split_k_reduce_paths_agree_bitwise(epi):
+    """The split-K sums are reduced four outputs per thread when the output rows allow 8-byte stores, else one
+    output per thread (here forced by a row stride that is not a multiple of 4); both sum the K chunks in the same
+    order with the same rounding points, so they give the same bits."""
+    M, N, K = 64, 2048, 4096
+    a = torch.randn(M, K, device=DEV).bfloat16()
+    w = (torch.randn(N, K, device=DEV) / math.sqrt(K)).bfloat16()
+    n_out = N // 2 if epi == L.FS_EPI_SWIGLU else N
+    wide = torch.zeros(M, n_out + 2, device=DEV).bfloat16()
+    narrow = wide[:, :n_out]
+    if epi == L.FS_EPI_RESIDUAL:
+        x = torch.randn(M, n_out, device=DEV).bfloat16()
+        narrow.copy_(x)
+        ops.linear(a, w, epi, residual=x, out=x)
+        ops.linear(a, w, epi, residual=narrow, out=narrow)
+        assert torch.equal(x, narrow)
+    else:
+        assert torch.equal(ops.linear(a, w, epi), ops.linear(a, w, epi, out=narrow))
+    assert L.device_error(clear=True) == 0
+
+
 def test_gemm_tcgen05_strided_rows():
     """A operand that is a column slice of a wider buffer (row stride > K), as the q part of a qkv buffer."""
     buf = torch.randn(200, 384, device=DEV).bfloat16()
