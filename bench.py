@@ -8,6 +8,10 @@ last stage, exactly as the reference's pipeline_forward computes them.
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
     torchrun --nproc-per-node N bench.py --gpus N ...     (one rank per GPU, NCCL)
 
+Other workloads (not the headline): `--workload c4` (config 4: continuous-batching decode of 64 requests over a
+paged cache; one step is the whole batch) and `--workload c5` (config 5: the 70B shape, a micro-batch sweep of
+generation; one step is one generation per sweep point, so `--steps 1 --warmup 1` at 8 GPUs takes about a minute).
+
 Prints one JSON line on rank 0. `value` is device-timed (CUDA events, max over ranks) with the token ids already
 on the GPU; `e2e` is the same through the public API with the token ids copied from pinned host memory and the
 last-position logits copied back every step. `--impl reference` times the CPU oracle (a restatement of the
@@ -372,6 +376,140 @@ def run_c4(args):
     return result
 
 
+# --------------------------------------------------------------------------------------- config 5 (70B)
+C5_CFG = dict(vocab_size=128256, d_model=8192, n_layers=80, n_heads=64, n_kv_heads=8, ffn_dim=28672,
+              max_seq_len=2048 + 128, rope_theta=500000.0)
+C5 = dict(rows=2, seq=2048, new_tokens=128, sweep=(4, 8, 16, 32))
+C5_WORKLOAD = ("C5: 70B-shape generation (80 layers, d8192, 64/8 heads, ffn 28672, vocab 128256, theta 5e5), "
+               "micro-batches of 2 prompts x 2048 tokens, swept over 4/8/16/32 micro-batches, 128 greedy new tokens "
+               "each, one pipeline stage per GPU")
+
+
+def c5_stage_bytes(cfg, world: int, rank: int, m: int) -> int:
+    """Device bytes a stage needs for one sweep point: its weights, the contiguous K/V of its layers for 2m rows
+    (capacity up to twice the length, as the caches grow), and the largest activations (gate/up of one
+    micro-batch's prefill)."""
+    from forgeserve_b200.pipeline import stage_layers
+    lo, hi = stage_layers(cfg.n_layers, world)[rank]
+    d, f, hd = cfg.d_model, cfg.ffn_dim, cfg.head_dim
+    layer = d * (cfg.n_heads + 2 * cfg.n_kv_heads) * hd + cfg.n_heads * hd * d + 3 * d * f + 2 * d
+    weights = (hi - lo) * layer * 2 + cfg.vocab_size * d * 2 * ((rank == 0) + (rank == world - 1)) \
+        + (d * 2 if rank == world - 1 else 0)                   # embedding, head, final norm
+    kv = (hi - lo) * 2 * C5["rows"] * m * 2 * cfg.max_seq_len * cfg.n_kv_heads * hd * 2
+    act = C5["rows"] * C5["seq"] * (3 * f + 2 * d) * 2
+    return weights + kv + act
+
+
+def run_c5(args):
+    """Config 5: for each micro-batch count m of the sweep, pipeline_generate of 2m prompts (2048 tokens) and 128
+    greedy new tokens through p = N stages (with the overlapped token ring when m >= p, else the reference's
+    step-by-step loop), after a pipeline_forward of the prompts alone (the prefill phase). Reports per m the tokens/s
+    of the whole generation (prompt + new tokens), of the prefill, of the decode (generation minus prefill time), and
+    the measured bubble of the generation beside the analytic (p - 1) / (m + p - 1). A sweep point whose stage would
+    not fit in device memory is reported as skipped."""
+    import torch.distributed as dist
+
+    from forgeserve_b200 import ModelConfig, PipelineStage, PipelineState, _lib, bubble_fraction, pipeline_forward
+    from forgeserve_b200 import pipeline_generate
+    from forgeserve_b200.weights import init_stage_
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=900))
+    cfg = ModelConfig(**C5_CFG)
+    sweep = [int(x) for x in args.c5_sweep.split(",")] if args.c5_sweep else list(C5["sweep"])
+
+    def red(x, op):
+        t = torch.tensor([float(x)], device=dev, dtype=torch.float64)
+        if world > 1:
+            dist.all_reduce(t, op=op)
+        return float(t)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    free0 = torch.cuda.mem_get_info(dev)[0]
+    fits = [red(c5_stage_bytes(cfg, world, rank, m) < 0.92 * free0, dist.ReduceOp.MIN if world > 1 else None) > 0
+            for m in sweep]
+    stage = PipelineStage(cfg, rank, world, device=dev, dtype=torch.bfloat16).eval()
+    init_stage_(stage, seed=1234, std=0.02)
+    stream = torch.cuda.current_stream(dev)
+    launches0 = _lib.launch_count()
+    points, total_tokens, total_ms = [], 0, 0.0
+    sampler = ClockSampler([local] if world == 1 else range(world))
+    with sampler:
+        for m, ok in zip(sweep, fits):
+            B = C5["rows"] * m
+            if not ok:
+                points.append({"microbatches": m, "rows": B, "skipped": "the stage does not fit in device memory"})
+                continue
+            g = torch.Generator().manual_seed(100 + m)
+            prompt = torch.randint(0, cfg.vocab_size, (B, C5["seq"]), generator=g)
+            for _ in range(max(args.warmup, 1)):
+                pipeline_generate(stage, prompt, 2, m)
+            barrier()
+            pre_ms = gen_ms = 0.0
+            busy = 0.0
+            for _ in range(args.steps):
+                state = PipelineState(stage, B, m)
+                e0, e1, e2 = (torch.cuda.Event(enable_timing=True) for _ in range(3))
+                e0.record(stream)
+                pipeline_forward(stage, state, prompt.to(dev) if stage.is_first else None, C5["seq"], last_only=True)
+                e1.record(stream)
+                del state
+                barrier()
+                stage.trace = []
+                e1b = torch.cuda.Event(enable_timing=True)
+                e1b.record(stream)
+                pipeline_generate(stage, prompt, C5["new_tokens"], m)
+                e2.record(stream)
+                torch.cuda.synchronize()
+                busy += sum(a.elapsed_time(b) for _, a, b in stage.trace)
+                stage.trace = None
+                pre_ms += e0.elapsed_time(e1)
+                gen_ms += e1b.elapsed_time(e2)
+                barrier()
+            pre_ms = red(pre_ms, dist.ReduceOp.MAX if world > 1 else None)
+            gen_ms = red(gen_ms, dist.ReduceOp.MAX if world > 1 else None)
+            busy = red(busy, dist.ReduceOp.SUM if world > 1 else None)
+            n_tok = B * (C5["seq"] + C5["new_tokens"]) * args.steps
+            total_tokens += n_tok
+            total_ms += gen_ms
+            points.append({
+                "microbatches": m, "rows": B, "overlapped": m >= world > 1,
+                "tokens_per_s": round(n_tok / (gen_ms / 1e3), 1),
+                "prefill_tokens_per_s": round(B * C5["seq"] * args.steps / (pre_ms / 1e3), 1),
+                "decode_tokens_per_s": round(B * C5["new_tokens"] * args.steps / (max(gen_ms - pre_ms, 1e-6) / 1e3), 1),
+                "ms_per_generation": round(gen_ms / args.steps, 1),
+                "bubble": {"measured": round(1.0 - busy / (world * gen_ms), 4),
+                           "analytic": round(bubble_fraction(world, m), 4)}})
+    launches = red(_lib.launch_count() - launches0, dist.ReduceOp.SUM if world > 1 else None)
+    result = None
+    if rank == 0:
+        result = {
+            "metric": "PP generation tokens/s (prompt + new tokens), 70B-shape bf16 (config 5)",
+            "value": round(total_tokens / (total_ms / 1e3), 1) if total_ms > 0 else None, "unit": "tokens/s",
+            "n_gpus": world, "steps": args.steps, "warmup": max(args.warmup, 1),
+            "ms_per_step": round(total_ms / max(args.steps, 1), 1), "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic: seeded token ids, seeded N(0, 0.02) weights (no checkpoint or dataset)",
+            "config": {"workload": C5_WORKLOAD, "stages": world, "parallelism": f"pp{world}",
+                       "head": "on the last stage (last position only)"},
+            "sweep": points, "gpu_launches": int(launches), "clocks": sampler.summary(),
+        }
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return result
+
+
 def gemm_traffic():
     """DRAM bytes per launch of the profiled gate/up GEMM launch, from the committed ncu summary (or None)."""
     p = ROOT / "profiles" / "gemm_tc_8b_gateup.txt"
@@ -566,8 +704,10 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--whole-head", action="store_true", help="N > 1: keep the whole output head on the last stage")
-    ap.add_argument("--workload", choices=["c3", "c4"], default="c3",
-                    help="c3: pipeline prefill (the headline metric); c4: continuous-batching decode")
+    ap.add_argument("--workload", choices=["c3", "c4", "c5"], default="c3",
+                    help="c3: pipeline prefill (the headline metric); c4: continuous-batching decode; "
+                         "c5: 70B-shape generation, micro-batch sweep")
+    ap.add_argument("--c5-sweep", default="", help="c5: comma-separated micro-batch counts (default 4,8,16,32)")
     ap.add_argument("--microbatches", type=int, default=0, help="c4 with N > 1: micro-batches per engine step")
     ap.add_argument("--no-graphs", action="store_true", help="c4: launch every decode kernel from Python")
     ap.add_argument("--no-windows", action="store_true", help="c4 with N > 1: drain the pipeline after every step")
@@ -582,7 +722,14 @@ def main():
         return
     if args.warmup < 3 and args.impl == "ours":
         print("warning: fewer than 3 warm-up steps", file=sys.stderr)
-    if args.workload == "c4":
+    if args.workload == "c5":
+        if args.impl == "reference":
+            res = None if int(os.environ.get("RANK", "0")) else {
+                "impl": "reference", "metric": "PP generation tokens/s (prompt + new tokens), 70B-shape bf16 (config 5)",
+                "unavailable": "config 5 is not run on the CPU (a 70B fp32 model is about 280 GB)"}
+        else:
+            res = run_c5(args)
+    elif args.workload == "c4":
         if args.impl == "reference":
             res = None if int(os.environ.get("RANK", "0")) else {
                 "impl": "reference", "metric": "continuous-batching decode tokens/s, 8B-shape bf16 (config 4)",

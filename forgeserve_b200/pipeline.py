@@ -515,11 +515,18 @@ def _generate_overlapped(stage: PipelineStage, prompt: torch.Tensor, n: int, mic
             else:
                 work, x = act_in.pop(k)
                 work.wait()
+            if stage.trace is not None:
+                e0 = torch.cuda.Event(enable_timing=True)
+                e0.record(torch.cuda.current_stream(dev))
             stage.run_layers_(x, _positions(T + t, 1, sizes[j], dev), state.caches[j])
             if stage.is_last:
                 toks[rows, T + t + 1].copy_(ops.argmax(stage.head(x)[:, -1]))
             else:
                 act_out[k] = x
+            if stage.trace is not None:
+                e1 = torch.cuda.Event(enable_timing=True)
+                e1.record(torch.cuda.current_stream(dev))
+                stage.trace.append((j, e0, e1))
     for work, _ in sends:
         work.wait()
     tr.broadcast(toks, src=p - 1)

@@ -1,0 +1,38 @@
+"""Host-side parts of bench.py that need no GPU: the config-5 memory plan and the reference arm's lines for the
+workloads that are not run on the CPU."""
+
+import json
+import math
+import subprocess
+import sys
+from pathlib import Path
+
+import pytest
+
+ROOT = Path(__file__).resolve().parent.parent
+sys.path.insert(0, str(ROOT))
+
+import bench  # noqa: E402
+from forgeserve_b200 import ModelConfig  # noqa: E402
+from forgeserve_b200.weights import model_shapes  # noqa: E402
+
+
+@pytest.mark.parametrize("world", [1, 2, 4, 8])
+def test_c5_stage_bytes_cover_the_whole_model(world):
+    cfg = ModelConfig(**bench.C5_CFG)
+    m = 4
+    act = bench.C5["rows"] * bench.C5["seq"] * (3 * cfg.ffn_dim + 2 * cfg.d_model) * 2
+    kv = cfg.n_layers * 2 * bench.C5["rows"] * m * 2 * cfg.max_seq_len * cfg.n_kv_heads * cfg.head_dim * 2
+    weights = sum(2 * math.prod(shape) for shape in model_shapes(cfg).values())
+    total = sum(bench.c5_stage_bytes(cfg, world, r, m) for r in range(world))
+    assert total == weights + kv + world * act
+    assert weights / 1e9 == pytest.approx(141.1, abs=0.2)          # 70.6 B parameters in bf16, untied head
+
+
+@pytest.mark.parametrize("workload", ["c4", "c5"])
+def test_reference_arm_reports_unavailable_workloads(workload):
+    out = subprocess.run([sys.executable, str(ROOT / "bench.py"), "--impl", "reference", "--workload", workload],
+                         capture_output=True, text=True, timeout=120, cwd=ROOT)
+    assert out.returncode == 0, out.stderr
+    line = json.loads(out.stdout.strip().splitlines()[-1])
+    assert line["impl"] == "reference" and "unavailable" in line
