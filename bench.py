@@ -109,6 +109,7 @@ def run_ours(args):
 
     from forgeserve_b200 import ModelConfig, PipelineStage, PipelineState, bubble_fraction, ops, pipeline_forward
     from forgeserve_b200 import _lib
+    from forgeserve_b200.pipeline import seq_pieces
     from forgeserve_b200.weights import init_stage_
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -147,7 +148,7 @@ def run_ours(args):
 
     def step(idx):
         state = PipelineState(stage, batch, MICROBATCHES)
-        return pipeline_forward(stage, state, idx if stage.is_first else None, SEQ)
+        return pipeline_forward(stage, state, idx if stage.is_first else None, SEQ, seq_chunks=args.seq_chunks)
 
     for _ in range(args.warmup):
         step(idx_dev)
@@ -225,9 +226,12 @@ def run_ours(args):
             "config": {"workload": WORKLOAD, "global_batch": batch, "seq_len": SEQ, "microbatches": MICROBATCHES,
                        "stages": world, "parallelism": f"pp{world}",
                        "head": "split over the stages by vocab range" if split_head else "on the last stage",
+                       "seq_pieces": len(seq_pieces(SEQ, args.seq_chunks)),
                        "l2": "no flush needed: every step streams 16 GB of weights (> 126 MB L2)"},
             "bubble": {"measured": round(1.0 - busy_sum / (world * ms_max), 4),
-                       "analytic": round(bubble_fraction(world, MICROBATCHES), 4)},
+                       "analytic": round(bubble_fraction(world, MICROBATCHES * len(seq_pieces(SEQ, args.seq_chunks))),
+                                         4),
+                       "analytic_whole_microbatches": round(bubble_fraction(world, MICROBATCHES), 4)},
             "model_tflops": round(step_flops * args.steps / (ms_max / 1e3) / 1e12, 1),
             "roofline": {"bound": "tensor",
                          "kernel": "gemm_tc2_kernel, the 2-SM tcgen05 GEMM (every projection GEMM of the timed region)",
@@ -704,6 +708,8 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--whole-head", action="store_true", help="N > 1: keep the whole output head on the last stage")
+    ap.add_argument("--seq-chunks", type=int, default=1,
+                    help="c3: pieces per micro-batch along the sequence (pipeline_forward's seq_chunks; same logits)")
     ap.add_argument("--workload", choices=["c3", "c4", "c5"], default="c3",
                     help="c3: pipeline prefill (the headline metric); c4: continuous-batching decode; "
                          "c5: 70B-shape generation, micro-batch sweep")

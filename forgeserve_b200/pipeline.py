@@ -299,13 +299,48 @@ def _positions(start: int, t: int, rows: int, device) -> torch.Tensor:
     return p
 
 
+# Sequence pieces start at multiples of this many tokens: the attention kernels tile queries in blocks of 128 from
+# the first new token, so pieces aligned to it see the same query blocks (and key tiles) as the whole sequence.
+SEQ_PIECE_QUANTUM = 128
+
+
+def seq_pieces(t: int, pieces: int) -> List[Tuple[int, int]]:
+    """[c0, c1) ranges splitting t new tokens into at most `pieces` parts whose starts are multiples of
+    SEQ_PIECE_QUANTUM (the earlier parts as long as the later ones, or longer); one part if t is too short."""
+    q = SEQ_PIECE_QUANTUM
+    n = max(1, min(pieces, t // q))
+    if n == 1:
+        return [(0, t)]
+    step = -(-(-(-t // n)) // q) * q          # ceil(t / n) rounded up to the quantum
+    bounds, c0 = [], 0
+    while c0 < t:
+        bounds.append((c0, min(c0 + step, t)))
+        c0 += step
+    return bounds
+
+
+def _reserve_caches(stage: PipelineStage, caches: List, rows: int, t: int) -> None:
+    """Give a micro-batch's contiguous caches room for all t new tokens before its first piece, so that later
+    pieces never grow (and copy) them."""
+    cfg = stage.cfg
+    for kv in caches:
+        if isinstance(kv, ContiguousKV):
+            kv.reserve(rows, cfg.n_kv_heads, cfg.head_dim, t, stage.dtype, stage.device)
+
+
 @torch.no_grad()
 def pipeline_forward(stage: PipelineStage, state: PipelineState, idx: Optional[torch.Tensor], t: int,
-                     last_only: bool = False):
+                     last_only: bool = False, seq_chunks: int = 1):
     """Push t new tokens per row through the pipeline. `idx` (B, t) is needed on stage 0 only.
 
     Returns the logits (B, t, vocab) on the last stage (on its device) and None elsewhere.
-    last_only=True computes the head for the last position only and returns (B, 1, vocab)."""
+    last_only=True computes the head for the last position only and returns (B, 1, vocab).
+
+    seq_chunks (extra): every stage calls with the same value. Each micro-batch goes through the pipeline in up to
+    this many pieces along the sequence (seq_pieces). A piece needs the keys and values of the earlier pieces of its
+    rows, which the stage's caches hold by the time it arrives, so the schedule carries m * pieces items instead of
+    m and its fill and drain, (p - 1) / (m * pieces + p - 1) of the time, shrink. Every kernel on the path treats
+    rows independently and the pieces keep the attention tiles aligned, so the logits are the same."""
     cfg = stage.cfg
     start = state.length
     if start + t > cfg.max_seq_len:
@@ -317,10 +352,12 @@ def pipeline_forward(stage: PipelineStage, state: PipelineState, idx: Optional[t
     act_dtype = stage.dtype
     recvs = {}
     split = stage.head_split is not None and not last_only
+    pieces = seq_pieces(t, seq_chunks)
+    items = [(mb, c0, c1) for mb in range(len(state.sizes)) for c0, c1 in pieces]
     if not stage.is_first and all(state.sizes) and not split:
-        for mb, size in enumerate(state.sizes):
-            buf = torch.empty(size, t, d, dtype=act_dtype, device=dev)
-            recvs[mb] = (tr.irecv(buf, stage.rank - 1), buf)
+        for k, (mb, c0, c1) in enumerate(items):
+            buf = torch.empty(state.sizes[mb], c1 - c0, d, dtype=act_dtype, device=dev)
+            recvs[k] = (tr.irecv(buf, stage.rank - 1), buf)
     if stage.is_first:
         idx = torch.as_tensor(idx)
         if idx.shape != (batch, t):
@@ -337,30 +374,40 @@ def pipeline_forward(stage: PipelineStage, state: PipelineState, idx: Optional[t
         # forgeserve/model.py:77); refuse up front, on every stage, instead of part-way through.
         raise RuntimeError(f"more micro-batches ({len(state.sizes)}) than batch rows ({batch})")
     if split:
-        _forward_split_head(stage, state, idx, t, start, out)
+        _forward_split_head(stage, state, idx, t, start, out, items)
         if not state.caches[0]:
             state._length = start + t
         return out
-    sends, row = [], 0
-    for mb, size in enumerate(state.sizes):
+    sends = []
+    rows0 = [sum(state.sizes[:j]) for j in range(len(state.sizes))]
+    for k, (mb, c0, c1) in enumerate(items):
+        size, row = state.sizes[mb], rows0[mb]
         if stage.is_first:
-            x = stage.embed(idx[row : row + size])
+            x = stage.embed(idx[row : row + size, c0:c1])
         else:
-            work, x = recvs.pop(mb)
+            work, x = recvs.pop(k)
             work.wait()
         if stage.trace is not None:
             e0 = torch.cuda.Event(enable_timing=True)
             e0.record(stream)
-        stage.run_layers_(x, _positions(start, t, size, dev), state.caches[mb])
+        if len(pieces) > 1 and c0 == 0:
+            _reserve_caches(stage, state.caches[mb], size, t)
+        stage.run_layers_(x, _positions(start + c0, c1 - c0, size, dev), state.caches[mb])
         if stage.is_last:
-            stage.head(x[:, -1:] if last_only else x, out=out[row : row + size])
+            if last_only:
+                if c1 == t:
+                    stage.head(x[:, -1:], out=out[row : row + size])
+            elif len(pieces) == 1:
+                stage.head(x, out=out[row : row + size])
+            else:                                    # a piece's positions of each row are contiguous in `out`
+                for b in range(size):
+                    stage.head(x[b : b + 1], out=out[row + b : row + b + 1, c0:c1])
         else:
             sends.append(tr.isend(x, stage.rank + 1))
         if stage.trace is not None:
             e1 = torch.cuda.Event(enable_timing=True)
             e1.record(stream)
             stage.trace.append((mb, e0, e1))
-        row += size
     for work in sends:
         work.wait()
     if not state.caches[0]:
@@ -369,9 +416,9 @@ def pipeline_forward(stage: PipelineStage, state: PipelineState, idx: Optional[t
 
 
 def _forward_split_head(stage: PipelineStage, state: PipelineState, idx: Optional[torch.Tensor], t: int,
-                        start: int, out: Optional[torch.Tensor]) -> None:
+                        start: int, out: Optional[torch.Tensor], items: List[Tuple[int, int, int]]) -> None:
     """pipeline_forward with the output head split over the stages (PipelineStage.split_head_), in the host order
-    of split_head_program."""
+    of split_head_program over `items` (micro-batch, first and end position of a sequence piece)."""
     import torch.distributed as dist
     cfg, hs, tr = stage.cfg, stage.head_split, stage.transport
     dev, p, r = stage.device, stage.size, stage.rank
@@ -399,54 +446,68 @@ def _forward_split_head(stage: PipelineStage, state: PipelineState, idx: Optiona
         e.record(stream)
         return e
 
-    for kind, j in split_head_program(r, p, len(sizes)):
-        rows = slice(rows0[j], rows0[j] + sizes[j])
+    whole = len(items) == len(sizes)          # one piece per micro-batch: a slice's rows are evenly spaced in out
+    for kind, k in split_head_program(r, p, len(items)):
+        j, c0, c1 = items[k]
+        rows, tc = slice(rows0[j], rows0[j] + sizes[j]), c1 - c0
         if kind == "recv":
             # Posted from the side stream (the transfer does not wait for queued compute); the buffer comes from
             # that stream's pool and is marked as used by the compute stream.
             with torch.cuda.stream(hs.side):
-                buf = torch.empty(sizes[j], t, cfg.d_model, dtype=stage.dtype, device=dev)
-                acts[j] = (tr.irecv(buf, r - 1), buf)
+                buf = torch.empty(sizes[j], tc, cfg.d_model, dtype=stage.dtype, device=dev)
+                acts[k] = (tr.irecv(buf, r - 1), buf)
             buf.record_stream(stream)
         elif kind == "layers":
             if stage.is_first:
-                x = stage.embed(idx[rows])
+                x = stage.embed(idx[rows, c0:c1])
             else:
-                work, x = acts.pop(j)
+                work, x = acts.pop(k)
                 work.wait()
             e0 = mark()
-            stage.run_layers_(x, _positions(start, t, sizes[j], dev), state.caches[j])
+            if not whole and c0 == 0:
+                _reserve_caches(stage, state.caches[j], sizes[j], t)
+            stage.run_layers_(x, _positions(start + c0, tc, sizes[j], dev), state.caches[j])
             if stage.is_last:
-                xn[j] = (None, ops.rmsnorm(x, stage.norm.weight, stage.norm.eps))
+                xn[k] = (None, ops.rmsnorm(x, stage.norm.weight, stage.norm.eps))
             else:
-                acts[j] = (None, x)
+                acts[k] = (None, x)
             if e0 is not None:
                 stage.trace.append((j, e0, mark()))
         elif kind == "send":
-            sends.append(tr.isend(acts.pop(j)[1], r + 1))
+            sends.append(tr.isend(acts.pop(k)[1], r + 1))
         elif kind == "bcast":
             if stage.is_last:
-                h = xn[j][1]
+                h = xn[k][1]
             else:
-                h = torch.empty(sizes[j], t, cfg.d_model, dtype=stage.dtype, device=dev)
-            xn[j] = (dist.broadcast(h, src=p - 1, group=hs.group, async_op=True), h)
+                h = torch.empty(sizes[j], tc, cfg.d_model, dtype=stage.dtype, device=dev)
+            xn[k] = (dist.broadcast(h, src=p - 1, group=hs.group, async_op=True), h)
         else:
-            work, h = xn.pop(j)
+            work, h = xn.pop(k)
             if not stage.is_last:
                 work.wait()
             keep.append(h)
             if hs.hi > hs.lo:
                 e0 = mark()
-                dst = None if stage.is_last else logits_at + (rows0[j] * t * V + hs.lo) * elt
-                if stage.is_last:
+                # this stage's columns of the logits of row b of micro-batch j, positions c0.. (rows of V elements)
+                base = (out.data_ptr() if stage.is_last else logits_at) + hs.lo * elt
+                at = [base + ((rows0[j] + b) * t + c0) * V * elt for b in range(sizes[j])]
+                if whole and stage.is_last:
                     ops.linear(h, hs.weight, out=out[rows, :, hs.lo : hs.hi])
-                elif hs.peer_store:
-                    ops.linear_to(h, hs.weight, dst, V, system_fence=True)
+                elif hs.peer_store and not stage.is_last:
+                    if whole:
+                        ops.linear_to(h, hs.weight, at[0], V, system_fence=True)
+                    else:
+                        for b in range(sizes[j]):
+                            ops.linear_to(h[b], hs.weight, at[b], V, system_fence=True)
                 else:
                     part = ops.linear(h, hs.weight)
                     hs.copy.wait_stream(stream)
                     with torch.cuda.stream(hs.copy):
-                        ops.copy_2d_to(dst, V * elt, part)
+                        if whole:                  # the micro-batch's rows follow one another in out
+                            ops.copy_2d_to(at[0], V * elt, part)
+                        else:
+                            for b in range(sizes[j]):
+                                ops.copy_2d_to(at[b], V * elt, part[b])
                     part.record_stream(hs.copy)
                 if e0 is not None:
                     stage.trace.append((j, e0, mark()))

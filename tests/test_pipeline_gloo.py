@@ -58,6 +58,24 @@ def forward_worker(rank, size, cfg_dict, full_sd, idx, more, microbatches):
     return logits, logits2, layer_params
 
 
+def pieces_worker(rank, size, cfg_dict, full_sd, idx, more, microbatches, pieces, quantum):
+    import forgeserve_b200.pipeline as P
+    from forgeserve_b200 import ModelConfig, PipelineState, pipeline_forward
+    P.SEQ_PIECE_QUANTUM = quantum     # test-only: the golden model's sequences are shorter than 128 tokens
+    cfg = ModelConfig(**cfg_dict)
+    stage = _oracle_stage_class()(cfg, rank, size, device="cpu")
+    stage.load_from_full(full_sd)
+    res = []
+    for c in (1, pieces):
+        state = PipelineState(stage, idx.shape[0], microbatches)
+        first = pipeline_forward(stage, state, idx if rank == 0 else None, idx.shape[1], seq_chunks=c)
+        cont = pipeline_forward(stage, state, more if rank == 0 else None, more.shape[1], seq_chunks=c)
+        state = PipelineState(stage, idx.shape[0], microbatches)
+        last = pipeline_forward(stage, state, idx if rank == 0 else None, idx.shape[1], last_only=True, seq_chunks=c)
+        res.append((first, cont, last, state.length))
+    return res
+
+
 def generate_worker(rank, size, cfg_dict, full_sd, prompt, microbatches, n):
     import forgeserve_b200.pipeline as P
     from forgeserve_b200 import ModelConfig
@@ -111,3 +129,37 @@ def test_more_microbatches_than_rows_is_refused_on_every_rank(golden):
     g, sd = golden
     with pytest.raises(RuntimeError, match="micro-batches"):
         run_distributed(empty_microbatch_worker, 2, g["cfg"], sd, g["idx"][:2], backend="gloo", timeout=60)
+
+
+@pytest.mark.parametrize("size,microbatches,pieces,quantum", [(2, 1, 2, 4), (3, 2, 3, 1), (3, 4, 2, 2)])
+def test_sequence_pieces_give_the_same_logits(golden, size, microbatches, pieces, quantum):
+    """pipeline_forward with each micro-batch split into pieces along the sequence (more items in the schedule,
+    every piece after the earlier ones of its rows on every stage): the logits of every position, of a forward
+    continued through the caches, and of last_only, as with whole micro-batches and as the reference's."""
+    from forgeserve_b200.pipeline import seq_pieces
+    from forgeserve_b200.tensor_parallel import run_distributed
+    g, sd = golden
+    t = g["idx"].shape[1]
+    res = run_distributed(pieces_worker, size, g["cfg"], sd, g["idx"], g["more"], microbatches, pieces, quantum,
+                          backend="gloo")
+    (first, cont, last, n), (first_p, cont_p, last_p, n_p) = res[-1]
+    want, want2 = g["pipeline"][(size, microbatches)]
+    # the fp32 bar: the CPU stand-in's attention sums in another order for another number of queries
+    for got, ref in ((first_p, first), (first_p, want), (cont_p, cont), (cont_p, want2), (last_p, first[:, -1:])):
+        torch.testing.assert_close(got, ref, atol=1e-4, rtol=1e-4)
+    assert last.shape == last_p.shape and n == n_p == t
+    assert all(r[1][0] is None for r in res[:-1])
+
+
+def test_seq_pieces_bounds():
+    import forgeserve_b200.pipeline as P
+    assert P.SEQ_PIECE_QUANTUM == 128
+    assert P.seq_pieces(2048, 4) == [(0, 512), (512, 1024), (1024, 1536), (1536, 2048)]
+    assert P.seq_pieces(2048, 3) == [(0, 768), (768, 1536), (1536, 2048)]
+    assert P.seq_pieces(1000, 4) == [(0, 256), (256, 512), (512, 768), (768, 1000)]
+    assert P.seq_pieces(200, 4) == [(0, 200)] and P.seq_pieces(2048, 1) == [(0, 2048)]
+    for t in range(1, 3000, 37):
+        for n in (1, 2, 3, 5, 8):
+            b = P.seq_pieces(t, n)
+            assert b[0][0] == 0 and b[-1][1] == t and len(b) <= n
+            assert all(c1 == d0 and c0 % 128 == 0 and c1 > c0 for (c0, c1), (d0, _) in zip(b, b[1:] + [(t, t)]))

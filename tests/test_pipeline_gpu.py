@@ -122,6 +122,65 @@ def test_nccl_split_head_matches_whole_head(microbatches, transfer):
     assert err == 0 and res[0][3] == 0
 
 
+def test_sequence_pieces_are_bit_identical_on_one_gpu():
+    """bf16, head_dim 128: micro-batches pushed through in 4 pieces of 256 tokens give exactly the logits of whole
+    micro-batches (every kernel treats rows independently; every GEMM has more than 128 rows either way, so the
+    same 2-SM kernel runs), for all positions, continued through the caches, and with last_only."""
+    from forgeserve_b200 import _lib
+    from forgeserve_b200.weights import init_stage_
+    cfg = ModelConfig(vocab_size=1000, d_model=512, n_layers=2, n_heads=4, n_kv_heads=2, max_seq_len=2048)
+    stage = PipelineStage(cfg, 0, 1, dtype=torch.bfloat16).eval()
+    init_stage_(stage, seed=13, std=0.05)
+    g = torch.Generator().manual_seed(2)
+    idx = torch.randint(0, 1000, (6, 1024), generator=g)
+    more = torch.randint(0, 1000, (6, 1024), generator=g)
+
+    def run(pieces):
+        state = PipelineState(stage, 6, 2)
+        a = pipeline_forward(stage, state, idx, 1024, seq_chunks=pieces)
+        b = pipeline_forward(stage, state, more, 1024, seq_chunks=pieces)
+        c = pipeline_forward(stage, PipelineState(stage, 6, 2), idx, 1024, last_only=True, seq_chunks=pieces)
+        return a, b, c
+
+    whole, pieces = run(1), run(4)
+    for x, y in zip(whole, pieces):
+        assert torch.isfinite(x.float()).all() and torch.equal(x, y)
+    assert _lib.device_error(clear=True) == 0
+
+
+def pieces_split_head_worker(rank, size, cfg_dict, batch, t, microbatches, pieces):
+    from forgeserve_b200 import _lib
+    from forgeserve_b200.weights import init_stage_
+    cfg = ModelConfig(**cfg_dict)
+    stage = PipelineStage(cfg, rank, size, dtype=torch.bfloat16).eval()
+    init_stage_(stage, seed=17, std=0.05)
+    idx = torch.randint(0, cfg.vocab_size, (batch, t), generator=torch.Generator().manual_seed(4))
+
+    def run(n):
+        out = pipeline_forward(stage, PipelineState(stage, batch, microbatches), idx if rank == 0 else None, t,
+                               seq_chunks=n)
+        return None if out is None else out.cpu()
+
+    whole = run(1)
+    stage.split_head_()
+    return whole, run(1), run(pieces), _lib.device_error(clear=True)
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+@pytest.mark.parametrize("microbatches,pieces", [(1, 3), (3, 2)])
+def test_nccl_sequence_pieces_with_split_head(microbatches, pieces):
+    """Two stages over NCCL with the split head: sequence pieces (more items in split_head_program's order, each
+    head slice copied row by row into the last stage's logits) give the logits of whole micro-batches, bit for
+    bit."""
+    cfg = dict(vocab_size=1000, d_model=256, n_layers=4, n_heads=4, n_kv_heads=2, max_seq_len=512)
+    res = run_distributed(pieces_split_head_worker, 2, cfg, 6, 384, microbatches, pieces, backend="nccl",
+                          timeout=300)
+    assert res[0][:3] == (None, None, None)
+    whole, split, split_pieces, err = res[1]
+    assert torch.equal(whole, split) and torch.equal(whole, split_pieces)
+    assert err == 0 and res[0][3] == 0
+
+
 def overlap_worker(rank, size, cfg_dict, prompt, n, microbatches):
     from forgeserve_b200 import _lib
     from forgeserve_b200.weights import init_stage_
