@@ -69,7 +69,7 @@ def run_serialised(progs):
 
 
 @pytest.mark.parametrize("size", [2, 3, 4, 5, 8])
-@pytest.mark.parametrize("m", [1, 2, 3, 7, 16, 32])
+@pytest.mark.parametrize("m", [1, 2, 3, 7, 16, 32, 64])     # 64: 16 micro-batches in 4 sequence pieces
 def test_program_completes_when_every_rank_is_serialised(size, m):
     assert run_serialised([split_head_program(r, size, m) for r in range(size)])
 
