@@ -8,7 +8,8 @@ last stage, exactly as the reference's pipeline_forward computes them.
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
     torchrun --nproc-per-node N bench.py --gpus N ...     (one rank per GPU, NCCL)
 
-Other workloads (not the headline): `--workload c4` (config 4: continuous-batching decode of 64 requests over a
+Other workloads (not the headline): `--workload c2` (config 2: the same prefill on the 1B shape, 8 micro-batches of
+4 x 1024 tokens), `--workload c4` (config 4: continuous-batching decode of 64 requests over a
 paged cache; one step is the whole batch) and `--workload c5` (config 5: the 70B shape, a micro-batch sweep of
 generation; one step is one generation per sweep point, so `--steps 1 --warmup 1` at 8 GPUs takes about a minute).
 
@@ -39,6 +40,17 @@ CFG = dict(vocab_size=128256, d_model=4096, n_layers=32, n_heads=32, n_kv_heads=
 MICROBATCHES, MB_ROWS, SEQ = 16, 4, 2048
 WORKLOAD = ("C3: 8B-shape prefill (32 layers, d4096, 32/8 heads, ffn 14336, vocab 128256, theta 5e5), "
             "16 micro-batches x (4 x 2048 tokens), one pipeline stage per GPU")
+
+# Pipeline-prefill workloads: config 3 (the headline) and config 2 (the 1B shape; its RoPE theta is not given,
+# so it keeps the reference's default).
+PREFILL = {
+    "c3": dict(cfg=CFG, microbatches=MICROBATCHES, rows=MB_ROWS, seq=SEQ, metric=METRIC, workload=WORKLOAD),
+    "c2": dict(cfg=dict(vocab_size=128256, d_model=2048, n_layers=16, n_heads=32, n_kv_heads=8, ffn_dim=8192,
+                        max_seq_len=1024),
+               microbatches=8, rows=4, seq=1024, metric="PP prefill tokens/s, 1B-shape bf16 (config 2)",
+               workload=("C2: 1B-shape prefill (16 layers, d2048, 32/8 heads, head_dim 64, ffn 8192, vocab 128256), "
+                         "8 micro-batches x (4 x 1024 tokens), one pipeline stage per GPU")),
+}
 
 
 def peaks():
@@ -104,7 +116,7 @@ class ClockSampler:
 
 
 # --------------------------------------------------------------------------------------------------- ours
-def run_ours(args):
+def run_ours(args, spec):
     import torch.distributed as dist
 
     from forgeserve_b200 import ModelConfig, PipelineStage, PipelineState, bubble_fraction, ops, pipeline_forward
@@ -134,21 +146,24 @@ def run_ours(args):
             dist.all_reduce(t, op=op)
         return float(t)
 
-    cfg = ModelConfig(**CFG)
+    cfg = ModelConfig(**spec["cfg"])
+    microbatches, mb_rows, seq = spec["microbatches"], spec["rows"], spec["seq"]
     stage = PipelineStage(cfg, rank, world, device=dev, dtype=torch.bfloat16).eval()
     init_stage_(stage, seed=1234, std=0.02)
+    weight_gb = allreduce(sum(p.numel() * p.element_size() for p in stage.parameters()),
+                          dist.ReduceOp.SUM if world > 1 else None) / 1e9
     split_head = world > 1 and not args.whole_head
     if split_head:
         stage.split_head_()   # every stage computes a vocab slice of the head (logits still land on the last stage)
-    batch = MICROBATCHES * MB_ROWS
+    batch = microbatches * mb_rows
     g = torch.Generator(device="cpu").manual_seed(7)
-    idx_host = torch.randint(0, cfg.vocab_size, (batch, SEQ), generator=g).pin_memory()
+    idx_host = torch.randint(0, cfg.vocab_size, (batch, seq), generator=g).pin_memory()
     idx_dev = idx_host.to(dev)
-    tokens_per_step = batch * SEQ
+    tokens_per_step = batch * seq
 
     def step(idx):
-        state = PipelineState(stage, batch, MICROBATCHES)
-        return pipeline_forward(stage, state, idx if stage.is_first else None, SEQ, seq_chunks=args.seq_chunks)
+        state = PipelineState(stage, batch, microbatches)
+        return pipeline_forward(stage, state, idx if stage.is_first else None, seq, seq_chunks=args.seq_chunks)
 
     for _ in range(args.warmup):
         step(idx_dev)
@@ -214,30 +229,33 @@ def run_ours(args):
         peak, peak_src = peaks()
         achieved = gemm_flops / (gemm_ms / 1e3) / 1e12 if gemm_ms > 0 else None
         flops_per_token = 2 * (cfg.d_model * (cfg.n_heads + 2 * cfg.n_kv_heads) * cfg.head_dim +
-                               cfg.n_heads * cfg.head_dim * cfg.d_model + 3 * cfg.d_model * cfg.ffn_dim) * cfg.n_layers \
+                               cfg.n_heads * cfg.head_dim * cfg.d_model + 3 * cfg.d_model * cfg.ffn_dim) \
+            * cfg.n_layers \
             + 2 * cfg.d_model * cfg.vocab_size
-        attn_flops = 2 * MB_ROWS * cfg.n_heads * SEQ * SEQ * cfg.head_dim * cfg.n_layers * MICROBATCHES  # causal
+        attn_flops = 2 * mb_rows * cfg.n_heads * seq * seq * cfg.head_dim * cfg.n_layers * microbatches  # causal
         step_flops = flops_per_token * tokens_per_step + attn_flops
         result = {
-            "metric": METRIC, "value": round(value, 1), "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+            "metric": spec["metric"], "value": round(value, 1), "unit": "tokens/s", "n_gpus": world,
+            "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(ms_max / args.steps, 3), "higher_is_better": True,
             "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic: uniform token ids, seeded N(0, 0.02) weights (no checkpoint or dataset)",
-            "config": {"workload": WORKLOAD, "global_batch": batch, "seq_len": SEQ, "microbatches": MICROBATCHES,
+            "config": {"workload": spec["workload"], "global_batch": batch, "seq_len": seq,
+                       "microbatches": microbatches,
                        "stages": world, "parallelism": f"pp{world}",
                        "head": "split over the stages by vocab range" if split_head else "on the last stage",
-                       "seq_pieces": len(seq_pieces(SEQ, args.seq_chunks)),
-                       "l2": "no flush needed: every step streams 16 GB of weights (> 126 MB L2)"},
+                       "seq_pieces": len(seq_pieces(seq, args.seq_chunks)),
+                       "l2": f"no flush needed: every step streams {weight_gb:.1f} GB of weights (> 126 MB L2)"},
             "bubble": {"measured": round(1.0 - busy_sum / (world * ms_max), 4),
-                       "analytic": round(bubble_fraction(world, MICROBATCHES * len(seq_pieces(SEQ, args.seq_chunks))),
+                       "analytic": round(bubble_fraction(world, microbatches * len(seq_pieces(seq, args.seq_chunks))),
                                          4),
-                       "analytic_whole_microbatches": round(bubble_fraction(world, MICROBATCHES), 4)},
+                       "analytic_whole_microbatches": round(bubble_fraction(world, microbatches), 4)},
             "model_tflops": round(step_flops * args.steps / (ms_max / 1e3) / 1e12, 1),
             "roofline": {"bound": "tensor",
                          "kernel": "gemm_tc2_kernel, the 2-SM tcgen05 GEMM (every projection GEMM of the timed region)",
                          "achieved": round(achieved, 1) if achieved else None, "peak": peak, "unit": "TFLOP/s",
                          "frac": round(achieved / peak, 4) if achieved else None, "peak_source": peak_src,
-                         "launches": int(gemm_n), "traffic": gemm_traffic()},
+                         "launches": int(gemm_n), "traffic": gemm_traffic() if spec["cfg"] is CFG else None},
             "e2e": {"value": round(tokens_per_step * args.steps / (e2e_ms / 1e3), 1), "unit": "tokens/s",
                     "h2d_bytes_per_step": idx_host.numel() * idx_host.element_size(),
                     "d2h_bytes_per_step": batch * cfg.vocab_size * 2},
@@ -529,12 +547,14 @@ def gemm_traffic():
 
 
 # ------------------------------------------------------------------------------------------- CPU baseline
-def cpu_sample(steps: int, warmup: int):
+def cpu_sample(steps: int, warmup: int, spec=None):
     """The oracle (CPU restatement of the reference path, fp32, all host threads) on a bounded sample of the
-    workload: one decoder layer and the head on one 2048-token row; tokens/s for the whole 32-layer model is
-    2048 / (32 * t_layer + t_head)."""
+    workload: one decoder layer and the head on one row of the workload's sequence length; tokens/s for the whole
+    model is seq / (n_layers * t_layer + t_head)."""
     from oracle import forge_oracle as O
-    cfg = O.Cfg(**CFG)
+    spec = spec or PREFILL["c3"]
+    seq = spec["seq"]
+    cfg = O.Cfg(**spec["cfg"])
     threads = torch.get_num_threads()
     g = torch.Generator().manual_seed(0)
     names = O.param_order(cfg)
@@ -544,8 +564,8 @@ def cpu_sample(steps: int, warmup: int):
             sd[name] = torch.randn(shape, generator=g) * 0.02 if len(shape) > 1 else torch.ones(shape)
     sd["lm_head.weight"] = torch.randn(cfg.vocab_size, cfg.d_model, generator=g) * 0.02
     cos, sin = O.rope_tables(cfg.head_dim, cfg.max_seq_len, cfg.rope_theta)
-    x = torch.randn(1, SEQ, cfg.d_model, generator=g)
-    pos = torch.arange(SEQ)[None]
+    x = torch.randn(1, seq, cfg.d_model, generator=g)
+    pos = torch.arange(seq)[None]
     times = []
     for i in range(warmup + steps):
         t0 = time.perf_counter()
@@ -558,25 +578,27 @@ def cpu_sample(steps: int, warmup: int):
     t_layer = statistics.median(t for t, _ in times)
     t_head = statistics.median(h for _, h in times)
     per_row = cfg.n_layers * t_layer + t_head
-    return {"value": round(SEQ / per_row, 2), "unit": "tokens/s", "cores": threads, "kind": "port",
-            "sample": f"oracle fp32: 1 of 32 layers + final norm/head on 1 x {SEQ} tokens per step, "
-                      f"extrapolated to the 32-layer model (t_layer {t_layer:.3f} s, t_head {t_head:.3f} s)"}
+    return {"value": round(seq / per_row, 2), "unit": "tokens/s", "cores": threads, "kind": "port",
+            "sample": f"oracle fp32: 1 of {cfg.n_layers} layers + final norm/head on 1 x {seq} tokens per step, "
+                      f"extrapolated to the {cfg.n_layers}-layer model "
+                      f"(t_layer {t_layer:.3f} s, t_head {t_head:.3f} s)"}
 
 
-def run_reference(args):
+def run_reference(args, spec):
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return None
     t0 = time.perf_counter()
-    cb = cpu_sample(args.steps, args.warmup)
+    cb = cpu_sample(args.steps, args.warmup, spec)
     wall = time.perf_counter() - t0
-    return {"metric": METRIC, "value": cb["value"], "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": round(SEQ / cb["value"] * 1e3, 3), "higher_is_better": True,
+    seq = spec["seq"]
+    return {"metric": spec["metric"], "value": cb["value"], "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(seq / cb["value"] * 1e3, 3), "higher_is_better": True,
             "scaling": "strong", "vs_baseline": None, "dtype": "f32", "impl": "reference",
             "data": "synthetic: random fp32 weights (std 0.02) and activations",
-            "config": {"workload": WORKLOAD, "global_batch": MICROBATCHES * MB_ROWS, "seq_len": SEQ,
-                       "microbatches": MICROBATCHES, "stages": world, "parallelism": "cpu"},
+            "config": {"workload": spec["workload"], "global_batch": spec["microbatches"] * spec["rows"],
+                       "seq_len": seq, "microbatches": spec["microbatches"], "stages": world, "parallelism": "cpu"},
             "cpu_baseline": cb,
             "e2e": {"value": cb["value"], "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
             "wall_s": round(wall, 1)}
@@ -710,9 +732,9 @@ def main():
     ap.add_argument("--whole-head", action="store_true", help="N > 1: keep the whole output head on the last stage")
     ap.add_argument("--seq-chunks", type=int, default=1,
                     help="c3: pieces per micro-batch along the sequence (pipeline_forward's seq_chunks; same logits)")
-    ap.add_argument("--workload", choices=["c3", "c4", "c5"], default="c3",
-                    help="c3: pipeline prefill (the headline metric); c4: continuous-batching decode; "
-                         "c5: 70B-shape generation, micro-batch sweep")
+    ap.add_argument("--workload", choices=["c3", "c2", "c4", "c5"], default="c3",
+                    help="c3: 8B-shape pipeline prefill (the headline metric); c2: 1B-shape pipeline prefill; "
+                         "c4: continuous-batching decode; c5: 70B-shape generation, micro-batch sweep")
     ap.add_argument("--c5-sweep", default="", help="c5: comma-separated micro-batch counts (default 4,8,16,32)")
     ap.add_argument("--microbatches", type=int, default=0, help="c4 with N > 1: micro-batches per engine step")
     ap.add_argument("--no-graphs", action="store_true", help="c4: launch every decode kernel from Python")
@@ -731,7 +753,8 @@ def main():
     if args.workload == "c5":
         if args.impl == "reference":
             res = None if int(os.environ.get("RANK", "0")) else {
-                "impl": "reference", "metric": "PP generation tokens/s (prompt + new tokens), 70B-shape bf16 (config 5)",
+                "impl": "reference",
+                "metric": "PP generation tokens/s (prompt + new tokens), 70B-shape bf16 (config 5)",
                 "unavailable": "config 5 is not run on the CPU (a 70B fp32 model is about 280 GB)"}
         else:
             res = run_c5(args)
@@ -743,12 +766,12 @@ def main():
         else:
             res = run_c4(args)
     elif args.impl == "reference":
-        res = run_reference(args)
+        res = run_reference(args, PREFILL[args.workload])
     else:
-        res = run_ours(args)
+        res = run_ours(args, PREFILL[args.workload])
         if res is not None and args.gpus == 1 and not args.no_cpu_baseline:
             torch.cuda.empty_cache()
-            res["cpu_baseline"] = cpu_sample(steps=2, warmup=1)
+            res["cpu_baseline"] = cpu_sample(steps=2, warmup=1, spec=PREFILL[args.workload])
     if res is not None:
         print(json.dumps(res), flush=True)
 

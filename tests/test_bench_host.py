@@ -36,3 +36,14 @@ def test_reference_arm_reports_unavailable_workloads(workload):
     assert out.returncode == 0, out.stderr
     line = json.loads(out.stdout.strip().splitlines()[-1])
     assert line["impl"] == "reference" and "unavailable" in line
+
+
+def test_reference_arm_runs_config_2_on_the_host_cores():
+    """The reference arm on the 1B-shape prefill: the oracle on one of its 16 layers and the head."""
+    out = subprocess.run([sys.executable, str(ROOT / "bench.py"), "--impl", "reference", "--workload", "c2",
+                          "--steps", "1", "--warmup", "0"], capture_output=True, text=True, timeout=300, cwd=ROOT)
+    assert out.returncode == 0, out.stderr
+    line = json.loads(out.stdout.strip().splitlines()[-1])
+    assert line["impl"] == "reference" and "1B-shape" in line["metric"] and line["value"] > 0
+    assert line["config"]["seq_len"] == 1024 and line["config"]["microbatches"] == 8
+    assert "1 of 16 layers" in line["cpu_baseline"]["sample"]
