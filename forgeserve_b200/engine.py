@@ -308,7 +308,12 @@ class Engine(Scheduler):
     """Continuous batching of one model on one GPU (forgeserve/engine.py:36-45).
 
     cuda_graphs=True (extra): decode steps whose rows are all greedy replay a captured CUDA graph per row count
-    (_DecodeGraph) instead of launching every kernel from Python; the tokens are the same."""
+    (_DecodeGraph) instead of launching every kernel from Python; the tokens are the same. A tensor-parallel model
+    (its all-reduces run through torch.distributed) always launches eagerly.
+
+    Under tensor parallelism every shard runs the same Engine over its own model shard (model.tp): the pool holds
+    the shard's KV heads, the logits are replicated, so every shard samples the same tokens (engine.py:36-45 with
+    the TP model of model.py:112)."""
 
     MAX_GRAPHS = 4
 
@@ -321,7 +326,7 @@ class Engine(Scheduler):
         self._init_scheduler(max_batch, seed)
 
     def _forward_rows(self, reqs, idx, positions, tables):
-        if (self.cuda_graphs and self.pool.device.type == "cuda" and idx.shape[1] == 1
+        if (self.cuda_graphs and self.pool.device.type == "cuda" and idx.shape[1] == 1 and self.model.tp.size == 1
                 and all(r.temperature == 0 for r in reqs)
                 and tables.shape[1] * self.pool.block_size <= self.cfg.max_seq_len + self.pool.block_size):
             g = self._graphs.pop(idx.shape[0], None)

@@ -90,16 +90,16 @@ def _fused(parts: List[nn.Parameter], cache_attr: str, owner: nn.Module) -> torc
 
 
 class Attention(nn.Module):
-    """q/k/v/o projections of one layer (model.py:48-78); the computation lives in `layer_forward_`."""
+    """q/k/v/o projections of one layer (model.py:48-78); the computation lives in `layer_forward_`. Under tensor
+    parallelism (tp.size > 1) this shard holds n_heads / size query heads and n_kv_heads / size KV heads (whole
+    heads: q/k/v split by output rows, wo by input columns, model.py:47-58)."""
 
     def __init__(self, cfg: ModelConfig, tp: TPContext = SINGLE, device=None, dtype=None):
         super().__init__()
-        if tp.size != 1:
-            raise NotImplementedError("tensor-parallel layers are not part of forgeserve_b200 (pipeline stages "
-                                      "run whole layers)")
+        cfg.check_tensor_parallel(tp.size)
         self.tp = tp
         self.hd = cfg.head_dim
-        self.nh, self.nkv = cfg.n_heads, cfg.n_kv_heads
+        self.nh, self.nkv = cfg.n_heads // tp.size, cfg.n_kv_heads // tp.size
         self.rep = cfg.n_heads // cfg.n_kv_heads
         f = dict(bias=False, device=device, dtype=dtype)
         self.wq = nn.Linear(cfg.d_model, self.nh * self.hd, **f)
@@ -112,17 +112,18 @@ class Attention(nn.Module):
 
 
 class SwiGLU(nn.Module):
-    """gate/up/down projections of one layer (model.py:81-93)."""
+    """gate/up/down projections of one layer (model.py:81-93); under tensor parallelism ffn_dim / size hidden
+    features of them (gate/up split by output rows, down by input columns)."""
 
     def __init__(self, cfg: ModelConfig, tp: TPContext = SINGLE, device=None, dtype=None):
         super().__init__()
-        if tp.size != 1:
-            raise NotImplementedError("tensor-parallel layers are not part of forgeserve_b200")
+        cfg.check_tensor_parallel(tp.size)
         self.tp = tp
+        hidden = cfg.ffn_dim // tp.size
         f = dict(bias=False, device=device, dtype=dtype)
-        self.w_gate = nn.Linear(cfg.d_model, cfg.ffn_dim, **f)
-        self.w_up = nn.Linear(cfg.d_model, cfg.ffn_dim, **f)
-        self.w_down = nn.Linear(cfg.ffn_dim, cfg.d_model, **f)
+        self.w_gate = nn.Linear(cfg.d_model, hidden, **f)
+        self.w_up = nn.Linear(cfg.d_model, hidden, **f)
+        self.w_down = nn.Linear(hidden, cfg.d_model, **f)
 
     def w_gate_up(self) -> torch.Tensor:
         return _fused([self.w_gate.weight, self.w_up.weight], "_wgu", self)
@@ -180,10 +181,18 @@ def layer_forward_(blk: "Block", x: torch.Tensor, positions: torch.Tensor, kv, r
     if bound is not None:
         commit()
     del keep
-    ops.linear(attn, a.wo.weight, L.FS_EPI_RESIDUAL, residual=x, out=x)
+    if a.tp.size == 1:
+        ops.linear(attn, a.wo.weight, L.FS_EPI_RESIDUAL, residual=x, out=x)
+    else:
+        # row-parallel: this shard's partial sum (rounded as nn.Linear rounds), summed over the shards, then added
+        # to the residual stream (x + all_reduce(wo(a)), model.py:77,105)
+        x.add_(a.tp.all_reduce(ops.linear(attn, a.wo.weight)))
     ops.rmsnorm(x, blk.mlp_norm.weight, blk.mlp_norm.eps, out=h)
     g = ops.linear(h, blk.mlp.w_gate_up(), L.FS_EPI_SWIGLU)
-    ops.linear(g, blk.mlp.w_down.weight, L.FS_EPI_RESIDUAL, residual=x, out=x)
+    if blk.mlp.tp.size == 1:
+        ops.linear(g, blk.mlp.w_down.weight, L.FS_EPI_RESIDUAL, residual=x, out=x)
+    else:
+        x.add_(blk.mlp.tp.all_reduce(ops.linear(g, blk.mlp.w_down.weight)))
     return x
 
 
@@ -212,7 +221,11 @@ def check_positions(positions: torch.Tensor, max_seq_len: int) -> None:
 
 class ForgeModel(nn.Module):
     """Embeddings and the output head are tied (model.py:109-159). `device`/`dtype` build it in place
-    (the reference builds on the CPU in fp32; move it with .to(device, dtype) before running)."""
+    (the reference builds on the CPU in fp32; move it with .to(device, dtype) before running).
+
+    tp: this process's shard of a tensor-parallel model (load it with tensor_parallel.shard_state_dict); the
+    embedding, norms and head are replicated, and the two row-parallel projections of each layer end in one
+    all-reduce each (2 * n_layers per forward, TPContext counts them)."""
 
     def __init__(self, cfg: ModelConfig, tp: TPContext = SINGLE, device=None, dtype=None):
         super().__init__()

@@ -9,6 +9,9 @@ error instead of a hang.
 
 `run_in_threads(fn, size, *args)` runs the ranks as threads of this process on the current GPU, exchanging
 activations through a LocalHub (transport.py): a way to run a multi-stage pipeline on a single GPU.
+
+`shard_state_dict(full, cfg, rank, size)` cuts a full model's weights into one tensor-parallel shard
+(forgeserve/tensor_parallel.py:25-39), for `ForgeModel(cfg, TPContext(rank, size))`.
 """
 
 import datetime
@@ -17,13 +20,39 @@ import pickle
 import socket
 import threading
 import traceback
-from typing import Callable, List, Optional
+from typing import Callable, Dict, List, Optional
 
 import torch
 import torch.distributed as dist
 import torch.multiprocessing as mp
 
+from .config import ModelConfig
 from .transport import LocalHub, LocalTransport, set_thread_transport
+
+# Weights split by output feature (rows of an nn.Linear weight: whole heads for q/k/v) and by input feature
+# (columns: the matching slice of the attention output and of the SwiGLU hidden features).
+_BY_ROWS = ("attn.wq.weight", "attn.wk.weight", "attn.wv.weight", "mlp.w_gate.weight", "mlp.w_up.weight")
+_BY_COLUMNS = ("attn.wo.weight", "mlp.w_down.weight")
+
+
+def shard_state_dict(full: Dict[str, torch.Tensor], cfg: ModelConfig, rank: int, size: int) -> Dict[str, torch.Tensor]:
+    """Shard `rank` of `size` of a full state dict: q/k/v/gate/up keep rows [rank * n / size, (rank + 1) * n / size)
+    of their n output features, wo/w_down the same range of their input columns, and the embedding, norms and head
+    are replicated. Every tensor is a contiguous copy. ValueError when a head count or ffn_dim does not divide."""
+    cfg.check_tensor_parallel(size)
+    if not 0 <= rank < size:
+        raise ValueError("rank must be in [0, size)")
+    out = {}
+    for name, w in full.items():
+        if name.endswith(_BY_ROWS):
+            n = w.shape[0] // size
+            out[name] = w[rank * n : (rank + 1) * n].contiguous().clone()
+        elif name.endswith(_BY_COLUMNS):
+            n = w.shape[1] // size
+            out[name] = w[:, rank * n : (rank + 1) * n].contiguous().clone()
+        else:
+            out[name] = w.clone()
+    return out
 
 
 def _free_port() -> int:

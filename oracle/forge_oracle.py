@@ -18,6 +18,10 @@ Restated from the reference (omkarbhad/forgeserve; file:line of that project):
   pipeline_forward    forgeserve/pipeline.py:95-118 (stages simulated in order in one process: every
                       micro-batch visits stage 0 .. p-1, the data each stage would send is what the next receives)
   greedy_generate     forgeserve/sampling.py:24-35 with temperature 0 (argmax, first index on ties)
+  shard               forgeserve/tensor_parallel.py:25-39 (q/k/v/gate/up by output rows, wo/down by input columns)
+  shard_cfg           forgeserve/model.py:54,87 (a shard's head and hidden counts; head_dim unchanged)
+  model_forward_tp    forgeserve/model.py:77,93,104-106 with parallel.py:20-26 (the shards' partial outputs of
+                      attention and of the MLP summed before each residual add; shards simulated in one process)
 
 Arithmetic is plain torch on whatever device the tensors are on (CPU in every CPU test), in the dtype of the
 weights passed in: fp32 for the 1e-4 parity mode; bf16 reproduces the reference's bf16 rounding points.
@@ -163,6 +167,57 @@ def model_forward(sd: Dict[str, torch.Tensor], cfg: Cfg, idx: torch.Tensor, posi
     for i in (layers if layers is not None else range(cfg.n_layers)):
         x = block(sd, i, x, cfg, cos, sin, positions, kv[i])
     return head(sd, x, cfg)
+
+
+_BY_ROWS = ("attn.wq.weight", "attn.wk.weight", "attn.wv.weight", "mlp.w_gate.weight", "mlp.w_up.weight")
+_BY_COLUMNS = ("attn.wo.weight", "mlp.w_down.weight")
+
+
+def shard(sd: Dict[str, torch.Tensor], rank: int, size: int) -> Dict[str, torch.Tensor]:
+    """Tensor-parallel shard `rank` of `size` of a full state dict (embedding, norms and head replicated)."""
+    out = {}
+    for name, w in sd.items():
+        if name.endswith(_BY_ROWS):
+            n = w.shape[0] // size
+            out[name] = w[rank * n : (rank + 1) * n]
+        elif name.endswith(_BY_COLUMNS):
+            n = w.shape[1] // size
+            out[name] = w[:, rank * n : (rank + 1) * n]
+        else:
+            out[name] = w
+    return out
+
+
+def shard_cfg(cfg: Cfg, size: int) -> Cfg:
+    """The head and hidden-feature counts one shard holds (head_dim stays the model's)."""
+    c = Cfg(cfg.vocab_size, cfg.d_model, cfg.n_layers, cfg.n_heads, cfg.n_kv_heads, cfg.ffn_dim, cfg.max_seq_len,
+            cfg.rope_theta, cfg.norm_eps)
+    c.n_heads, c.n_kv_heads, c.ffn_dim = cfg.n_heads // size, cfg.n_kv_heads // size, cfg.ffn_dim // size
+    return c
+
+
+def model_forward_tp(shards: List[Dict[str, torch.Tensor]], cfg: Cfg, idx: torch.Tensor,
+                     kvs: Optional[List[List]] = None) -> torch.Tensor:
+    """The reference's tensor-parallel forward with every shard in this process: shard r attends over its own
+    heads with its own caches (kvs[r]); the partial attention and MLP outputs are summed in rank order (what the
+    all-reduce computes) and added to the replicated residual stream."""
+    size = len(shards)
+    c = shard_cfg(cfg, size)
+    b, t = idx.shape
+    cos, sin = rope_tables(cfg.head_dim, cfg.max_seq_len, cfg.rope_theta)
+    if kvs is None:
+        kvs = [[ContiguousCache() for _ in range(cfg.n_layers)] for _ in range(size)]
+    positions = (kvs[0][0].length + torch.arange(t))[None, :].expand(b, t)
+    x = shards[0]["tok_emb.weight"][idx]
+    for i in range(cfg.n_layers):
+        p = f"layers.{i}."
+        h = rms_norm(x, shards[0][p + "attn_norm.weight"], cfg.norm_eps)
+        parts = [attention(sd, p, h, c, cos, sin, positions, kvs[r][i]) for r, sd in enumerate(shards)]
+        x = x + sum(parts[1:], parts[0])
+        h = rms_norm(x, shards[0][p + "mlp_norm.weight"], cfg.norm_eps)
+        parts = [swiglu(sd, p, h) for sd in shards]
+        x = x + sum(parts[1:], parts[0])
+    return head(shards[0], x, cfg)
 
 
 def stage_layers(n_layers: int, size: int) -> List[Tuple[int, int]]:

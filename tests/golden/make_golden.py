@@ -32,7 +32,8 @@ sys.path.insert(0, str(ROOT))
 from forgeserve import (Engine, ForgeModel, ModelConfig, PagedKVPool, PipelineStage, PipelineState,  # noqa: E402
                         generate, new_contiguous_cache, pipeline_forward, pipeline_generate)
 from forgeserve.model import apply_rope, precompute_rope, RMSNorm  # noqa: E402
-from forgeserve.tensor_parallel import run_distributed  # noqa: E402
+from forgeserve.parallel import TPContext  # noqa: E402
+from forgeserve.tensor_parallel import run_distributed, shard_state_dict  # noqa: E402
 
 from oracle import forge_oracle as O  # noqa: E402
 
@@ -66,6 +67,33 @@ def generate_worker(rank, size, cfg_dict, full_sd, prompt, microbatches, n):
     stage = PipelineStage(cfg, rank, size).eval()
     stage.load_from_full(full_sd)
     return pipeline_generate(stage, prompt, n, microbatches)
+
+
+def tp_worker(rank, size, cfg_dict, full_sd, idx, more, prompt, n_new):
+    """One tensor-parallel shard of the reference model: a forward, a chunk continued through its cache, the number
+    of all-reduces those two took, and a greedy generation."""
+    cfg = ModelConfig(**cfg_dict)
+    tp = TPContext(rank, size)
+    model = ForgeModel(cfg, tp).eval()
+    model.load_state_dict(shard_state_dict(full_sd, cfg, rank, size))
+    kv = new_contiguous_cache(cfg.n_layers)
+    first = model(idx, kv=kv)
+    cont = model(more, kv=kv)
+    # numpy copies travel by value through the launcher's queue (a tensor would be passed as a shared-memory handle,
+    # which the parent cannot open once the worker has exited)
+    gen = generate(model, prompt, n_new)
+    return first.numpy().copy(), cont.numpy().copy(), tp.num_all_reduces, gen.numpy().copy()
+
+
+def tp_engine_worker(rank, size, cfg_dict, full_sd, requests, num_blocks, max_batch):
+    """The reference Engine over one tensor-parallel shard."""
+    cfg = ModelConfig(**cfg_dict)
+    model = ForgeModel(cfg, TPContext(rank, size)).eval()
+    model.load_state_dict(shard_state_dict(full_sd, cfg, rank, size))
+    eng = Engine(model, num_blocks=num_blocks, block_size=4, max_batch=max_batch)
+    ids = [eng.add_request(p, n) for p, n in requests]
+    res = eng.run()
+    return [res[i] for i in ids], eng.steps, eng.preemptions, tuple(eng.pool.k[0].shape)
 
 
 def make_requests(n=6, seed=1):
@@ -164,6 +192,32 @@ def small_fixture():
     return out
 
 
+def tp_fixture():
+    """The reference's tensor parallelism (model.py:47-106, parallel.py, tensor_parallel.py) over gloo on the test
+    suite's model: 2 and 4 shards (n_kv_heads 4), forward + continued chunk + greedy generation, and the Engine
+    over 2 shards with a pool small enough to preempt."""
+    cfg = ModelConfig(**SMALL)
+    sd = {k: v.detach().clone() for k, v in small_model().state_dict().items()}
+    idx = torch.randint(0, 64, (4, 9), generator=torch.Generator().manual_seed(2))
+    more = torch.randint(0, 64, (4, 3), generator=torch.Generator().manual_seed(9))
+    prompt = torch.randint(0, 64, (4, 5), generator=torch.Generator().manual_seed(4))
+    out = {"cfg": SMALL, "weights": ("test_model_weights", 1, 0.25), "checksum": O.checksum(sd), "idx": idx,
+           "more": more, "prompt": prompt, "tp": {}}
+    for size in (2, 4):
+        res = [tuple(torch.from_numpy(a) if not isinstance(a, int) else a for a in r)
+               for r in run_distributed(tp_worker, size, cfg.to_dict(), sd, idx, more, prompt, 10)]
+        first, cont, n_ar, gen = res[0]
+        for r in res[1:]:
+            assert torch.equal(r[0], first) and torch.equal(r[3], gen) and r[2] == n_ar
+        out["tp"][size] = {"logits": first, "logits_more": cont, "all_reduces": n_ar, "generate": gen}
+    reqs = make_requests(5)
+    res = run_distributed(tp_engine_worker, 2, cfg.to_dict(), sd, reqs, 12, 5)
+    assert all(r[:3] == res[0][:3] for r in res)
+    out["tp_engine"] = {"requests": reqs, "outputs": res[0][0], "steps": res[0][1], "preemptions": res[0][2],
+                        "pool_shape": res[0][3], "num_blocks": 12, "max_batch": 5}
+    return out
+
+
 def c1_fixture():
     """tiny fp32 decoder, 2 pipeline stages over gloo, 4 micro-batches of 2 x 16 tokens."""
     cfg = ModelConfig(**C1)
@@ -184,10 +238,13 @@ def c1_fixture():
             "generate": generate(model, prompt, 8), "pipeline_generate": gen[0]}
 
 
+FIXTURES = {"small": small_fixture, "c1": c1_fixture, "tp": tp_fixture}
+
 if __name__ == "__main__":
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", default=REF)
-    ap.parse_args()
-    torch.save(small_fixture(), HERE / "small.pt")
-    torch.save(c1_fixture(), HERE / "c1.pt")
+    ap.add_argument("--only", default="", help="comma-separated fixture names (default: all)")
+    args = ap.parse_args()
+    for name in (args.only.split(",") if args.only else FIXTURES):
+        torch.save(FIXTURES[name](), HERE / f"{name}.pt")
     print("wrote", sorted(p.name for p in HERE.glob("*.pt")))

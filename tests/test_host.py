@@ -141,8 +141,48 @@ def test_kernels_refuse_cpu_tensors():
 def test_out_of_scope_names_refuse():
     with pytest.raises(NotImplementedError):
         fs.speculative_generate(None, None, None, 1)
-    with pytest.raises(NotImplementedError):
-        fs.ForgeModel(small_cfg(), fs.TPContext(0, 2))
+
+
+def test_shard_state_dict_cuts_and_rebuilds_the_model():
+    """forgeserve/tensor_parallel.py:25-39: q/k/v/gate/up by output rows, wo/down by input columns, the rest
+    replicated; the shards put back together are the full weights; sizes that do not divide are refused."""
+    from forgeserve_b200.tensor_parallel import shard_state_dict
+    cfg = small_cfg()
+    full = O.test_model_weights(O.Cfg(**cfg.to_dict()), seed=2)
+    for size in (2, 4):
+        shards = [shard_state_dict(full, cfg, r, size) for r in range(size)]
+        for name, w in full.items():
+            parts = [sh[name] for sh in shards]
+            assert all(p.is_contiguous() for p in parts)
+            if name.endswith(("wq.weight", "wk.weight", "wv.weight", "w_gate.weight", "w_up.weight")):
+                assert torch.equal(torch.cat(parts, 0), w) and parts[0].shape[0] == w.shape[0] // size
+            elif name.endswith(("wo.weight", "w_down.weight")):
+                assert torch.equal(torch.cat(parts, 1), w) and parts[0].shape[1] == w.shape[1] // size
+            else:
+                assert all(torch.equal(p, w) for p in parts)
+            assert all(torch.equal(p, q) for p, q in zip(parts, [O.shard(full, r, size)[name] for r in range(size)]))
+    with pytest.raises(ValueError, match="n_kv_heads"):
+        shard_state_dict(full, cfg, 0, 8)                    # 4 KV heads over 8 shards
+    with pytest.raises(ValueError):
+        fs.ForgeModel(cfg, fs.TPContext(0, 8))
+
+
+def test_tensor_parallel_model_holds_its_shard():
+    """ForgeModel(cfg, TPContext(rank, size)): a shard's heads and hidden features, the reference's keys, and a
+    shard of the state dict loads into it (the replicated embedding stays tied to the head)."""
+    from forgeserve_b200.tensor_parallel import shard_state_dict
+    cfg = small_cfg()
+    full = O.test_model_weights(O.Cfg(**cfg.to_dict()), seed=2)
+    m = fs.ForgeModel(cfg, fs.TPContext(1, 2), device="cpu")
+    a, mlp = m.layers[0].attn, m.layers[0].mlp
+    assert (a.nh, a.nkv, a.hd) == (4, 2, 8)
+    assert a.wq.weight.shape == (32, 64) and a.wk.weight.shape == (16, 64) and a.wo.weight.shape == (64, 32)
+    assert mlp.w_gate.weight.shape == (cfg.ffn_dim // 2, 64) and mlp.w_down.weight.shape == (64, cfg.ffn_dim // 2)
+    m.load_state_dict(shard_state_dict(full, cfg, 1, 2))
+    assert torch.equal(a.wqkv()[:32], full["layers.0.attn.wq.weight"][32:])
+    assert m.lm_head.weight is m.tok_emb.weight
+    pool = fs.PagedKVPool(cfg, 8, 4, tp=m.tp)
+    assert pool.k[0].shape == (8, 2, 4, 8)
 
 
 def _mapped_ranges(path):

@@ -158,3 +158,20 @@ def test_known_answers_from_the_reference_tests():
         O.stage_layers(2, 3)
     assert O.microbatch_sizes(2, 4) == [1, 1, 0, 0]
     assert O.microbatch_sizes(8, 4) == [2, 2, 2, 2]
+
+
+@pytest.mark.parametrize("size", [2, 4])
+def test_tensor_parallel_restatement(size):
+    """The oracle's tensor-parallel forward (shards' partial outputs summed at the two all-reduce points) against
+    the reference's own tensor parallelism over gloo: forward and a chunk continued through the shards' caches."""
+    g = load("tp.pt")
+    cfg = O.Cfg(**g["cfg"])
+    sd = O.test_model_weights(cfg, *g["weights"][1:])
+    assert O.checksum(sd) == g["checksum"]
+    shards = [O.shard(sd, r, size) for r in range(size)]
+    kvs = [[O.ContiguousCache() for _ in range(cfg.n_layers)] for _ in range(size)]
+    close(O.model_forward_tp(shards, cfg, g["idx"], kvs), g["tp"][size]["logits"], tol=5e-5)
+    close(O.model_forward_tp(shards, cfg, g["more"], kvs), g["tp"][size]["logits_more"], tol=5e-5)
+    assert g["tp"][size]["all_reduces"] == 2 * 2 * cfg.n_layers      # two forwards, two per layer
+    # the reference's shards give the single-process model's tokens
+    assert torch.equal(g["tp"][size]["generate"], O.greedy_generate(sd, cfg, g["prompt"], 10))
