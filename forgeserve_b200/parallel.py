@@ -1,8 +1,7 @@
-"""Tensor-parallel context (forgeserve/parallel.py:7-29).
-
-Pipeline stages run every layer whole (`SINGLE`, forgeserve/pipeline.py:50), so only the size-1 context is
-on this build's path. TPContext keeps the reference's constructor, counters and in-place sum so that code
-written against it still runs; sharded layers (size > 1) are not built here and are refused by the model."""
+"""Tensor-parallel context (forgeserve/parallel.py:7-29): which shard this process is, and the in-place sum of
+partial results over the shards (torch.distributed all-reduce on the context's group), with the reference's
+counters. ForgeModel(cfg, TPContext(rank, size)) holds one shard of every layer (model.py); pipeline stages run
+every layer whole (`SINGLE`, forgeserve/pipeline.py:50)."""
 
 import torch
 import torch.distributed as dist
