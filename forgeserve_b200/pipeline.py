@@ -21,8 +21,9 @@ from . import ops
 from .config import ModelConfig
 from .kv import ContiguousKV
 from .model import Block, RMSNorm, RopeTables, layer_forward_
-from .parallel import SINGLE
+from .parallel import SINGLE, TPContext
 from .sampling import sample
+from .tensor_parallel import shard_state_dict
 from .transport import default_transport
 from .weights import open_state_dict
 
@@ -137,17 +138,22 @@ class PipelineStage(nn.Module):
     final norm and an untied copy of the output head on the last (pipeline.py:44-58).
 
     `device` / `dtype` build the stage in place (default: the current CUDA device if there is one, fp32).
-    `transport` defaults to the torch.distributed default group (or the thread's hub in run_in_threads)."""
+    `transport` defaults to the torch.distributed default group (or the thread's hub in run_in_threads).
 
-    def __init__(self, cfg: ModelConfig, rank: int, size: int, device=None, dtype=None, transport=None):
+    tp (extra): tensor parallelism inside the stage (the reference runs stages whole, SINGLE, pipeline.py:50):
+    this process holds shard tp.rank of the stage's layers, and load_from_full cuts the weights to it. Build the
+    stage's tp and transport with transport.make_grid (a stages x shards grid of processes)."""
+
+    def __init__(self, cfg: ModelConfig, rank: int, size: int, device=None, dtype=None, transport=None,
+                 tp: TPContext = SINGLE):
         super().__init__()
-        self.cfg, self.rank, self.size = cfg, rank, size
+        self.cfg, self.rank, self.size, self.tp = cfg, rank, size, tp
         self.lo, self.hi = stage_layers(cfg.n_layers, size)[rank]
         self.is_first, self.is_last = rank == 0, rank == size - 1
         if device is None:
             device = torch.device("cuda", torch.cuda.current_device()) if torch.cuda.is_available() else "cpu"
         f = dict(device=device, dtype=dtype)
-        self.layers = nn.ModuleList(Block(cfg, SINGLE, **f) for _ in range(self.hi - self.lo))
+        self.layers = nn.ModuleList(Block(cfg, tp, **f) for _ in range(self.hi - self.lo))
         if self.is_first:
             self.tok_emb = nn.Embedding(cfg.vocab_size, cfg.d_model, **f)
         if self.is_last:
@@ -179,6 +185,8 @@ class PipelineStage(nn.Module):
             elif (name == "tok_emb.weight" and self.is_first) or (name in ("norm.weight", "lm_head.weight")
                                                                   and self.is_last):
                 own[name] = w
+        if self.tp.size > 1:
+            own = shard_state_dict(own, self.cfg, self.tp.rank, self.tp.size)
         self.load_state_dict(own)
         hs = self.head_split
         if hs is not None and not self.is_last and "lm_head.weight" in full:

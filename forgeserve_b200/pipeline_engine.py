@@ -38,8 +38,8 @@ class PipelineEngine(Scheduler):
     def __init__(self, stage, num_blocks: int, block_size: int = 16, max_batch: int = 8, seed: int = 0,
                  microbatches: int = 1, overlap: Optional[bool] = None):
         self.stage, self.cfg = stage, stage.cfg
-        self.pool = PagedKVPool(self.cfg, num_blocks, block_size, dtype=stage.dtype, device=stage.device,
-                                n_layers=len(stage.layers))
+        self.pool = PagedKVPool(self.cfg, num_blocks, block_size, tp=stage.tp, dtype=stage.dtype,
+                                device=stage.device, n_layers=len(stage.layers))
         self.microbatches = max(1, microbatches)
         self.overlap = overlap
         self.windows = 0          # decode windows taken by run()

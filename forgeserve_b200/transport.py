@@ -95,13 +95,10 @@ class DistTransport:
         if group is None and dist.is_available() and dist.is_initialized() and dist.get_world_size() > 1:
             self.pairs = _pair_groups()
             if dist.get_backend() == "nccl" and torch.cuda.is_available():
-                from . import ops
-                sms = torch.cuda.get_device_properties(torch.cuda.current_device()).multi_processor_count
-                ops.set_persistent_sms(max(sms - COMM_SMS, 1))
                 # A CTA pair needs two free SMs of one GPC, and NCCL kernels resident on scattered SMs delay some
                 # pairs; the GEMMs claim their tiles at run time, so a late pair just takes fewer tiles.
                 # FORGESERVE_PAIR_GEMM=0 keeps stages on single-CTA tiles.
-                ops.set_gemm_pair_mode(PAIR_GEMM)
+                _reserve_sms_for_nccl()
 
     def _group_with(self, peer: int):
         if self.pairs is None:
@@ -137,6 +134,79 @@ class DistTransport:
             t.copy_(host)
         else:
             dist.broadcast(t, src=src, group=self.group)
+
+
+def _reserve_sms_for_nccl() -> None:
+    """Keep SMs out of the persistent GEMM grid for resident NCCL kernels (see COMM_SMS)."""
+    from . import ops
+    sms = torch.cuda.get_device_properties(torch.cuda.current_device()).multi_processor_count
+    ops.set_persistent_sms(max(sms - COMM_SMS, 1))
+    ops.set_gemm_pair_mode(PAIR_GEMM)
+
+
+class GridTransport:
+    """Pipeline transport for `stages` x `shards` processes, tensor parallelism inside every stage: global rank =
+    stage * shards + shard. After its all-reduces every shard of a stage holds the whole activation, so shard r of
+    stage s sends to shard r of stage s + 1, over a process group of those two ranks; broadcasts (sampled tokens)
+    go down the shard's column of stages. Built by `make_grid`, which also gives the stage's TPContext.
+    Peers are stage indices, as PipelineStage uses them."""
+
+    def __init__(self, stage: int, shard: int, stages: int, shards: int, pairs: Dict[int, object], column):
+        self.stage, self.shard, self.stages, self.shards = stage, shard, stages, shards
+        self.pairs, self.column = pairs, column      # pairs[s]: this shard's group of stages s and s + 1
+        self.group = column
+
+    def _rank(self, stage: int) -> int:
+        return stage * self.shards + self.shard
+
+    def _pair(self, peer: int):
+        if abs(peer - self.stage) != 1:
+            raise ValueError("a stage exchanges activations with its neighbours only")
+        return self.pairs[min(peer, self.stage)]
+
+    def isend(self, t: torch.Tensor, dst: int):
+        g = self._pair(dst)
+        if t.is_cuda and dist.get_backend(g) == "gloo":
+            t = t.to("cpu")
+        return _KeepAlive(dist.isend(t, dst=self._rank(dst), group=g), t)
+
+    def irecv(self, buf: torch.Tensor, src: int):
+        g = self._pair(src)
+        if buf.is_cuda and dist.get_backend(g) == "gloo":
+            host = torch.empty(buf.shape, dtype=buf.dtype)
+            return _HostStagedRecv(dist.irecv(host, src=self._rank(src), group=g), host, buf)
+        return dist.irecv(buf, src=self._rank(src), group=g)
+
+    def broadcast(self, t: torch.Tensor, src: int) -> None:
+        if t.is_cuda and dist.get_backend(self.column) == "gloo":
+            host = t.to("cpu")
+            dist.broadcast(host, src=self._rank(src), group=self.column)
+            t.copy_(host)
+        else:
+            dist.broadcast(t, src=self._rank(src), group=self.column)
+
+
+def make_grid(stages: int, shards: int):
+    """Process groups of a stages x shards grid over the whole torch.distributed world, created collectively (every
+    rank calls this, in the same order). Returns this rank's (stage, TPContext of its stage's shards,
+    GridTransport): build the stage as PipelineStage(cfg, stage, stages, tp=tp, transport=transport)."""
+    from .parallel import TPContext
+    world, me = dist.get_world_size(), dist.get_rank()
+    if world != stages * shards:
+        raise ValueError(f"a {stages} x {shards} grid needs {stages * shards} ranks, the world has {world}")
+    stage, shard = divmod(me, shards)
+    tp_groups = [dist.new_group(list(range(s * shards, (s + 1) * shards))) for s in range(stages)]
+    columns = [dist.new_group([s * shards + r for s in range(stages)]) for r in range(shards)]
+    pairs = {}
+    for s in range(stages - 1):
+        for r in range(shards):
+            g = dist.new_group([s * shards + r, (s + 1) * shards + r])
+            if r == shard:
+                pairs[s] = g
+    if dist.get_backend() == "nccl" and torch.cuda.is_available():
+        _reserve_sms_for_nccl()
+    return stage, TPContext(shard, shards, group=tp_groups[stage]), GridTransport(stage, shard, stages, shards, pairs,
+                                                                                  columns[shard])
 
 
 class _KeepAlive:

@@ -163,3 +163,67 @@ def test_seq_pieces_bounds():
             b = P.seq_pieces(t, n)
             assert b[0][0] == 0 and b[-1][1] == t and len(b) <= n
             assert all(c1 == d0 and c0 % 128 == 0 and c1 > c0 for (c0, c1), (d0, _) in zip(b, b[1:] + [(t, t)]))
+
+
+def _oracle_tp_stage_class():
+    """A PipelineStage whose layers are computed by the oracle on this process's tensor-parallel shard: each shard's
+    partial attention and MLP outputs summed over the stage's shards by the all-reduce (test-only compute; the
+    grid, the groups, the weight cutting and the schedule are the product's)."""
+    import torch.distributed as dist
+    base = _oracle_stage_class()
+
+    class OracleTPStage(base):
+        def run_layers_(self, x, positions, caches):
+            cfg = self._ocfg()
+            c = O.shard_cfg(cfg, self.tp.size)
+            cos, sin = O.rope_tables(cfg.head_dim, cfg.max_seq_len, cfg.rope_theta)
+            for layer, kv in zip(self.layers, caches):
+                sd = {f"layers.0.{k}": v.detach() for k, v in layer.state_dict().items()}
+                h = O.rms_norm(x, sd["layers.0.attn_norm.weight"], cfg.norm_eps)
+                part = O.attention(sd, "layers.0.", h, c, cos, sin, positions, kv)
+                dist.all_reduce(part, group=self.tp.group)
+                x.add_(part)
+                part = O.swiglu(sd, "layers.0.", O.rms_norm(x, sd["layers.0.mlp_norm.weight"], cfg.norm_eps))
+                dist.all_reduce(part, group=self.tp.group)
+                x.add_(part)
+            return x
+
+    return OracleTPStage
+
+
+def grid_worker(rank, size, cfg_dict, full_sd, idx, more, microbatches, stages, prompt):
+    import forgeserve_b200.pipeline as P
+    from forgeserve_b200 import ModelConfig, PipelineState, pipeline_forward
+    from forgeserve_b200.transport import make_grid
+    P.sample = lambda logits, temperature=0.0, generator=None: logits.argmax(-1)   # CPU greedy, test-only
+    cfg = ModelConfig(**cfg_dict)
+    stage_idx, tp, transport = make_grid(stages, size // stages)
+    stage = _oracle_tp_stage_class()(cfg, stage_idx, stages, device="cpu", tp=tp, transport=transport)
+    stage.load_from_full(full_sd)
+    state = PipelineState(stage, idx.shape[0], microbatches)
+    first = pipeline_forward(stage, state, idx if stage.is_first else None, idx.shape[1])
+    cont = pipeline_forward(stage, state, more if stage.is_first else None, more.shape[1])
+    gen = P.pipeline_generate(stage, prompt, 10, microbatches)
+    shapes = {k: tuple(v.shape) for k, v in stage.state_dict().items()}
+    return stage_idx, tp.rank, first, cont, gen, shapes
+
+
+@pytest.mark.parametrize("stages,shards,microbatches", [(2, 2, 1), (2, 2, 2), (3, 2, 4)])
+def test_tensor_parallel_stages_over_gloo(golden, stages, shards, microbatches):
+    """A stages x shards grid (transport.make_grid): every shard of the last stage returns the reference pipeline's
+    logits, continued through the shards' caches, and every rank generates the reference's tokens; each shard holds
+    its cut of its stage's layers."""
+    from forgeserve_b200.tensor_parallel import run_distributed
+    g, sd = golden
+    res = run_distributed(grid_worker, stages * shards, g["cfg"], sd, g["idx"], g["more"], microbatches, stages,
+                          g["prompt"], backend="gloo", timeout=300)
+    for rank, (stage_idx, shard, first, cont, gen, shapes) in enumerate(res):
+        assert (stage_idx, shard) == divmod(rank, shards)
+        if stage_idx == stages - 1:
+            torch.testing.assert_close(first, g["logits"], atol=1e-4, rtol=1e-4)
+            torch.testing.assert_close(cont, g["logits_more"], atol=1e-4, rtol=1e-4)
+        else:
+            assert first is None and cont is None
+        assert torch.equal(gen, g["generate"])
+        assert shapes["layers.0.attn.wq.weight"][0] == g["cfg"]["d_model"] // shards
+        assert shapes["layers.0.mlp.w_down.weight"][1] == O.Cfg(**g["cfg"]).ffn_dim // shards
