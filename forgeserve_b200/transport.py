@@ -109,31 +109,38 @@ class DistTransport:
             return self.group
         return self.pairs[lo]
 
-    def _host_staged(self, group) -> bool:
-        return dist.get_backend(group) == "gloo"
-
     def isend(self, t: torch.Tensor, dst: int):
-        g = self._group_with(dst)
-        if t.is_cuda and self._host_staged(g):
-            host = t.to("cpu")
-            work = dist.isend(host, dst=dst, group=g)
-            return _KeepAlive(work, host)
-        return _KeepAlive(dist.isend(t, dst=dst, group=g), t)
+        return _isend(t, dst, self._group_with(dst))
 
     def irecv(self, buf: torch.Tensor, src: int):
-        g = self._group_with(src)
-        if buf.is_cuda and self._host_staged(g):
-            host = torch.empty(buf.shape, dtype=buf.dtype)
-            return _HostStagedRecv(dist.irecv(host, src=src, group=g), host, buf)
-        return dist.irecv(buf, src=src, group=g)
+        return _irecv(buf, src, self._group_with(src))
 
     def broadcast(self, t: torch.Tensor, src: int) -> None:
-        if t.is_cuda and self._host_staged(self.group):
-            host = t.to("cpu")
-            dist.broadcast(host, src=src, group=self.group)
-            t.copy_(host)
-        else:
-            dist.broadcast(t, src=src, group=self.group)
+        _broadcast(t, src, self.group)
+
+
+# Point-to-point and broadcast on one group. gloo moves host tensors only: a CUDA tensor is staged through host
+# memory (the send keeps its host copy alive until it completes; the receive copies into the CUDA buffer on wait).
+def _isend(t: torch.Tensor, dst: int, group):
+    if t.is_cuda and dist.get_backend(group) == "gloo":
+        t = t.to("cpu")
+    return _KeepAlive(dist.isend(t, dst=dst, group=group), t)
+
+
+def _irecv(buf: torch.Tensor, src: int, group):
+    if buf.is_cuda and dist.get_backend(group) == "gloo":
+        host = torch.empty(buf.shape, dtype=buf.dtype)
+        return _HostStagedRecv(dist.irecv(host, src=src, group=group), host, buf)
+    return dist.irecv(buf, src=src, group=group)
+
+
+def _broadcast(t: torch.Tensor, src: int, group) -> None:
+    if t.is_cuda and dist.get_backend(group) == "gloo":
+        host = t.to("cpu")
+        dist.broadcast(host, src=src, group=group)
+        t.copy_(host)
+    else:
+        dist.broadcast(t, src=src, group=group)
 
 
 def _reserve_sms_for_nccl() -> None:
@@ -165,25 +172,13 @@ class GridTransport:
         return self.pairs[min(peer, self.stage)]
 
     def isend(self, t: torch.Tensor, dst: int):
-        g = self._pair(dst)
-        if t.is_cuda and dist.get_backend(g) == "gloo":
-            t = t.to("cpu")
-        return _KeepAlive(dist.isend(t, dst=self._rank(dst), group=g), t)
+        return _isend(t, self._rank(dst), self._pair(dst))
 
     def irecv(self, buf: torch.Tensor, src: int):
-        g = self._pair(src)
-        if buf.is_cuda and dist.get_backend(g) == "gloo":
-            host = torch.empty(buf.shape, dtype=buf.dtype)
-            return _HostStagedRecv(dist.irecv(host, src=self._rank(src), group=g), host, buf)
-        return dist.irecv(buf, src=self._rank(src), group=g)
+        return _irecv(buf, self._rank(src), self._pair(src))
 
     def broadcast(self, t: torch.Tensor, src: int) -> None:
-        if t.is_cuda and dist.get_backend(self.column) == "gloo":
-            host = t.to("cpu")
-            dist.broadcast(host, src=self._rank(src), group=self.column)
-            t.copy_(host)
-        else:
-            dist.broadcast(t, src=self._rank(src), group=self.column)
+        _broadcast(t, self._rank(src), self.column)
 
 
 def make_grid(stages: int, shards: int):
