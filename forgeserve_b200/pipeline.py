@@ -10,6 +10,11 @@ B200 specifics: a stage's layers run as sm_100a kernels on its GPU; activations 
 NVLink (see transport.py) with every receive posted up front, so micro-batch i+1's compute is enqueued while
 micro-batch i is in flight; the last stage writes each micro-batch's logits into one preallocated output
 instead of concatenating at the end; optional CUDA events per micro-batch measure the real bubble.
+
+Extras, all with the same results: the output head split over the stages by vocab range (split_head_);
+micro-batches pushed through in pieces along the sequence (pipeline_forward's seq_chunks), which shrinks the
+pipeline's fill and drain; greedy generation without a drain after every token (a token ring from the last stage
+to the first); and tensor parallelism inside the stages (PipelineStage's tp, transport.make_grid).
 """
 
 from typing import Dict, List, Optional, Tuple
