@@ -208,7 +208,7 @@ def grid_worker(rank, size, cfg_dict, full_sd, idx, more, microbatches, stages, 
     return stage_idx, tp.rank, first, cont, gen, shapes
 
 
-@pytest.mark.parametrize("stages,shards,microbatches", [(2, 2, 1), (2, 2, 2), (3, 2, 4)])
+@pytest.mark.parametrize("stages,shards,microbatches", [(2, 2, 1), (2, 2, 2), (3, 2, 4), (3, 1, 2), (1, 4, 2)])
 def test_tensor_parallel_stages_over_gloo(golden, stages, shards, microbatches):
     """A stages x shards grid (transport.make_grid): every shard of the last stage returns the reference pipeline's
     logits, continued through the shards' caches, and every rank generates the reference's tokens; each shard holds
