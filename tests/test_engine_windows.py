@@ -187,3 +187,37 @@ def test_pipeline_engine_windows_over_gloo(size, microbatches):
         assert windowed[:6] == stepwise[:6]
         assert windowed[6] == stepwise[6]          # this stage's tables and positions, step by step
     assert res[0][0][1] == ref.steps and res[0][0][2] == ref.preemptions
+
+
+try:
+    from hypothesis import given, settings, strategies as st
+except ImportError:                       # hypothesis is optional
+    given = None
+
+if given is not None:
+    @settings(max_examples=150, deadline=None)
+    @given(seed=st.integers(0, 10_000), n=st.integers(1, 10), num_blocks=st.integers(6, 60),
+           block_size=st.sampled_from([1, 2, 4, 8]), max_batch=st.integers(1, 8),
+           max_seq_len=st.sampled_from([16, 24, 40]), eos_every=st.sampled_from([0, 2, 5]),
+           temp_every=st.sampled_from([0, 3]))
+    def test_windows_match_stepping_on_random_workloads(seed, n, num_blocks, block_size, max_batch, max_seq_len,
+                                                        eos_every, temp_every):
+        """Any mix of requests, pools and limits: windowed scheduling gives the outputs, per-step tables and
+        positions, and counters of stepping one by one (or both refuse the same unschedulable pool)."""
+        g = torch.Generator().manual_seed(seed)
+        reqs = []
+        for i in range(n):
+            plen = int(torch.randint(1, max_seq_len - 1, (1,), generator=g))
+            new = int(torch.randint(1, max_seq_len, (1,), generator=g))
+            eos = int(torch.randint(0, V, (1,), generator=g)) if eos_every and i % eos_every == 0 else None
+            temp = 0.8 if temp_every and i % temp_every == 1 else 0.0
+            reqs.append((torch.randint(0, V, (plen,), generator=g).tolist(), new, eos, temp))
+        runs = []
+        for windowed in (False, True):
+            try:
+                out, s = _run(windowed, reqs, num_blocks, block_size, max_batch, max_seq_len)
+                runs.append((out, s.trace, s.steps, s.preemptions, s.peak_running, s.peak_blocks,
+                             s.pool.allocator.num_free))
+            except (ValueError, RuntimeError) as e:
+                runs.append(("error", type(e).__name__, str(e)))
+        assert runs[0] == runs[1]
