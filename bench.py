@@ -475,7 +475,7 @@ def run_c5(args):
             g = torch.Generator().manual_seed(100 + m)
             prompt = torch.randint(0, cfg.vocab_size, (B, C5["seq"]), generator=g)
             for _ in range(max(args.warmup, 1)):
-                pipeline_generate(stage, prompt, 2, m)
+                pipeline_generate(stage, prompt, 2, m, seq_chunks=args.seq_chunks)
             barrier()
             pre_ms = gen_ms = 0.0
             busy = 0.0
@@ -483,14 +483,15 @@ def run_c5(args):
                 state = PipelineState(stage, B, m)
                 e0, e1, e2 = (torch.cuda.Event(enable_timing=True) for _ in range(3))
                 e0.record(stream)
-                pipeline_forward(stage, state, prompt.to(dev) if stage.is_first else None, C5["seq"], last_only=True)
+                pipeline_forward(stage, state, prompt.to(dev) if stage.is_first else None, C5["seq"], last_only=True,
+                                 seq_chunks=args.seq_chunks)
                 e1.record(stream)
                 del state
                 barrier()
                 stage.trace = []
                 e1b = torch.cuda.Event(enable_timing=True)
                 e1b.record(stream)
-                pipeline_generate(stage, prompt, C5["new_tokens"], m)
+                pipeline_generate(stage, prompt, C5["new_tokens"], m, seq_chunks=args.seq_chunks)
                 e2.record(stream)
                 torch.cuda.synchronize()
                 busy += sum(a.elapsed_time(b) for _, a, b in stage.trace)
@@ -523,7 +524,7 @@ def run_c5(args):
             "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic: seeded token ids, seeded N(0, 0.02) weights (no checkpoint or dataset)",
             "config": {"workload": C5_WORKLOAD, "stages": world, "parallelism": f"pp{world}",
-                       "head": "on the last stage (last position only)"},
+                       "head": "on the last stage (last position only)", "prompt_pieces": args.seq_chunks},
             "sweep": points, "gpu_launches": int(launches), "clocks": sampler.summary(),
         }
     if world > 1:
@@ -731,7 +732,8 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--whole-head", action="store_true", help="N > 1: keep the whole output head on the last stage")
     ap.add_argument("--seq-chunks", type=int, default=1,
-                    help="c3: pieces per micro-batch along the sequence (pipeline_forward's seq_chunks; same logits)")
+                    help="c3, c5: pieces per micro-batch along the sequence in the prompt's forward "
+                         "(pipeline_forward's seq_chunks; same results)")
     ap.add_argument("--workload", choices=["c3", "c2", "c4", "c5"], default="c3",
                     help="c3: 8B-shape pipeline prefill (the headline metric); c2: 1B-shape pipeline prefill; "
                          "c4: continuous-batching decode; c5: 70B-shape generation, micro-batch sweep")

@@ -544,7 +544,8 @@ def _overlap_possible(stage: PipelineStage, microbatches: int, temperature: floa
 
 
 @torch.no_grad()
-def _generate_overlapped(stage: PipelineStage, prompt: torch.Tensor, n: int, microbatches: int) -> torch.Tensor:
+def _generate_overlapped(stage: PipelineStage, prompt: torch.Tensor, n: int, microbatches: int,
+                         seq_chunks: int = 1) -> torch.Tensor:
     """Greedy generation without draining the pipeline after every token (ring_program): after the prefill, the
     last stage sends each micro-batch's new tokens straight to the first stage, which starts that micro-batch's
     next step while the other stages still work on the other micro-batches. Same tokens as the step-by-step
@@ -560,7 +561,8 @@ def _generate_overlapped(stage: PipelineStage, prompt: torch.Tensor, n: int, mic
     rows0 = [sum(sizes[:j]) for j in range(m)]
     toks = torch.zeros(b, T + n, dtype=torch.int64, device=dev)
     toks[:, :T].copy_(prompt.to(dev))
-    logits = pipeline_forward(stage, state, toks[:, :T] if stage.is_first else None, T, last_only=True)
+    logits = pipeline_forward(stage, state, toks[:, :T] if stage.is_first else None, T, last_only=True,
+                              seq_chunks=seq_chunks)
     if stage.is_last:
         toks[:, T].copy_(ops.argmax(logits[:, -1]))
     del logits
@@ -609,27 +611,31 @@ def _generate_overlapped(stage: PipelineStage, prompt: torch.Tensor, n: int, mic
 
 @torch.no_grad()
 def pipeline_generate(stage: PipelineStage, prompt: torch.Tensor, max_new_tokens: int, microbatches: int = 1,
-                      temperature: float = 0.0, generator=None, overlap: Optional[bool] = None) -> torch.Tensor:
+                      temperature: float = 0.0, generator=None, overlap: Optional[bool] = None,
+                      seq_chunks: int = 1) -> torch.Tensor:
     """Generate with the pipeline. Every stage calls this with the same `prompt` (B, T) and gets the same result
     (on the prompt's device). The last stage samples; the tokens are broadcast from it (pipeline.py:121-137).
 
     overlap (extra): greedy decoding with at least as many micro-batches as stages, one process per GPU over
     NCCL, can overlap successive steps (_generate_overlapped) instead of draining the pipeline after every token;
-    None picks it whenever it applies. The tokens are the same either way."""
+    None picks it whenever it applies. The tokens are the same either way.
+    seq_chunks (extra): the prompt's forward goes through the pipeline in pieces along the sequence
+    (pipeline_forward's seq_chunks); the tokens are the same."""
     b, t = prompt.shape
     max_new_tokens = min(max_new_tokens, stage.cfg.max_seq_len - t)
     possible = _overlap_possible(stage, microbatches, temperature)
     if overlap and not possible:
         raise ValueError("overlapped decoding needs temperature 0, micro-batches >= stages >= 2, and NCCL ranks")
     if (overlap is None or overlap) and possible and max_new_tokens > 0:
-        return _generate_overlapped(stage, prompt, max_new_tokens, microbatches).to(prompt.device)
+        return _generate_overlapped(stage, prompt, max_new_tokens, microbatches, seq_chunks).to(prompt.device)
     state = PipelineState(stage, b, microbatches)
     dev = stage.device
     toks = torch.empty(b, t + max(max_new_tokens, 0), dtype=torch.int64, device=dev)
     toks[:, :t].copy_(prompt.to(dev))
     idx, new = toks[:, :t], t
     for i in range(max_new_tokens):
-        logits = pipeline_forward(stage, state, idx if stage.is_first else None, new, last_only=True)
+        logits = pipeline_forward(stage, state, idx if stage.is_first else None, new, last_only=True,
+                                  seq_chunks=seq_chunks if i == 0 else 1)
         if stage.is_last:
             nxt = sample(logits[:, -1], temperature, generator).to(torch.int64)
         else:

@@ -62,6 +62,7 @@ def pieces_worker(rank, size, cfg_dict, full_sd, idx, more, microbatches, pieces
     import forgeserve_b200.pipeline as P
     from forgeserve_b200 import ModelConfig, PipelineState, pipeline_forward
     P.SEQ_PIECE_QUANTUM = quantum     # test-only: the golden model's sequences are shorter than 128 tokens
+    P.sample = lambda logits, temperature=0.0, generator=None: logits.argmax(-1)   # CPU greedy, test-only
     cfg = ModelConfig(**cfg_dict)
     stage = _oracle_stage_class()(cfg, rank, size, device="cpu")
     stage.load_from_full(full_sd)
@@ -72,7 +73,8 @@ def pieces_worker(rank, size, cfg_dict, full_sd, idx, more, microbatches, pieces
         cont = pipeline_forward(stage, state, more if rank == 0 else None, more.shape[1], seq_chunks=c)
         state = PipelineState(stage, idx.shape[0], microbatches)
         last = pipeline_forward(stage, state, idx if rank == 0 else None, idx.shape[1], last_only=True, seq_chunks=c)
-        res.append((first, cont, last, state.length))
+        res.append((first, cont, last, state.length, P.pipeline_generate(stage, idx[:, :5], 6, microbatches,
+                                                                         seq_chunks=c)))
     return res
 
 
@@ -142,7 +144,8 @@ def test_sequence_pieces_give_the_same_logits(golden, size, microbatches, pieces
     t = g["idx"].shape[1]
     res = run_distributed(pieces_worker, size, g["cfg"], sd, g["idx"], g["more"], microbatches, pieces, quantum,
                           backend="gloo")
-    (first, cont, last, n), (first_p, cont_p, last_p, n_p) = res[-1]
+    (first, cont, last, n, gen), (first_p, cont_p, last_p, n_p, gen_p) = res[-1]
+    assert all(torch.equal(r[1][4], gen) and torch.equal(r[0][4], gen) for r in res)   # generation, prompt in pieces
     want, want2 = g["pipeline"][(size, microbatches)]
     # the fp32 bar: the CPU stand-in's attention sums in another order for another number of queries
     for got, ref in ((first_p, first), (first_p, want), (cont_p, cont), (cont_p, want2), (last_p, first[:, -1:])):
