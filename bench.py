@@ -306,7 +306,8 @@ def run_c4(args):
         stage = PipelineStage(cfg, rank, world, device=dev, dtype=torch.bfloat16).eval()
         init_stage_(stage, seed=1234, std=0.02)
         engine = PipelineEngine(stage, C4["num_blocks"], C4["block_size"], max_batch=C4["requests"], seed=0,
-                                microbatches=args.microbatches or world, overlap=False if args.no_windows else None)
+                                microbatches=args.microbatches or world, overlap=False if args.no_windows else None,
+                                prefill_chunks=args.seq_chunks)
         weight_bytes = sum(p.numel() * p.element_size() for p in stage.parameters())
     rng = random.Random(11)
     lengths = [rng.randint(C4["prompt_lo"], C4["prompt_hi"]) for _ in range(C4["requests"])]
@@ -383,6 +384,7 @@ def run_c4(args):
             "config": {"workload": C4_WORKLOAD, "stages": world, "parallelism": f"pp{world}",
                        "microbatches": 1 if world == 1 else (args.microbatches or world),
                        "decode_cuda_graphs": world == 1 and not args.no_graphs,
+                       "prefill_pieces": args.seq_chunks if world > 1 else 1,
                        "decode_windows": getattr(engine, "windows", 0)},
             "decode": {"tokens_per_s": round(dec_tokens / (dec_ms / 1e3), 1), "steps": steps_dec,
                        "ms_per_step": round(step_ms, 3)},
@@ -732,8 +734,8 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--whole-head", action="store_true", help="N > 1: keep the whole output head on the last stage")
     ap.add_argument("--seq-chunks", type=int, default=1,
-                    help="c3, c5: pieces per micro-batch along the sequence in the prompt's forward "
-                         "(pipeline_forward's seq_chunks; same results)")
+                    help="c3, c5: pieces per micro-batch along the sequence in the prompt's forward; c4 with N > 1: "
+                         "pieces per prefill (pipeline_forward's seq_chunks, PipelineEngine's prefill_chunks)")
     ap.add_argument("--workload", choices=["c3", "c2", "c4", "c5"], default="c3",
                     help="c3: 8B-shape pipeline prefill (the headline metric); c2: 1B-shape pipeline prefill; "
                          "c4: continuous-batching decode; c5: 70B-shape generation, micro-batch sweep")

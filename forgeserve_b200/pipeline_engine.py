@@ -25,23 +25,28 @@ import torch.distributed as dist
 
 from .engine import Request, Scheduler
 from .paged import PagedKVPool
-from .pipeline import microbatch_sizes, ring_program
+from .pipeline import microbatch_sizes, ring_program, seq_pieces
 from .transport import DistTransport, ring_group
 
 
 class PipelineEngine(Scheduler):
     """overlap (extra): None or True takes decode windows whenever they apply (the tokens, block tables and
-    counters are those of stepping one by one); False steps one by one, draining the pipeline every step."""
+    counters are those of stepping one by one); False steps one by one, draining the pipeline every step.
+
+    prefill_chunks (extra): a prefill step pushes the prompt through the stages in up to this many pieces along the
+    sequence (pipeline.seq_pieces), so the stages work on different pieces at once instead of taking turns; a
+    piece's keys and values of earlier positions are in the pool by the time it reaches a stage. Same tokens."""
 
     MAX_WINDOW = 64     # decode steps per window: bounds what the host enqueues ahead of the GPUs
 
     def __init__(self, stage, num_blocks: int, block_size: int = 16, max_batch: int = 8, seed: int = 0,
-                 microbatches: int = 1, overlap: Optional[bool] = None):
+                 microbatches: int = 1, overlap: Optional[bool] = None, prefill_chunks: int = 1):
         self.stage, self.cfg = stage, stage.cfg
         self.pool = PagedKVPool(self.cfg, num_blocks, block_size, tp=stage.tp, dtype=stage.dtype,
                                 device=stage.device, n_layers=len(stage.layers))
         self.microbatches = max(1, microbatches)
         self.overlap = overlap
+        self.prefill_chunks = max(1, prefill_chunks)
         self.windows = 0          # decode windows taken by run()
         self._init_scheduler(max_batch, seed)
 
@@ -52,31 +57,34 @@ class PipelineEngine(Scheduler):
         R, T = idx.shape
         d = self.cfg.d_model
         sizes = microbatch_sizes(R, min(self.microbatches, R))
+        starts = [sum(sizes[:j]) for j in range(len(sizes))]
+        pieces = seq_pieces(T, self.prefill_chunks) if T > 1 else [(0, T)]
+        items = [(j, c0, c1) for j in range(len(sizes)) for c0, c1 in pieces]
         tr = st.transport
         recvs = []
         if not st.is_first:
-            for size in sizes:
-                buf = torch.empty(size, T, d, dtype=st.dtype, device=dev)
+            for j, c0, c1 in items:
+                buf = torch.empty(sizes[j], c1 - c0, d, dtype=st.dtype, device=dev)
                 recvs.append((tr.irecv(buf, st.rank - 1), buf))
         if st.is_first:
             idx_dev = idx.to(device=dev, dtype=torch.int64, non_blocking=True)
         logits = torch.empty(R, 1, self.cfg.vocab_size, dtype=st.dtype, device=dev) if st.is_last else None
-        sends, row = [], 0
-        for mb, size in enumerate(sizes):
-            rows = slice(row, row + size)
-            views = self.pool.views(tables[rows], positions[rows])
-            pos = views[0].positions if views else positions[rows].to(dev)
+        sends = []
+        for k, (j, c0, c1) in enumerate(items):
+            rows = slice(starts[j], starts[j] + sizes[j])
+            views = self.pool.views(tables[rows], positions[rows, c0:c1])
+            pos = views[0].positions if views else positions[rows, c0:c1].to(dev)
             if st.is_first:
-                x = st.embed(idx_dev[rows])
+                x = st.embed(idx_dev[rows, c0:c1])
             else:
-                work, x = recvs[mb]
+                work, x = recvs[k]
                 work.wait()
             st.run_layers_(x, pos, views)
             if st.is_last:
-                st.head(x[:, -1:], out=logits[rows])
+                if c1 == T:
+                    st.head(x[:, -1:], out=logits[rows])
             else:
                 sends.append(tr.isend(x, st.rank + 1))
-            row += size
         for w in sends:
             w.wait()
         if st.is_last:

@@ -148,8 +148,10 @@ def _fake_stage_class():
     return FakeStage
 
 
-def window_worker(rank, size, cfg_dict, requests, num_blocks, max_batch, microbatches):
+def window_worker(rank, size, cfg_dict, requests, num_blocks, max_batch, microbatches, prefill_chunks=1):
+    import forgeserve_b200.pipeline as P
     from forgeserve_b200.pipeline_engine import PipelineEngine
+    P.SEQ_PIECE_QUANTUM = 4                    # test-only: prompts here are shorter than 128 tokens
 
     class CpuEngine(PipelineEngine):
         def _argmax(self, logits):
@@ -161,7 +163,7 @@ def window_worker(rank, size, cfg_dict, requests, num_blocks, max_batch, microba
         stage = _fake_stage_class()(cfg, rank, size, device="cpu")
         stage.seen = []
         eng = CpuEngine(stage, num_blocks=num_blocks, block_size=4, max_batch=max_batch, microbatches=microbatches,
-                        overlap=overlap)
+                        overlap=overlap, prefill_chunks=prefill_chunks)
         for prompt, new, eos, temp in requests:
             eng.add_request(prompt, new, eos, temp)
         out = eng.run()
@@ -221,3 +223,20 @@ if given is not None:
             except (ValueError, RuntimeError) as e:
                 runs.append(("error", type(e).__name__, str(e)))
         assert runs[0] == runs[1]
+
+
+def test_pipeline_engine_prefill_pieces_over_gloo():
+    """A prefill step pushed through the stages in pieces of the prompt (PipelineEngine's prefill_chunks): the
+    outputs and counters of whole prefills; every stage sees the pieces' positions in order."""
+    from forgeserve_b200.tensor_parallel import run_distributed
+    cfg = ModelConfig(vocab_size=V, d_model=16, n_layers=3, n_heads=2, n_kv_heads=1, max_seq_len=48)
+    reqs = [(p, n, None, 0.0) for p, n, _, _ in _requests(5, 8, 48)]
+    whole = run_distributed(window_worker, 2, cfg.to_dict(), reqs, 30, 6, 2, 1, backend="gloo", timeout=240)
+    pieces = run_distributed(window_worker, 2, cfg.to_dict(), reqs, 30, 6, 2, 3, backend="gloo", timeout=240)
+    for w, p in zip(whole, pieces):
+        for a, b in zip(w, p):
+            assert a[:6] == b[:6]                      # outputs, steps, preemptions, peaks, free blocks
+        seen_w, seen_p = w[0][6], p[0][6]
+        assert len(seen_p) > len(seen_w)               # prefills arrived in several pieces
+        starts = [pos[0][0] for _, pos in seen_p if len(pos[0]) > 1]
+        assert any(s0 > 0 for s0 in starts)            # pieces after the first start past position 0
