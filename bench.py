@@ -234,6 +234,7 @@ def run_ours(args, spec):
             + 2 * cfg.d_model * cfg.vocab_size
         attn_flops = 2 * mb_rows * cfg.n_heads * seq * seq * cfg.head_dim * cfg.n_layers * microbatches  # causal
         step_flops = flops_per_token * tokens_per_step + attn_flops
+        n_pieces = len(seq_pieces(seq, args.seq_chunks, mb_rows))
         result = {
             "metric": spec["metric"], "value": round(value, 1), "unit": "tokens/s", "n_gpus": world,
             "steps": args.steps,
@@ -244,11 +245,10 @@ def run_ours(args, spec):
                        "microbatches": microbatches,
                        "stages": world, "parallelism": f"pp{world}",
                        "head": "split over the stages by vocab range" if split_head else "on the last stage",
-                       "seq_pieces": len(seq_pieces(seq, args.seq_chunks)),
+                       "seq_pieces": n_pieces,
                        "l2": f"no flush needed: every step streams {weight_gb:.1f} GB of weights (> 126 MB L2)"},
             "bubble": {"measured": round(1.0 - busy_sum / (world * ms_max), 4),
-                       "analytic": round(bubble_fraction(world, microbatches * len(seq_pieces(seq, args.seq_chunks))),
-                                         4),
+                       "analytic": round(bubble_fraction(world, microbatches * n_pieces), 4),
                        "analytic_whole_microbatches": round(bubble_fraction(world, microbatches), 4)},
             "model_tflops": round(step_flops * args.steps / (ms_max / 1e3) / 1e12, 1),
             "roofline": {"bound": "tensor",

@@ -315,20 +315,30 @@ def _positions(start: int, t: int, rows: int, device) -> torch.Tensor:
 # Sequence pieces start at multiples of this many tokens: the attention kernels tile queries in blocks of 128 from
 # the first new token, so pieces aligned to it see the same query blocks (and key tiles) as the whole sequence.
 SEQ_PIECE_QUANTUM = 128
+# ... and give the projection GEMMs more than 128 rows (rows x piece length): from 129 rows on they always take the
+# 2-SM kernel with whole-K accumulation, as the whole sequence does (128 rows or fewer take the 1-SM kernel and may
+# split K, which sums in another order).
+PIECE_MIN_ROWS = 129
 
 
-def seq_pieces(t: int, pieces: int) -> List[Tuple[int, int]]:
-    """[c0, c1) ranges splitting t new tokens into at most `pieces` parts whose starts are multiples of
-    SEQ_PIECE_QUANTUM (the earlier parts as long as the later ones, or longer); one part if t is too short."""
+def seq_pieces(t: int, pieces: int, rows: int = 1) -> List[Tuple[int, int]]:
+    """[c0, c1) ranges splitting t new tokens of `rows` rows into at most `pieces` parts whose starts are multiples
+    of SEQ_PIECE_QUANTUM and each of which has at least PIECE_MIN_ROWS rows x tokens (a short last part joins the
+    one before it); one part if t is too short."""
     q = SEQ_PIECE_QUANTUM
-    n = max(1, min(pieces, t // q))
+    min_len = -(-PIECE_MIN_ROWS // max(rows, 1))    # tokens per piece for enough GEMM rows
+    min_len = -(-min_len // q) * q                   # ... as a whole number of quanta
+    n = max(1, min(pieces, t // min_len))
     if n == 1:
         return [(0, t)]
-    step = -(-(-(-t // n)) // q) * q          # ceil(t / n) rounded up to the quantum
+    per = -(-t // n)                                  # ceil(t / n)
+    step = -(-per // q) * q                           # rounded up to the quantum (>= min_len, as n <= t // min_len)
     bounds, c0 = [], 0
     while c0 < t:
         bounds.append((c0, min(c0 + step, t)))
         c0 += step
+    if len(bounds) > 1 and rows * (bounds[-1][1] - bounds[-1][0]) < PIECE_MIN_ROWS:
+        bounds[-2:] = [(bounds[-2][0], t)]
     return bounds
 
 
@@ -365,7 +375,7 @@ def pipeline_forward(stage: PipelineStage, state: PipelineState, idx: Optional[t
     act_dtype = stage.dtype
     recvs = {}
     split = stage.head_split is not None and not last_only
-    pieces = seq_pieces(t, seq_chunks)
+    pieces = seq_pieces(t, seq_chunks, min(state.sizes) if state.sizes else 1)
     items = [(mb, c0, c1) for mb in range(len(state.sizes)) for c0, c1 in pieces]
     if not stage.is_first and all(state.sizes) and not split:
         for k, (mb, c0, c1) in enumerate(items):

@@ -58,7 +58,7 @@ class PipelineEngine(Scheduler):
         d = self.cfg.d_model
         sizes = microbatch_sizes(R, min(self.microbatches, R))
         starts = [sum(sizes[:j]) for j in range(len(sizes))]
-        pieces = seq_pieces(T, self.prefill_chunks) if T > 1 else [(0, T)]
+        pieces = seq_pieces(T, self.prefill_chunks, min(sizes)) if T > 1 else [(0, T)]
         items = [(j, c0, c1) for j in range(len(sizes)) for c0, c1 in pieces]
         tr = st.transport
         recvs = []

@@ -152,6 +152,7 @@ def window_worker(rank, size, cfg_dict, requests, num_blocks, max_batch, microba
     import forgeserve_b200.pipeline as P
     from forgeserve_b200.pipeline_engine import PipelineEngine
     P.SEQ_PIECE_QUANTUM = 4                    # test-only: prompts here are shorter than 128 tokens
+    P.PIECE_MIN_ROWS = 1
 
     class CpuEngine(PipelineEngine):
         def _argmax(self, logits):

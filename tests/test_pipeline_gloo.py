@@ -62,6 +62,7 @@ def pieces_worker(rank, size, cfg_dict, full_sd, idx, more, microbatches, pieces
     import forgeserve_b200.pipeline as P
     from forgeserve_b200 import ModelConfig, PipelineState, pipeline_forward
     P.SEQ_PIECE_QUANTUM = quantum     # test-only: the golden model's sequences are shorter than 128 tokens
+    P.PIECE_MIN_ROWS = 1
     P.sample = lambda logits, temperature=0.0, generator=None: logits.argmax(-1)   # CPU greedy, test-only
     cfg = ModelConfig(**cfg_dict)
     stage = _oracle_stage_class()(cfg, rank, size, device="cpu")
@@ -156,16 +157,21 @@ def test_sequence_pieces_give_the_same_logits(golden, size, microbatches, pieces
 
 def test_seq_pieces_bounds():
     import forgeserve_b200.pipeline as P
-    assert P.SEQ_PIECE_QUANTUM == 128
-    assert P.seq_pieces(2048, 4) == [(0, 512), (512, 1024), (1024, 1536), (1536, 2048)]
-    assert P.seq_pieces(2048, 3) == [(0, 768), (768, 1536), (1536, 2048)]
-    assert P.seq_pieces(1000, 4) == [(0, 256), (256, 512), (512, 768), (768, 1000)]
-    assert P.seq_pieces(200, 4) == [(0, 200)] and P.seq_pieces(2048, 1) == [(0, 2048)]
+    assert P.SEQ_PIECE_QUANTUM == 128 and P.PIECE_MIN_ROWS == 129
+    assert P.seq_pieces(2048, 4, 4) == [(0, 512), (512, 1024), (1024, 1536), (1536, 2048)]     # config 3
+    assert P.seq_pieces(2048, 3, 4) == [(0, 768), (768, 1536), (1536, 2048)]
+    assert P.seq_pieces(1000, 4, 4) == [(0, 256), (256, 512), (512, 768), (768, 1000)]
+    assert P.seq_pieces(200, 4, 4) == [(0, 200)] and P.seq_pieces(2048, 1, 4) == [(0, 2048)]
+    assert P.seq_pieces(512, 4, 1) == [(0, 256), (256, 512)]          # one row: pieces of 256 tokens at least
+    assert P.seq_pieces(520, 2, 1) == [(0, 384), (384, 520)]
+    assert P.seq_pieces(300, 2, 1) == [(0, 300)]
     for t in range(1, 3000, 37):
         for n in (1, 2, 3, 5, 8):
-            b = P.seq_pieces(t, n)
-            assert b[0][0] == 0 and b[-1][1] == t and len(b) <= n
-            assert all(c1 == d0 and c0 % 128 == 0 and c1 > c0 for (c0, c1), (d0, _) in zip(b, b[1:] + [(t, t)]))
+            for rows in (1, 2, 4):
+                b = P.seq_pieces(t, n, rows)
+                assert b[0][0] == 0 and b[-1][1] == t and len(b) <= n
+                assert all(c1 == d0 and c0 % 128 == 0 and c1 > c0 for (c0, c1), (d0, _) in zip(b, b[1:] + [(t, t)]))
+                assert len(b) == 1 or all(rows * (c1 - c0) >= 129 for c0, c1 in b)   # every GEMM > 128 rows
 
 
 def _oracle_tp_stage_class():
