@@ -231,3 +231,32 @@ def test_8b_shape_layer_bf16_against_oracle():
     assert err < 0.05 * want.abs().max().item(), err
     rel = ((got - want).norm() / want.norm()).item()
     assert rel < 1e-2, rel
+
+
+def grid_worker(rank, size, cfg_dict, full_sd, idx, more, stages):
+    from forgeserve_b200 import _lib
+    from forgeserve_b200.transport import make_grid
+    cfg = ModelConfig(**cfg_dict)
+    stage_idx, tp, transport = make_grid(stages, size // stages)
+    stage = PipelineStage(cfg, stage_idx, stages, tp=tp, transport=transport).eval()
+    stage.load_from_full(full_sd)
+    state = PipelineState(stage, idx.shape[0], 2)
+    first = pipeline_forward(stage, state, idx if stage.is_first else None, idx.shape[1])
+    cont = pipeline_forward(stage, state, more if stage.is_first else None, more.shape[1])
+    return (None if first is None else first.cpu()), (None if cont is None else cont.cpu()), \
+        _lib.device_error(clear=True)
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 4, reason="needs 4 GPUs")
+def test_nccl_tensor_parallel_stages_match_reference():
+    """A 2 x 2 grid over NCCL (two stages, each split over two shards; transport.make_grid): the last stage's
+    shards return the reference's logits (fp32, 1e-4), continued through the shards' caches."""
+    g, sd = load_small()
+    res = run_distributed(grid_worker, 4, g["cfg"], sd, g["idx"], g["more"], 2, backend="nccl", timeout=300)
+    for rank, (first, cont, err) in enumerate(res):
+        assert err == 0
+        if rank >= 2:
+            torch.testing.assert_close(first, g["logits"], atol=1e-4, rtol=1e-4)
+            torch.testing.assert_close(cont, g["logits_more"], atol=1e-4, rtol=1e-4)
+        else:
+            assert first is None and cont is None
