@@ -251,6 +251,8 @@ def run_ours(args, spec):
                        "analytic": round(bubble_fraction(world, microbatches * n_pieces), 4),
                        "analytic_whole_microbatches": round(bubble_fraction(world, microbatches), 4)},
             "model_tflops": round(step_flops * args.steps / (ms_max / 1e3) / 1e12, 1),
+            # the whole step against the pipeline's peak: model FLOP/s / (stages x the measured GEMM peak)
+            "model_frac": round(step_flops * args.steps / (ms_max / 1e3) / 1e12 / (world * peak), 4),
             "roofline": {"bound": "tensor",
                          "kernel": "gemm_tc2_kernel, the 2-SM tcgen05 GEMM (every projection GEMM of the timed region)",
                          "achieved": round(achieved, 1) if achieved else None, "peak": peak, "unit": "TFLOP/s",
