@@ -189,35 +189,3 @@ def test_nccl_pipeline_engine_decode_windows_match_stepping(microbatches):
         assert stepwise[2] > 0
     assert res[0][0][0][0] == res[1][0][0][0]
     assert len({t for out in res[0][0][0][0] for t in out}) > 5           # tokens vary
-
-
-def prefill_pieces_worker(rank, size, cfg_dict, sd, requests, num_blocks, max_batch, pieces):
-    from forgeserve_b200 import PipelineEngine, PipelineStage, _lib
-    cfg = ModelConfig(**cfg_dict)
-    res = []
-    for n in (1, pieces):
-        stage = PipelineStage(cfg, rank, size)
-        stage.load_from_full(sd)
-        stage = stage.to(torch.bfloat16).eval()
-        eng = PipelineEngine(stage, num_blocks=num_blocks, block_size=16, max_batch=max_batch, microbatches=2,
-                             prefill_chunks=n)
-        ids = [eng.add_request(p, k) for p, k in requests]
-        out = eng.run()
-        res.append(([out[i] for i in ids], eng.steps, eng.preemptions))
-    return res, _lib.device_error(clear=True)
-
-
-@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-def test_nccl_pipeline_engine_prefill_pieces_match_whole_prefills():
-    """PipelineEngine over NCCL ranks with each prefill's prompt in pieces (every piece's GEMMs above 128 rows, the
-    attention rows independent): the same tokens and counters as whole prefills, in bf16 at head_dim 128."""
-    cfg = ModelConfig(vocab_size=512, d_model=512, n_layers=4, n_heads=4, n_kv_heads=2, max_seq_len=1024)
-    sd = O.test_model_weights(O.Cfg(**cfg.to_dict()), seed=11, scale=0.05)
-    gen = torch.Generator().manual_seed(7)
-    requests = [(torch.randint(0, 512, (n,), generator=gen).tolist(), k) for n, k in ((700, 12), (300, 20), (520, 9))]
-    res = run_distributed(prefill_pieces_worker, 2, cfg.to_dict(), sd, requests, 160, 3, 4, backend="nccl",
-                          timeout=300)
-    for (whole, pieces), err in res:
-        assert err == 0
-        assert pieces == whole
-    assert len({t for out in res[0][0][0][0] for t in out}) > 5

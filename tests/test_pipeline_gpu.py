@@ -148,39 +148,6 @@ def test_sequence_pieces_are_bit_identical_on_one_gpu():
     assert _lib.device_error(clear=True) == 0
 
 
-def pieces_split_head_worker(rank, size, cfg_dict, batch, t, microbatches, pieces):
-    from forgeserve_b200 import _lib
-    from forgeserve_b200.weights import init_stage_
-    cfg = ModelConfig(**cfg_dict)
-    stage = PipelineStage(cfg, rank, size, dtype=torch.bfloat16).eval()
-    init_stage_(stage, seed=17, std=0.05)
-    idx = torch.randint(0, cfg.vocab_size, (batch, t), generator=torch.Generator().manual_seed(4))
-
-    def run(n):
-        out = pipeline_forward(stage, PipelineState(stage, batch, microbatches), idx if rank == 0 else None, t,
-                               seq_chunks=n)
-        return None if out is None else out.cpu()
-
-    whole = run(1)
-    stage.split_head_()
-    return whole, run(1), run(pieces), _lib.device_error(clear=True)
-
-
-@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-@pytest.mark.parametrize("microbatches,pieces", [(1, 3), (3, 2)])
-def test_nccl_sequence_pieces_with_split_head(microbatches, pieces):
-    """Two stages over NCCL with the split head: sequence pieces (more items in split_head_program's order, each
-    head slice copied row by row into the last stage's logits) give the logits of whole micro-batches, bit for
-    bit."""
-    cfg = dict(vocab_size=1000, d_model=256, n_layers=4, n_heads=4, n_kv_heads=2, max_seq_len=512)
-    res = run_distributed(pieces_split_head_worker, 2, cfg, 6, 384, microbatches, pieces, backend="nccl",
-                          timeout=300)
-    assert res[0][:3] == (None, None, None)
-    whole, split, split_pieces, err = res[1]
-    assert torch.equal(whole, split) and torch.equal(whole, split_pieces)
-    assert err == 0 and res[0][3] == 0
-
-
 def overlap_worker(rank, size, cfg_dict, prompt, n, microbatches):
     from forgeserve_b200 import _lib
     from forgeserve_b200.weights import init_stage_
@@ -231,32 +198,3 @@ def test_8b_shape_layer_bf16_against_oracle():
     assert err < 0.05 * want.abs().max().item(), err
     rel = ((got - want).norm() / want.norm()).item()
     assert rel < 1e-2, rel
-
-
-def grid_worker(rank, size, cfg_dict, full_sd, idx, more, stages):
-    from forgeserve_b200 import _lib
-    from forgeserve_b200.transport import make_grid
-    cfg = ModelConfig(**cfg_dict)
-    stage_idx, tp, transport = make_grid(stages, size // stages)
-    stage = PipelineStage(cfg, stage_idx, stages, tp=tp, transport=transport).eval()
-    stage.load_from_full(full_sd)
-    state = PipelineState(stage, idx.shape[0], 2)
-    first = pipeline_forward(stage, state, idx if stage.is_first else None, idx.shape[1])
-    cont = pipeline_forward(stage, state, more if stage.is_first else None, more.shape[1])
-    return (None if first is None else first.cpu()), (None if cont is None else cont.cpu()), \
-        _lib.device_error(clear=True)
-
-
-@pytest.mark.skipif(torch.cuda.device_count() < 4, reason="needs 4 GPUs")
-def test_nccl_tensor_parallel_stages_match_reference():
-    """A 2 x 2 grid over NCCL (two stages, each split over two shards; transport.make_grid): the last stage's
-    shards return the reference's logits (fp32, 1e-4), continued through the shards' caches."""
-    g, sd = load_small()
-    res = run_distributed(grid_worker, 4, g["cfg"], sd, g["idx"], g["more"], 2, backend="nccl", timeout=300)
-    for rank, (first, cont, err) in enumerate(res):
-        assert err == 0
-        if rank >= 2:
-            torch.testing.assert_close(first, g["logits"], atol=1e-4, rtol=1e-4)
-            torch.testing.assert_close(cont, g["logits_more"], atol=1e-4, rtol=1e-4)
-        else:
-            assert first is None and cont is None
