@@ -347,8 +347,8 @@ def _reserve_caches(stage: PipelineStage, caches: List, rows: int, t: int) -> No
     pieces never grow (and copy) them."""
     cfg = stage.cfg
     for kv in caches:
-        if isinstance(kv, ContiguousKV):
-            kv.reserve(rows, cfg.n_kv_heads, cfg.head_dim, t, stage.dtype, stage.device)
+        if isinstance(kv, ContiguousKV):     # the stage's own KV heads (all of them, or its tensor-parallel share)
+            kv.reserve(rows, cfg.n_kv_heads // stage.tp.size, cfg.head_dim, t, stage.dtype, stage.device)
 
 
 @torch.no_grad()

@@ -200,32 +200,34 @@ def _oracle_tp_stage_class():
     return OracleTPStage
 
 
-def grid_worker(rank, size, cfg_dict, full_sd, idx, more, microbatches, stages, prompt):
+def grid_worker(rank, size, cfg_dict, full_sd, idx, more, microbatches, stages, prompt, pieces=1):
     import forgeserve_b200.pipeline as P
     from forgeserve_b200 import ModelConfig, PipelineState, pipeline_forward
     from forgeserve_b200.transport import make_grid
     P.sample = lambda logits, temperature=0.0, generator=None: logits.argmax(-1)   # CPU greedy, test-only
+    P.SEQ_PIECE_QUANTUM, P.PIECE_MIN_ROWS = 2, 1      # test-only: short sequences
     cfg = ModelConfig(**cfg_dict)
     stage_idx, tp, transport = make_grid(stages, size // stages)
     stage = _oracle_tp_stage_class()(cfg, stage_idx, stages, device="cpu", tp=tp, transport=transport)
     stage.load_from_full(full_sd)
     state = PipelineState(stage, idx.shape[0], microbatches)
-    first = pipeline_forward(stage, state, idx if stage.is_first else None, idx.shape[1])
-    cont = pipeline_forward(stage, state, more if stage.is_first else None, more.shape[1])
-    gen = P.pipeline_generate(stage, prompt, 10, microbatches)
+    first = pipeline_forward(stage, state, idx if stage.is_first else None, idx.shape[1], seq_chunks=pieces)
+    cont = pipeline_forward(stage, state, more if stage.is_first else None, more.shape[1], seq_chunks=pieces)
+    gen = P.pipeline_generate(stage, prompt, 10, microbatches, seq_chunks=pieces)
     shapes = {k: tuple(v.shape) for k, v in stage.state_dict().items()}
     return stage_idx, tp.rank, first, cont, gen, shapes
 
 
-@pytest.mark.parametrize("stages,shards,microbatches", [(2, 2, 1), (2, 2, 2), (3, 2, 4), (3, 1, 2), (1, 4, 2)])
-def test_tensor_parallel_stages_over_gloo(golden, stages, shards, microbatches):
+@pytest.mark.parametrize("stages,shards,microbatches,pieces",
+                         [(2, 2, 1, 1), (2, 2, 2, 1), (3, 2, 4, 1), (3, 1, 2, 1), (1, 4, 2, 1), (2, 2, 2, 3)])
+def test_tensor_parallel_stages_over_gloo(golden, stages, shards, microbatches, pieces):
     """A stages x shards grid (transport.make_grid): every shard of the last stage returns the reference pipeline's
     logits, continued through the shards' caches, and every rank generates the reference's tokens; each shard holds
     its cut of its stage's layers."""
     from forgeserve_b200.tensor_parallel import run_distributed
     g, sd = golden
     res = run_distributed(grid_worker, stages * shards, g["cfg"], sd, g["idx"], g["more"], microbatches, stages,
-                          g["prompt"], backend="gloo", timeout=300)
+                          g["prompt"], pieces, backend="gloo", timeout=300)
     for rank, (stage_idx, shard, first, cont, gen, shapes) in enumerate(res):
         assert (stage_idx, shard) == divmod(rank, shards)
         if stage_idx == stages - 1:
