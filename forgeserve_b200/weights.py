@@ -75,9 +75,18 @@ def open_state_dict(path) -> Dict[str, torch.Tensor]:
     return torch.load(path, map_location="cpu", mmap=True, weights_only=True)
 
 
+def _own_part(name: str, full: torch.Tensor, cfg: ModelConfig, tp) -> torch.Tensor:
+    """The part of a full tensor that a tensor-parallel shard holds (all of it without tensor parallelism)."""
+    if tp is None or tp.size == 1:
+        return full
+    from .tensor_parallel import shard_state_dict
+    return shard_state_dict({name: full}, cfg, tp.rank, tp.size)[name]
+
+
 @torch.no_grad()
 def init_stage_(stage, seed: int = 0, std: float = 0.02) -> None:
-    """Fill a PipelineStage with the seeded weights of its own layers (global layer numbering), on its device."""
+    """Fill a PipelineStage with the seeded weights of its own layers (global layer numbering), on its device; a
+    tensor-parallel stage takes its shard of each tensor."""
     shapes = model_shapes(stage.cfg)
     for name, p in stage.named_parameters():
         if name.startswith("layers."):
@@ -85,12 +94,15 @@ def init_stage_(stage, seed: int = 0, std: float = 0.02) -> None:
             gname = name.replace(f"layers.{i}.", f"layers.{i + stage.lo}.", 1)
         else:
             gname = name
-        p.copy_(seeded_tensor(gname, shapes[gname], seed, std, device=p.device, dtype=p.dtype))
+        full = seeded_tensor(gname, shapes[gname], seed, std, device=p.device, dtype=p.dtype)
+        p.copy_(_own_part(gname, full, stage.cfg, getattr(stage, "tp", None)))
 
 
 @torch.no_grad()
 def init_model_(model, seed: int = 0, std: float = 0.02) -> None:
-    """Fill a ForgeModel with the same seeded weights (tied head = embedding)."""
+    """Fill a ForgeModel with the same seeded weights (tied head = embedding); a tensor-parallel model takes its
+    shard of each tensor."""
     shapes = model_shapes(model.cfg)
     for name, p in model.named_parameters():
-        p.copy_(seeded_tensor(name, shapes[name], seed, std, device=p.device, dtype=p.dtype))
+        full = seeded_tensor(name, shapes[name], seed, std, device=p.device, dtype=p.dtype)
+        p.copy_(_own_part(name, full, model.cfg, getattr(model, "tp", None)))

@@ -228,3 +228,24 @@ def test_stages_load_from_a_mapped_state_dict_file(tmp_path):
     c.load_from_file(path)
     lo = c.lo
     assert torch.equal(c.layers[0].mlp.w_down.weight, full[f"layers.{lo}.mlp.w_down.weight"].to(torch.bfloat16))
+
+
+def test_seeded_weights_of_tensor_parallel_shards():
+    """weights.init_stage_ / init_model_ on tensor-parallel modules: each shard holds its cut of the same seeded
+    tensors that a whole stage or model gets."""
+    from forgeserve_b200.tensor_parallel import shard_state_dict
+    from forgeserve_b200.weights import init_model_, init_stage_, seeded_state_dict
+    cfg = small_cfg()
+    full = seeded_state_dict(cfg, seed=3)
+    for rank in range(2):
+        st = PipelineStage(cfg, 1, 2, device="cpu", tp=fs.TPContext(rank, 2))
+        init_stage_(st, seed=3)
+        want = PipelineStage(cfg, 1, 2, device="cpu", tp=fs.TPContext(rank, 2))
+        want.load_from_full(full)
+        for (k, a), (_, b) in zip(st.state_dict().items(), want.state_dict().items()):
+            assert torch.equal(a, b), k
+        m = fs.ForgeModel(cfg, fs.TPContext(rank, 2), device="cpu")
+        init_model_(m, seed=3)
+        shard = shard_state_dict(full, cfg, rank, 2)
+        for k, v in m.state_dict().items():
+            assert torch.equal(v, shard[k]), k
