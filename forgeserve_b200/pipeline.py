@@ -167,6 +167,9 @@ class PipelineStage(nn.Module):
         self._rope = RopeTables(cfg)
         self.register_buffer("rope_cos", self._rope.cos.to(device), persistent=False)
         self.register_buffer("rope_sin", self._rope.sin.to(device), persistent=False)
+        if tp.size > 1 and transport is None:
+            raise ValueError("a tensor-parallel stage needs the transport of its grid (transport.make_grid): the "
+                             "default one pairs neighbouring world ranks, not the same shard of neighbouring stages")
         self.transport = transport if transport is not None else default_transport()
         self.trace: Optional[List] = None   # set to a list to record (mb, start, end) CUDA events per micro-batch
         self.head_split: Optional[_HeadSplit] = None   # see split_head_

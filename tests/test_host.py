@@ -230,6 +230,11 @@ def test_stages_load_from_a_mapped_state_dict_file(tmp_path):
     assert torch.equal(c.layers[0].mlp.w_down.weight, full[f"layers.{lo}.mlp.w_down.weight"].to(torch.bfloat16))
 
 
+def test_tensor_parallel_stage_needs_the_grid_transport():
+    with pytest.raises(ValueError, match="make_grid"):
+        PipelineStage(small_cfg(), 0, 2, device="cpu", tp=fs.TPContext(0, 2))
+
+
 def test_seeded_weights_of_tensor_parallel_shards():
     """weights.init_stage_ / init_model_ on tensor-parallel modules: each shard holds its cut of the same seeded
     tensors that a whole stage or model gets."""
@@ -238,9 +243,10 @@ def test_seeded_weights_of_tensor_parallel_shards():
     cfg = small_cfg()
     full = seeded_state_dict(cfg, seed=3)
     for rank in range(2):
-        st = PipelineStage(cfg, 1, 2, device="cpu", tp=fs.TPContext(rank, 2))
+        # the stages only hold weights here: a placeholder stands in for the grid transport
+        st = PipelineStage(cfg, 1, 2, device="cpu", tp=fs.TPContext(rank, 2), transport=object())
         init_stage_(st, seed=3)
-        want = PipelineStage(cfg, 1, 2, device="cpu", tp=fs.TPContext(rank, 2))
+        want = PipelineStage(cfg, 1, 2, device="cpu", tp=fs.TPContext(rank, 2), transport=object())
         want.load_from_full(full)
         for (k, a), (_, b) in zip(st.state_dict().items(), want.state_dict().items()):
             assert torch.equal(a, b), k
