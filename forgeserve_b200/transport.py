@@ -190,6 +190,7 @@ def make_grid(stages: int, shards: int):
     if world != stages * shards:
         raise ValueError(f"a {stages} x {shards} grid needs {stages * shards} ranks, the world has {world}")
     stage, shard = divmod(me, shards)
+    os.environ.setdefault("NCCL_MAX_P2P_NCHANNELS", "2")     # as for the pair groups of one rank per stage
     tp_groups = [dist.new_group(list(range(s * shards, (s + 1) * shards))) for s in range(stages)]
     columns = [dist.new_group([s * shards + r for s in range(stages)]) for r in range(shards)]
     pairs = {}
