@@ -42,6 +42,7 @@ SIGNATURES = {
     "fs_last_error": (ctypes.c_char_p, []),
     "fs_device_error": (c_int, [c_int, ctypes.POINTER(ctypes.c_uint)]),
     "fs_launch_count": (c_i64, []),
+    "fs_wait_selftest": (c_int, [c_i64, c_vp, c_vp]),
     "fs_set_persistent_sms": (c_int, [c_int]),
     "fs_set_gemm_pair_mode": (c_int, [c_int]),
     "fs_ipc_handle": (c_int, [c_vp, c_vp, ctypes.POINTER(c_i64)]),

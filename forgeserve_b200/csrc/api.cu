@@ -52,12 +52,7 @@ static bool dtype_ok(int dtype) { return dtype == F32 || dtype == BF16; }
 
 static unsigned* g_error_words[64] = {nullptr};
 
-// The device's error word if it has been created already (no allocation); nullptr otherwise.
-unsigned* error_word_if_present() {
-  int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
-  return g_error_words[dev];
-}
+int static_decode_error_bits(int clear, unsigned* bits);  // attention_decode.cu
 
 unsigned* error_word() {
   unsigned** words = g_error_words;
@@ -77,11 +72,42 @@ unsigned* error_word() {
   return words[dev];
 }
 
+// Wait self-test: one warp. Lane 0 sets up an mbarrier that needs two arrivals and arrives once, then every lane
+// waits on its first phase with the bounded wait of the tensor-core kernels (mbar_wait) and a short limit. Nothing
+// else ever arrives, so the wait must run out, flag ERR_WAIT_TIMEOUT and return; the kernel then exits normally.
+// out[0] = nanoseconds lane 0 waited, out[1] = 1 if its wait completed (it never should).
+__global__ void wait_selftest_kernel(uint64_t limit_ns, unsigned* err, unsigned long long* out) {
+  __shared__ __align__(8) uint64_t bar;
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 2);
+    fence_barrier_init();
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) mbar_arrive(&bar);
+  const uint64_t t0 = globaltimer_ns();
+  const bool done = mbar_wait(&bar, 0, err, limit_ns);
+  const uint64_t t1 = globaltimer_ns();
+  if (threadIdx.x == 0) {
+    out[0] = t1 - t0;
+    out[1] = done ? 1ull : 0ull;
+  }
+}
+
 }  // namespace fs
 
 using namespace fs;
 
 extern "C" {
+
+int fs_wait_selftest(int64_t limit_ns, unsigned long long* out, void* stream) {
+  if (!out) return fail("fs_wait_selftest: NULL output");
+  if (limit_ns < 1000 || limit_ns > static_cast<int64_t>(kWaitLimitNs))
+    return fail("fs_wait_selftest: limit_ns must lie in [1000, " + std::to_string(kWaitLimitNs) + "]");
+  unsigned* err = error_word();
+  if (!err) return -1;
+  wait_selftest_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(static_cast<uint64_t>(limit_ns), err, out);
+  return check_launch("wait_selftest_kernel");
+}
 
 int fs_version(void) { return 100; }
 
@@ -99,6 +125,9 @@ int fs_device_error(int clear, unsigned* out_bits) {
     e = cudaMemset(word, 0, sizeof(unsigned));
     if (e != cudaSuccess) return fail(std::string("fs_device_error: ") + cudaGetErrorString(e));
   }
+  unsigned static_bits = 0;
+  if (static_decode_error_bits(clear, &static_bits)) return -1;
+  bits |= static_bits;
   if (out_bits) *out_bits = bits;
   return 0;
 }

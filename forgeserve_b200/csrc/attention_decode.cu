@@ -652,49 +652,78 @@ int launch(int dtype, const void* q, int64_t ldq, const KVCache& kv, int64_t n_s
 // synchronisation a cudaMalloc / cudaFree may cause in the middle of a step. fs_attention_decode needs a
 // workspace for its per-split partial results; this entry point uses a fixed scratch area that is part of the
 // library image instead: a file-scope __device__ array of kStaticScratchBytes (4 MiB), which every GPU that
-// loads the library holds until the process exits.
+// loads this module holds until the process exits.
 //
-// * Set-up: the first call on a device resolves the array's device address with cudaGetSymbolAddress (and the
-//   first launch of each kernel sets its shared-memory attribute) with that device current; make that first call
-//   before any stream capture on that device.
+// * Set-up and loading: the first call on a device resolves the array's device address (and that of a device
+//   error word beside it) with cudaGetSymbolAddress, with that device current, and launches the kernels for the
+//   first time. Under CUDA's lazy module loading (the default since CUDA 12) that first call is also what loads
+//   this module onto the device, which reserves the 4 MiB array and the kernels' code. So make one real call at
+//   start-up, before a host pool takes the device's free memory and before any stream capture on that device;
+//   after it, calls need no further device memory.
 // * Limit: calls whose split partials need more than kStaticScratchBytes are refused with an error naming the
-//   size (fs_attention_decode_workspace() gives the size a call needs).
+//   size (fs_attention_decode_workspace() gives the size a call needs: B * n_heads * splits * (head_dim + 2) * 4
+//   bytes). Example: at 32 query heads of head_dim 128, 64 rows fit up to 1536 cache slots (3 splits of 512).
 // * Sharing: every call uses the same array and leaves its contents behind; each call writes every partial it
 //   reads, so nothing needs clearing, but calls that overlap on the GPU (different streams, no ordering) race on
 //   the array and must not be issued.
-// * It allocates nothing: no cudaMalloc, cudaFree or allocating library routine. Device-side input errors (a block
-//   table entry outside the pool) are recorded in the library's error word only if that word already exists on
-//   the device (any other entry point creates it); the kernel never reads outside the cache either way.
+// * Errors: bad block-table entries and waits that run out of time are recorded in the file-scope word
+//   g_static_error (never in allocated memory); fs_device_error() reports and clears it together with the
+//   library's allocated error word.
+// * It allocates nothing: no cudaMalloc, cudaFree or allocating library routine.
 // =============================================================================================================
 namespace fs {
 namespace decode {
 
 constexpr int64_t kStaticScratchBytes = int64_t(4) << 20;
 static __device__ __align__(256) unsigned char g_static_scratch[kStaticScratchBytes];
+static __device__ unsigned g_static_error;
 
 struct StaticScratch {
   float* ptr = nullptr;
+  unsigned* err = nullptr;
   bool ready = false;
 };
+static StaticScratch g_static_per_dev[64];
 
-static int static_scratch(float** out) {
-  static StaticScratch per_dev[64];
+static int static_scratch(float** out, unsigned** err) {
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return fail("no current CUDA device");
-  StaticScratch& s = per_dev[dev];
+  StaticScratch& s = g_static_per_dev[dev];
   if (!s.ready) {
     void* p = nullptr;
-    const cudaError_t e = cudaGetSymbolAddress(&p, g_static_scratch);
+    void* e_word = nullptr;
+    cudaError_t e = cudaGetSymbolAddress(&p, g_static_scratch);
     if (e != cudaSuccess) return fail(std::string("cudaGetSymbolAddress(decode scratch): ") + cudaGetErrorString(e));
+    e = cudaGetSymbolAddress(&e_word, g_static_error);
+    if (e != cudaSuccess) return fail(std::string("cudaGetSymbolAddress(decode error word): ") + cudaGetErrorString(e));
     s.ptr = static_cast<float*>(p);
+    s.err = static_cast<unsigned*>(e_word);
     s.ready = true;
   }
   *out = s.ptr;
+  *err = s.err;
   return 0;
 }
 
 }  // namespace decode
-unsigned* error_word_if_present();
+
+// Bits of the static entry point's error word on the current device (0 if it never ran there); clears them if
+// asked. Called by fs_device_error after a device synchronisation; copies only, no allocation.
+int static_decode_error_bits(int clear, unsigned* bits) {
+  *bits = 0;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 0;
+  const decode::StaticScratch& s = decode::g_static_per_dev[dev];
+  if (!s.ready) return 0;
+  cudaError_t e = cudaMemcpy(bits, s.err, sizeof(unsigned), cudaMemcpyDeviceToHost);
+  if (e != cudaSuccess) return fail(std::string("static decode error word: ") + cudaGetErrorString(e));
+  if (clear) {
+    e = cudaMemset(s.err, 0, sizeof(unsigned));
+    if (e != cudaSuccess) return fail(std::string("static decode error word: ") + cudaGetErrorString(e));
+  }
+  return 0;
+}
+
 }  // namespace fs
 
 extern "C" int fs_attention_decode_static(const void* q, int64_t ldq, const fs_kv_cache* kvd, int64_t n_slots,
@@ -734,7 +763,8 @@ extern "C" int fs_attention_decode_static(const void* q, int64_t ldq, const fs_k
                 " bytes of scratch, more than the fixed " + std::to_string(kStaticScratchBytes) +
                 " bytes; use fs_attention_decode with a caller-owned workspace");
   float* ws = nullptr;
-  if (static_scratch(&ws)) return -1;
-  return launch(dtype, q, ldq, *kv, n_slots, positions, out, ldo, B, nh, nkv, hd, scale, splits, ws,
-                error_word_if_present(), static_cast<cudaStream_t>(stream));
+  unsigned* err = nullptr;
+  if (static_scratch(&ws, &err)) return -1;
+  return launch(dtype, q, ldq, *kv, n_slots, positions, out, ldo, B, nh, nkv, hd, scale, splits, ws, err,
+                static_cast<cudaStream_t>(stream));
 }

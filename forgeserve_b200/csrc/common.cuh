@@ -103,14 +103,16 @@ __device__ __forceinline__ uint64_t globaltimer_ns() {
 constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s
 
 // Bounded wait on an mbarrier phase. Returns false (and flags ERR_WAIT_TIMEOUT) if the phase did not
-// complete within kWaitLimitNs; callers then abandon their work and fall through to the kernel's clean-up.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, unsigned* err) {
+// complete within limit_ns (kWaitLimitNs unless a caller passes a shorter limit, as the wait self-test does);
+// callers then abandon their work and fall through to the kernel's clean-up.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, unsigned* err,
+                                          uint64_t limit_ns = kWaitLimitNs) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = globaltimer_ns();
   uint32_t spins = 0;
   while (true) {
     if (mbar_try_wait(bar, parity)) return true;
-    if ((++spins & 255u) == 0 && globaltimer_ns() - t0 > kWaitLimitNs) {
+    if ((++spins & 255u) == 0 && globaltimer_ns() - t0 > limit_ns) {
       flag_error(err, ERR_WAIT_TIMEOUT);
       return false;
     }

@@ -36,6 +36,14 @@ const char* fs_last_error(void);
 /* Reads (and, if clear != 0, resets) the device error word of the current device. Synchronises the device. */
 int fs_device_error(int clear, unsigned* out_bits);
 
+/* Self-test of the bounded device waits: launches one warp that waits, through the same bounded mbarrier wait as
+ * the tensor-core kernels, on a barrier that never completes, with a time limit of limit_ns (1000 ns .. 2 s; the
+ * kernels use 2 s). The wait gives up, sets FS_ERR_WAIT_TIMEOUT in the device error word and the kernel returns, so
+ * the context stays usable. out: two device uint64 words, the nanoseconds waited and 1 if the wait completed.
+ * Stands in, on the device, for the reference's host-side timeout on a stuck rank (forgeserve/tensor_parallel.py
+ * :76-87, a RuntimeError instead of a hang). */
+int fs_wait_selftest(int64_t limit_ns, unsigned long long* out, void* stream);
+
 /* Number of kernel launches made by this library in this process (all devices). */
 int64_t fs_launch_count(void);
 
@@ -150,10 +158,14 @@ int fs_attention_decode(const void* q, int64_t ldq, const fs_kv_cache* kv, int64
 /* fs_attention_decode for callers that cannot allocate device memory where they run a decode step (a host that
  * owns all device memory through its own pool, a plugin that is only handed device pointers, a loop that cannot
  * take the synchronisation of a cudaMalloc mid-step): the split partials go to a fixed 4 MiB scratch array that is
- * part of the library image (held on every GPU that loads the library until exit) instead of a caller workspace.
- * Allocates nothing. The first call on a device looks up that array's address (make it before any stream capture
- * on the device). Calls needing more scratch than 4 MiB (see fs_attention_decode_workspace) are refused with an
- * error. All calls share the array, so calls that overlap on the GPU race and must not be issued.
+ * part of the library image (held on every GPU that loads it until exit) instead of a caller workspace.
+ * Allocates nothing. The first call on a device looks up that array's address and, under CUDA's default lazy
+ * module loading, loads the kernels and reserves the array: make one real call at start-up, before a host pool
+ * takes the device's free memory and before any stream capture on the device. Calls needing more scratch than
+ * 4 MiB (fs_attention_decode_workspace: B * n_heads * splits * (head_dim + 2) * 4 bytes, a split per 512 cache
+ * slots; e.g. 64 rows of 32 x 128 heads fit up to 1536 slots) are refused with an error. All calls share the
+ * array, so calls that overlap on the GPU race and must not be issued. Device-side errors go to a file-scope
+ * word that fs_device_error reads with the library's own.
  * No counterpart in the reference (it has no kernels or device memory). */
 int fs_attention_decode_static(const void* q, int64_t ldq, const fs_kv_cache* kv, int64_t n_slots,
                                const int64_t* positions, void* out, int64_t ldo, int64_t B, int64_t nh, int64_t nkv,

@@ -66,3 +66,20 @@ def test_empty_work_is_a_no_op(lib):
     assert lib.fs_gemm(None, 64, None, 64, None, 64, None, 0, 0, 64, 64, 64, 0, 1, None) == 0
     assert lib.fs_argmax(None, 0, 10, 10, None, 1, None) == 0
     assert lib.fs_embed(None, 0, None, 10, 8, None, 1, None) == 0
+
+
+def test_static_decode_refuses_a_call_beyond_its_fixed_scratch_on_the_host(lib):
+    """fs_attention_decode_static answers a call whose split partials exceed its fixed 4 MiB array with an error
+    naming the size, before any device work (the pointers below are never dereferenced)."""
+    p = 4096
+    B, nh, nkv, hd, n_slots = 64, 32, 8, 128, 2048
+    need = lib.fs_attention_decode_workspace(B, nh, nkv, hd, n_slots)
+    assert need == B * nh * 4 * (hd + 2) * 4 > 4 << 20
+    assert lib.fs_attention_decode_workspace(B, nh, nkv, hd, 1536) == B * nh * 3 * (hd + 2) * 4 <= 4 << 20
+    desc = L.KVCacheDesc(k=p, v=p, table=p, table_stride=128, table_cols=128, block_size=16,
+                         block_stride=nkv * 16 * hd, head_stride=16 * hd, num_blocks=128)
+    rc = lib.fs_attention_decode_static(ctypes.c_void_p(p), nh * hd, ctypes.byref(desc), n_slots, ctypes.c_void_p(p),
+                                        ctypes.c_void_p(p), nh * hd, B, nh, nkv, hd, ctypes.c_float(hd ** -0.5),
+                                        L.FS_BF16, None)
+    assert rc == -1
+    assert f"needs {need} bytes of scratch".encode() in lib.fs_last_error()

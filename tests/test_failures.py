@@ -53,3 +53,16 @@ def test_thread_ranks_report_failures():
     from forgeserve_b200.tensor_parallel import run_in_threads
     with pytest.raises(RuntimeError, match="rank 1 failed"):
         run_in_threads(raising_worker, 2, timeout=10)
+
+
+def test_wait_selftest_rejects_limits_outside_its_range_on_the_host():
+    """Argument checks of the bounded-wait self-test answer before anything touches a GPU."""
+    import ctypes
+    from forgeserve_b200 import _lib as L
+    lib = L.load()
+    out = ctypes.c_void_p(16)
+    assert lib.fs_wait_selftest(10, out, None) == -1
+    assert b"limit_ns" in lib.fs_last_error()
+    assert lib.fs_wait_selftest(3_000_000_000, out, None) == -1
+    assert lib.fs_wait_selftest(1_000_000, None, None) == -1
+    assert b"NULL" in lib.fs_last_error()
