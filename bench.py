@@ -115,6 +115,75 @@ class ClockSampler:
                 "samples": len(sm)}
 
 
+# ------------------------------------------------------------------------------------------ parity prologue
+PARITY_FIXTURE = ROOT / "tests" / "golden" / "pp8.pt"
+
+
+def parity_check(world, rank, dev, split_head: bool, seq_chunks: int):
+    """Before any timing: the pipeline this run times (N stages over NCCL, the same head split and sequence pieces)
+    on the 8-layer golden model of tests/golden/pp8.pt, against the reference's own outputs recorded there
+    (its single-process model, which its pipeline matches within 1e-4): fp32 logits at 10 positions of 8 rows x
+    512 tokens within atol = rtol = 1e-4, its 16 greedy tokens per row through pipeline_generate, and the bf16
+    logits (tensor-core path) within max(2e-2, 1.1 x the spread between two bf16 renderings of the reference) after
+    log-softmax. Outside the timed region; the result goes into the JSON line."""
+    import torch.distributed as dist
+
+    from forgeserve_b200 import ModelConfig, PipelineStage, PipelineState, pipeline_forward, pipeline_generate
+    from forgeserve_b200.weights import checksum, test_suite_state_dict
+
+    g = torch.load(PARITY_FIXTURE, weights_only=False)
+    cfg = ModelConfig(**g["cfg"])
+    B, T = g["idx"].shape
+    mbs = 4
+    res = {"model": "tests/golden/pp8.pt: 8 layers, d_model 512, 4/2 heads (head_dim 128), vocab 2048; reference "
+                    "outputs", "stages": world, "microbatches": mbs,
+           "seq_pieces": seq_chunks, "head": "split over the stages" if split_head else "on the last stage"}
+    for mode, dtype in (("fp32", torch.float32), ("bf16", torch.bfloat16)):
+        recipe, ck = (g["weights"], g["checksum"]) if mode == "fp32" else (g["bf16_weights"], g["bf16_checksum"])
+        sd = test_suite_state_dict(cfg, recipe[1], recipe[2])
+        got_ck = checksum(sd)      # fp64 sums: equal up to the host's reduction order
+        if set(got_ck) != set(ck) or any(abs(a - b) > 1e-9 * max(1.0, abs(b))
+                                         for k in ck for a, b in zip(got_ck[k], ck[k])):
+            raise RuntimeError("parity fixture: the weight recipe does not reproduce the recorded checksums")
+        stage = PipelineStage(cfg, rank, world, device=dev, dtype=dtype).eval()
+        stage.load_from_full(sd)
+        if split_head:
+            stage.split_head_()
+        state = PipelineState(stage, B, mbs)
+        logits = pipeline_forward(stage, state, g["idx"].to(dev) if stage.is_first else None, T,
+                                  seq_chunks=seq_chunks)
+        err = torch.zeros(2, dtype=torch.float64, device=dev)
+        if stage.is_last:
+            got = logits[:, g["positions"].to(dev)].float().cpu()
+            if mode == "fp32":
+                want = g["logits"]
+                err[0] = float(((got - want).abs() / (1e-4 + 1e-4 * want.abs())).max())   # <= 1 passes
+                err[1] = float((got - want).abs().max())
+            else:
+                lg = torch.log_softmax(got, -1) - torch.log_softmax(g["bf16_logits"].float(), -1)
+                err[0] = float(lg.abs().max())
+        if world > 1:
+            dist.broadcast(err, src=world - 1)
+        if mode == "fp32":
+            res["fp32_logits_maxabs"] = round(float(err[1]), 7)
+            res["fp32_within_1e-4"] = bool(float(err[0]) <= 1.0)
+            toks = pipeline_generate(stage, g["prompt"], 16, microbatches=mbs)
+            res["greedy_tokens_equal"] = bool(torch.equal(toks.cpu(), g["generate"]))
+        else:
+            bar = max(2e-2, 1.1 * g["bf16_spread"])
+            res.update({"bf16_logsoftmax_maxabs": round(float(err[0]), 5), "bf16_bar": round(bar, 5),
+                        "bf16_within_bar": bool(float(err[0]) <= bar)})
+        del stage, state, logits
+    if world > 1:
+        flag = torch.tensor([float(res["greedy_tokens_equal"])], device=dev)
+        dist.all_reduce(flag, op=dist.ReduceOp.MIN)
+        res["greedy_tokens_equal"] = bool(float(flag) == 1.0)
+    res["ok"] = res["fp32_within_1e-4"] and res["greedy_tokens_equal"] and res["bf16_within_bar"]
+    torch.cuda.synchronize()
+    torch.cuda.empty_cache()
+    return res
+
+
 # --------------------------------------------------------------------------------------------------- ours
 def run_ours(args, spec):
     import torch.distributed as dist
@@ -148,11 +217,12 @@ def run_ours(args, spec):
 
     cfg = ModelConfig(**spec["cfg"])
     microbatches, mb_rows, seq = spec["microbatches"], spec["rows"], spec["seq"]
+    split_head = world > 1 and not args.whole_head
+    parity = parity_check(world, rank, dev, split_head, args.seq_chunks)
     stage = PipelineStage(cfg, rank, world, device=dev, dtype=torch.bfloat16).eval()
     init_stage_(stage, seed=1234, std=0.02)
     weight_gb = allreduce(sum(p.numel() * p.element_size() for p in stage.parameters()),
                           dist.ReduceOp.SUM if world > 1 else None) / 1e9
-    split_head = world > 1 and not args.whole_head
     if split_head:
         stage.split_head_()   # every stage computes a vocab slice of the head (logits still land on the last stage)
     batch = microbatches * mb_rows
@@ -260,7 +330,10 @@ def run_ours(args, spec):
                          "launches": int(gemm_n), "traffic": gemm_traffic() if spec["cfg"] is CFG else None},
             "e2e": {"value": round(tokens_per_step * args.steps / (e2e_ms / 1e3), 1), "unit": "tokens/s",
                     "h2d_bytes_per_step": idx_host.numel() * idx_host.element_size(),
-                    "d2h_bytes_per_step": batch * cfg.vocab_size * 2},
+                    "d2h_bytes_per_step": batch * cfg.vocab_size * 2,
+                    "io": "token ids from pinned host memory in; the last position's logits of every row "
+                          "(B x vocab bf16) back to pinned host memory; all-position logits stay on the device"},
+            "parity": parity,
             "per_rank": gathered,
             "gpu_launches": int(launches),
             "clocks": clocks,
@@ -584,9 +657,11 @@ def cpu_sample(steps: int, warmup: int, spec=None):
     t_head = statistics.median(h for _, h in times)
     per_row = cfg.n_layers * t_layer + t_head
     return {"value": round(seq / per_row, 2), "unit": "tokens/s", "cores": threads, "kind": "port",
-            "sample": f"oracle fp32: 1 of {cfg.n_layers} layers + final norm/head on 1 x {seq} tokens per step, "
-                      f"extrapolated to the {cfg.n_layers}-layer model "
-                      f"(t_layer {t_layer:.3f} s, t_head {t_head:.3f} s)"}
+            "sample": f"oracle fp32: 1 of {cfg.n_layers} layers + final norm/head on 1 x {seq} tokens per step "
+                      f"(measured: t_layer {t_layer:.3f} s, t_head {t_head:.3f} s per step), value extrapolated "
+                      f"to the {cfg.n_layers}-layer model: {seq} tokens / ({cfg.n_layers} t_layer + t_head)",
+            "sample_ms_per_step": round((t_layer + t_head) * 1e3, 3),
+            "extrapolated_ms_per_row": round(per_row * 1e3, 3)}
 
 
 def run_reference(args, spec):
@@ -598,8 +673,11 @@ def run_reference(args, spec):
     cb = cpu_sample(args.steps, args.warmup, spec)
     wall = time.perf_counter() - t0
     seq = spec["seq"]
+    # ms_per_step is the measured time of one step of the sample that ran (one layer and the head on one row);
+    # the whole model's time for that row, from which `value` comes, is extrapolated_ms_per_row
     return {"metric": spec["metric"], "value": cb["value"], "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": round(seq / cb["value"] * 1e3, 3), "higher_is_better": True,
+            "warmup": args.warmup, "ms_per_step": cb["sample_ms_per_step"],
+            "extrapolated_ms_per_row": cb["extrapolated_ms_per_row"], "higher_is_better": True,
             "scaling": "strong", "vs_baseline": None, "dtype": "f32", "impl": "reference",
             "data": "synthetic: random fp32 weights (std 0.02) and activations",
             "config": {"workload": spec["workload"], "global_batch": spec["microbatches"] * spec["rows"],
@@ -735,9 +813,10 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--whole-head", action="store_true", help="N > 1: keep the whole output head on the last stage")
-    ap.add_argument("--seq-chunks", type=int, default=1,
-                    help="c3, c5: pieces per micro-batch along the sequence in the prompt's forward; c4 with N > 1: "
-                         "pieces per prefill (pipeline_forward's seq_chunks, PipelineEngine's prefill_chunks)")
+    ap.add_argument("--seq-chunks", type=int, default=0,
+                    help="c3, c2, c5: pieces per micro-batch along the sequence in the prompt's forward; c4 with "
+                         "N > 1: pieces per prefill (pipeline_forward's seq_chunks, PipelineEngine's "
+                         "prefill_chunks). 0 (default): 4 for c3 and c2 with N > 1, else 1")
     ap.add_argument("--workload", choices=["c3", "c2", "c4", "c5"], default="c3",
                     help="c3: 8B-shape pipeline prefill (the headline metric); c2: 1B-shape pipeline prefill; "
                          "c4: continuous-batching decode; c5: 70B-shape generation, micro-batch sweep")
@@ -750,6 +829,8 @@ def main():
     ap.add_argument("--reps", type=int, default=3)
     ap.add_argument("--timed", action="store_true", help="with --profile-case: also time cold-L2 launches")
     args = ap.parse_args()
+    if args.seq_chunks <= 0:
+        args.seq_chunks = 4 if args.workload in ("c3", "c2") and args.gpus > 1 else 1
     if args.profile_case:
         for name in args.profile_case.split(","):
             profile_case(name, args.reps, args.timed)

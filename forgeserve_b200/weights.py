@@ -106,3 +106,23 @@ def init_model_(model, seed: int = 0, std: float = 0.02) -> None:
     for name, p in model.named_parameters():
         full = seeded_tensor(name, shapes[name], seed, std, device=p.device, dtype=p.dtype)
         p.copy_(_own_part(name, full, model.cfg, getattr(model, "tp", None)))
+
+
+def test_suite_state_dict(cfg: ModelConfig, seed: int, scale: float) -> Dict[str, torch.Tensor]:
+    """The weights the reference's test suite gives its models (forgeserve tests/conftest.py:18-27): every
+    parameter of two or more dimensions, in ForgeModel.parameters() order (model.py:109-122: embedding, then per
+    layer attn_norm, wq, wk, wv, wo, mlp_norm, w_gate, w_up, w_down, then the final norm), replaced by
+    randn(shape, generator seeded `seed`) * scale; norms stay ones; the head is the embedding (tied). fp32, CPU."""
+    g = torch.Generator().manual_seed(seed)
+    sd = {}
+    for name, shape in model_shapes(cfg).items():
+        if name == "lm_head.weight":
+            continue
+        sd[name] = torch.randn(shape, generator=g) * scale if len(shape) >= 2 else torch.ones(shape)
+    sd["lm_head.weight"] = sd["tok_emb.weight"]
+    return sd
+
+
+def checksum(sd: Dict[str, torch.Tensor]) -> Dict[str, tuple]:
+    """Per-tensor (sum, sum of squares) in fp64: how a recorded fixture names the weights it was made with."""
+    return {k: (float(v.double().sum()), float(v.double().pow(2).sum())) for k, v in sd.items()}

@@ -7,7 +7,8 @@ Restated from the reference (omkarbhad/forgeserve; file:line of that project):
   rope_tables         forgeserve/model.py:34-37
   apply_rope          forgeserve/model.py:40-45
   attention           forgeserve/model.py:62-78 (repeat_interleave :70-71, mask :75, SDPA :76 written out as
-                      softmax(QK^T / sqrt(hd) + mask) V)
+                      softmax(QK^T / sqrt(hd) + mask) V in fp32; or, with attn_core=sdpa_torch, the reference's
+                      own torch scaled_dot_product_attention call in the inputs' dtype)
   swiglu              forgeserve/model.py:92-93
   block               forgeserve/model.py:104-106
   model_forward       forgeserve/model.py:140-159 (tied head :120, :137-138)
@@ -76,6 +77,14 @@ def sdpa(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, mask: torch.Tensor) 
     return torch.matmul(p, v.float()).to(q.dtype)
 
 
+def sdpa_torch(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, mask: torch.Tensor) -> torch.Tensor:
+    """The reference's own attention call (model.py:76): torch's fused scaled_dot_product_attention with the
+    boolean mask, in the inputs' dtype. In fp32 on the CPU it equals `sdpa` within rounding; in bf16 on a GPU it is
+    the kernel the reference's module itself would run there (bf16 probabilities into P V), one of several valid
+    bf16 renderings of the same algebra."""
+    return torch.nn.functional.scaled_dot_product_attention(q, k, v, attn_mask=mask)
+
+
 class ContiguousCache:
     def __init__(self):
         self.k: Optional[torch.Tensor] = None
@@ -118,7 +127,8 @@ class PagedPool:
         return _View()
 
 
-def attention(sd: Dict[str, torch.Tensor], p: str, x: torch.Tensor, cfg: Cfg, cos, sin, positions, kv) -> torch.Tensor:
+def attention(sd: Dict[str, torch.Tensor], p: str, x: torch.Tensor, cfg: Cfg, cos, sin, positions, kv,
+              attn_core=None) -> torch.Tensor:
     b, t, _ = x.shape
     nh, nkv, hd = cfg.n_heads, cfg.n_kv_heads, cfg.head_dim
     q = (x @ sd[p + "attn.wq.weight"].t()).view(b, t, nh, hd).transpose(1, 2)
@@ -131,7 +141,7 @@ def attention(sd: Dict[str, torch.Tensor], p: str, x: torch.Tensor, cfg: Cfg, co
     v_all = v_all.repeat_interleave(rep, dim=1)
     s = k_all.shape[2]
     mask = (torch.arange(s, device=positions.device)[None, None, :] <= positions[:, :, None])[:, None]
-    out = sdpa(q, k_all, v_all, mask)
+    out = (attn_core or sdpa)(q, k_all, v_all, mask)
     return out.transpose(1, 2).reshape(b, t, -1) @ sd[p + "attn.wo.weight"].t()
 
 
@@ -141,9 +151,10 @@ def swiglu(sd, p: str, x: torch.Tensor) -> torch.Tensor:
     return (torch.nn.functional.silu(g) * u) @ sd[p + "mlp.w_down.weight"].t()
 
 
-def block(sd, i: int, x, cfg: Cfg, cos, sin, positions, kv):
+def block(sd, i: int, x, cfg: Cfg, cos, sin, positions, kv, attn_core=None):
     p = f"layers.{i}."
-    x = x + attention(sd, p, rms_norm(x, sd[p + "attn_norm.weight"], cfg.norm_eps), cfg, cos, sin, positions, kv)
+    x = x + attention(sd, p, rms_norm(x, sd[p + "attn_norm.weight"], cfg.norm_eps), cfg, cos, sin, positions, kv,
+                      attn_core)
     return x + swiglu(sd, p, rms_norm(x, sd[p + "mlp_norm.weight"], cfg.norm_eps))
 
 
@@ -153,19 +164,21 @@ def head(sd, x, cfg: Cfg):
 
 
 def model_forward(sd: Dict[str, torch.Tensor], cfg: Cfg, idx: torch.Tensor, positions: Optional[torch.Tensor] = None,
-                  kv: Optional[List] = None, layers: Optional[range] = None) -> torch.Tensor:
-    """Single-process forward: idx (B, T) -> logits (B, T, V)."""
+                  kv: Optional[List] = None, layers: Optional[range] = None, attn_core=None) -> torch.Tensor:
+    """Single-process forward: idx (B, T) -> logits (B, T, V), on idx's device (the reference's model is
+    device-agnostic: its positions follow idx.device, model.py:153, and its RoPE buffers move with it)."""
     b, t = idx.shape
-    cos, sin = rope_tables(cfg.head_dim, cfg.max_seq_len, cfg.rope_theta)
+    cos, sin = (x.to(idx.device) for x in rope_tables(cfg.head_dim, cfg.max_seq_len, cfg.rope_theta))
     if kv is None:
         kv = [ContiguousCache() for _ in range(cfg.n_layers)]
     if positions is None:
-        positions = (kv[0].length + torch.arange(t))[None, :].expand(b, t)
+        positions = (kv[0].length + torch.arange(t, device=idx.device))[None, :].expand(b, t)
+    positions = positions.to(idx.device)
     if int(positions.max()) >= cfg.max_seq_len:
         raise ValueError("position exceeds max_seq_len")
     x = sd["tok_emb.weight"][idx]
     for i in (layers if layers is not None else range(cfg.n_layers)):
-        x = block(sd, i, x, cfg, cos, sin, positions, kv[i])
+        x = block(sd, i, x, cfg, cos, sin, positions, kv[i], attn_core)
     return head(sd, x, cfg)
 
 
@@ -267,15 +280,15 @@ def pipeline_forward(sd, sim: PipelineSim, idx: torch.Tensor, t: int) -> torch.T
     return torch.cat(outs, dim=0)
 
 
-def greedy_generate(sd, cfg: Cfg, prompt: torch.Tensor, max_new_tokens: int) -> torch.Tensor:
+def greedy_generate(sd, cfg: Cfg, prompt: torch.Tensor, max_new_tokens: int, attn_core=None) -> torch.Tensor:
     kv = [ContiguousCache() for _ in range(cfg.n_layers)]
     max_new_tokens = min(max_new_tokens, cfg.max_seq_len - prompt.shape[1])
     out = prompt
-    logits = model_forward(sd, cfg, prompt, kv=kv)
+    logits = model_forward(sd, cfg, prompt, kv=kv, attn_core=attn_core)
     for _ in range(max_new_tokens):
         nxt = logits[:, -1].argmax(-1)[:, None]
         out = torch.cat([out, nxt], dim=1)
-        logits = model_forward(sd, cfg, nxt, kv=kv)
+        logits = model_forward(sd, cfg, nxt, kv=kv, attn_core=attn_core)
     return out
 
 

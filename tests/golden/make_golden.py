@@ -238,7 +238,42 @@ def c1_fixture():
             "generate": generate(model, prompt, 8), "pipeline_generate": gen[0]}
 
 
-FIXTURES = {"small": small_fixture, "c1": c1_fixture, "tp": tp_fixture}
+PP8 = dict(vocab_size=2048, d_model=512, n_layers=8, n_heads=4, n_kv_heads=2, max_seq_len=544)
+PP8_POSITIONS = [0, 1, 127, 128, 255, 256, 300, 383, 384, 511]
+
+
+def pp8_fixture():
+    """A head_dim-128 model that splits into 1, 2, 4 or 8 pipeline stages (8 layers) with a vocab of 8 head tiles of
+    256 (one per stage at 8). The multi-GPU bench checks its own NCCL pipeline against these before timing; the
+    reference's pipeline matches its single-process model within 1e-4 (its tests/test_pipeline.py:44-68), so the
+    single-process outputs are what a pipeline of any depth must give.
+    fp32: the reference test suite's randn recipe at scale 0.05 (greedy tokens vary; fp32 rounding stays near
+    2e-5, inside the 1e-4 bar, where 0.25 reaches 2.4e-4 at this depth), logits at positions that
+    straddle 128-token boundaries (where sequence pieces start) for 8 rows x 512 tokens, and 16 greedy tokens.
+    bf16: the same recipe at scale 0.02, the reference's module in bf16 on the CPU, logits at the same positions."""
+    cfg = ModelConfig(**PP8)
+    model = ForgeModel(cfg).eval()
+    model.load_state_dict(O.test_model_weights(O.Cfg(**PP8), seed=4321, scale=0.05))
+    sd = {k: v.detach().clone() for k, v in model.state_dict().items()}
+    idx = torch.randint(0, PP8["vocab_size"], (8, 512), generator=torch.Generator().manual_seed(31))
+    pos = torch.tensor(PP8_POSITIONS)
+    logits = model(idx)[:, pos]
+    prompt = torch.randint(0, PP8["vocab_size"], (8, 32), generator=torch.Generator().manual_seed(32))
+    m16 = ForgeModel(cfg).eval()
+    sd16 = O.test_model_weights(O.Cfg(**PP8), seed=4321, scale=0.02)
+    m16.load_state_dict(sd16)
+    bf16_logits = m16.to(torch.bfloat16)(idx)[:, pos]
+    # the spread between two bf16 renderings of the reference's module (its own attention call, and the oracle's
+    # written-out fp32 softmax rounded to bf16): a bf16 implementation is held to this (or 2e-2 if larger)
+    o16 = O.model_forward({k: v.bfloat16() for k, v in sd16.items()}, O.Cfg(**PP8), idx)[:, pos]
+    spread = O.log_softmax_maxabs(o16, bf16_logits)
+    return {"cfg": PP8, "weights": ("test_model_weights", 4321, 0.05), "checksum": O.checksum(sd), "idx": idx,
+            "positions": pos, "logits": logits, "prompt": prompt, "generate": generate(model, prompt, 16),
+            "bf16_weights": ("test_model_weights", 4321, 0.02), "bf16_checksum": O.checksum(sd16),
+            "bf16_logits": bf16_logits, "bf16_spread": spread}
+
+
+FIXTURES = {"small": small_fixture, "c1": c1_fixture, "tp": tp_fixture, "pp8": pp8_fixture}
 
 if __name__ == "__main__":
     ap = argparse.ArgumentParser()

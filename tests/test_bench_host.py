@@ -47,3 +47,16 @@ def test_reference_arm_runs_config_2_on_the_host_cores():
     assert line["impl"] == "reference" and "1B-shape" in line["metric"] and line["value"] > 0
     assert line["config"]["seq_len"] == 1024 and line["config"]["microbatches"] == 8
     assert "1 of 16 layers" in line["cpu_baseline"]["sample"]
+
+
+def test_reference_arm_step_time_is_the_measured_sample():
+    """--impl reference: ms_per_step is the time one step of the sample actually took (so steps x ms_per_step fits
+    inside the run's wall time); the whole-model extrapolation behind `value` has its own field."""
+    res = subprocess.run([sys.executable, str(ROOT / "bench.py"), "--impl", "reference", "--workload", "c2",
+                          "--steps", "2", "--warmup", "1"], capture_output=True, text=True, timeout=600, cwd=ROOT)
+    assert res.returncode == 0, res.stderr
+    line = json.loads(res.stdout.strip().splitlines()[-1])
+    assert line["impl"] == "reference" and line["cpu_baseline"]["kind"] == "port"
+    assert line["ms_per_step"] * (line["steps"] + line["warmup"]) <= line["wall_s"] * 1e3
+    assert line["extrapolated_ms_per_row"] > line["ms_per_step"]
+    assert math.isclose(line["value"], 1024 / (line["extrapolated_ms_per_row"] / 1e3), rel_tol=1e-3)

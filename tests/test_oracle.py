@@ -175,3 +175,32 @@ def test_tensor_parallel_restatement(size):
     assert g["tp"][size]["all_reduces"] == 2 * 2 * cfg.n_layers      # two forwards, two per layer
     # the reference's shards give the single-process model's tokens
     assert torch.equal(g["tp"][size]["generate"], O.greedy_generate(sd, cfg, g["prompt"], 10))
+
+
+def test_reference_attention_call_matches_the_written_out_one_in_fp32():
+    """oracle.sdpa_torch (the reference's own scaled_dot_product_attention call, model.py:76) and the written-out
+    softmax give the reference's golden logits alike in fp32."""
+    g = torch.load(GOLDEN / "small.pt", weights_only=False)
+    cfg = O.Cfg(**g["cfg"])
+    sd = O.test_model_weights(cfg, *g["weights"][1:])
+    got = O.model_forward(sd, cfg, g["idx"], attn_core=O.sdpa_torch)
+    torch.testing.assert_close(got, g["logits"], atol=1e-4, rtol=1e-4)
+    assert torch.equal(O.greedy_generate(sd, cfg, g["prompt"], 10, attn_core=O.sdpa_torch), g["generate"])
+
+
+def test_pp8_fixture_weights_and_outputs():
+    """The multi-GPU bench's parity fixture: the product's restatement of the test suite's weight recipe gives the
+    recorded checksums, and the oracle reproduces the reference's fp32 logits and greedy tokens."""
+    from forgeserve_b200 import ModelConfig
+    from forgeserve_b200.weights import checksum, test_suite_state_dict
+    g = torch.load(GOLDEN / "pp8.pt", weights_only=False)
+    cfg = O.Cfg(**g["cfg"])
+    sd = test_suite_state_dict(ModelConfig(**g["cfg"]), *g["weights"][1:])
+    assert checksum(sd) == g["checksum"]
+    assert checksum(test_suite_state_dict(ModelConfig(**g["cfg"]), *g["bf16_weights"][1:])) == g["bf16_checksum"]
+    for k, v in O.test_model_weights(cfg, *g["weights"][1:]).items():
+        assert torch.equal(v, sd[k]), k
+    got = O.model_forward(sd, cfg, g["idx"])[:, g["positions"]]
+    torch.testing.assert_close(got, g["logits"], atol=1e-4, rtol=1e-4)
+    assert torch.equal(O.greedy_generate(sd, cfg, g["prompt"], 16), g["generate"])
+    assert 0 < g["bf16_spread"] < 0.05
