@@ -27,14 +27,20 @@ from .paged import PagedKVPool
 
 @dataclass
 class Request:
+    """One submitted sequence. The field names are the reference's (callers read `output`, `blocks`, `finished`).
+
+    blocks: the physical cache blocks this request owns, in sequence order; empty while it waits (never started,
+            or preempted and stripped of its blocks).
+    cached: how many of its tokens (prompt, then generated) already have their keys and values stored in those
+            blocks; the next token written goes to position `cached`."""
     id: int
     prompt: List[int]
     max_new_tokens: int
     eos_id: Optional[int] = None
     temperature: float = 0.0
     output: List[int] = field(default_factory=list)
-    blocks: List[int] = field(default_factory=list)    # block table while the request holds cache blocks
-    cached: int = 0                                     # tokens whose keys/values are in the cache
+    blocks: List[int] = field(default_factory=list)
+    cached: int = 0
     finished: bool = False
 
 
@@ -94,7 +100,8 @@ class Scheduler:
     # ---- scheduling ------------------------------------------------------------------------------------
     def _try_prefill(self) -> bool:
         req = self.waiting[0]
-        tokens = req.prompt + req.output             # after a preemption this includes earlier output
+        # a preempted request comes back with the tokens it already generated: they are re-encoded with the prompt
+        tokens = req.prompt + req.output
         need = self.pool.blocks_for(len(tokens))
         if need > self.pool.allocator.num_free:
             return False

@@ -116,6 +116,8 @@ class DistTransport:
         return _irecv(buf, src, self._group_with(src))
 
     def broadcast(self, t: torch.Tensor, src: int) -> None:
+        if not dist.is_initialized():      # a one-stage pipeline in a process without a group: t is already here
+            return
         _broadcast(t, src, self.group)
 
 
