@@ -776,6 +776,57 @@ def profile_case(name: str, reps: int, timed: bool = False):
                           "splits_workspace": L.load().fs_attention_decode_workspace(rows, nh, nkv, hd, W * bs)}))
         fn = lambda: ops.attention_decode(q, desc, W * bs, positions, out, rows, nh, nkv, hd)
         work = (kv_bytes + 2.0 * rows * nh * hd * 2, "B")  # K and V of every key, q in, o out
+    elif name == "decode_layer":       # one whole decode layer of the C4 batch (8 layers per CUDA graph replay)
+        import random
+        from forgeserve_b200 import ModelConfig
+        from forgeserve_b200.model import Block, RopeTables, layer_forward_
+        from forgeserve_b200.paged import PagedKVPool
+        from forgeserve_b200.weights import layer_shapes, seeded_tensor
+        rng = random.Random(0)
+        bs, rows, per_replay = 16, 64, 8
+        cfg = ModelConfig(**CFG)
+        lengths = [rng.randint(512, 4096) + 128 for _ in range(rows)]
+        widths = [-(-(n + 1) // bs) for n in lengths]
+        nblk = sum(widths) + 64
+        blocks = list(range(nblk))
+        rng.shuffle(blocks)
+        it = iter(blocks)
+        W = max(widths)
+        table = torch.tensor([[next(it) for _ in range(w)] + [0] * (W - w) for w in widths], device=dev)
+        pool = PagedKVPool(cfg, nblk, bs, dtype=torch.bfloat16, device=dev, n_layers=1)
+        pool.k[0].normal_(generator=g)
+        pool.v[0].normal_(generator=g)
+        blk = Block(cfg, device=dev, dtype=torch.bfloat16)
+        with torch.no_grad():
+            for pname, prm in blk.named_parameters():
+                full = "layers.0." + pname
+                prm.copy_(seeded_tensor(full, layer_shapes(cfg, 0)[full], 1234, 0.02, device=dev, dtype=prm.dtype))
+        positions = torch.tensor([[n] for n in lengths], device=dev)
+        view = pool.views(table, positions)[0]
+        cos, sin = RopeTables(cfg).on(dev)
+        x = rnd(rows, 1, d)
+        x0 = x.clone()
+
+        def layers():
+            for _ in range(per_replay):
+                layer_forward_(blk, x, positions, view, cos, sin)
+
+        cap = torch.cuda.Stream(dev)                      # warm-up on the capture stream: its per-stream GEMM
+        cap.wait_stream(torch.cuda.current_stream(dev))   # counters and workspaces exist before the capture
+        with torch.cuda.stream(cap):
+            layers()
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=cap):
+            layers()
+        x.copy_(x0)
+
+        def fn():
+            graph.replay()
+        weight_bytes = sum(prm.numel() * prm.element_size() for prm in blk.parameters())
+        kv_bytes = sum(n + 1 for n in lengths) * nkv * hd * 2 * 2
+        print(json.dumps({"decode_layer_weight_bytes": weight_bytes, "kv_bytes": kv_bytes, "layers_per_launch": 8}))
+        work = (per_replay * (weight_bytes + kv_bytes + 4.0 * rows * d * 2), "B")
     else:
         raise SystemExit(f"unknown profile case {name}")
     for _ in range(reps):

@@ -2,6 +2,7 @@
 #include <cudaTypedefs.h>
 
 #include <atomic>
+#include <cstdlib>
 #include <cstring>
 #include <string>
 
@@ -20,6 +21,14 @@ int fail(const std::string& msg) {
   set_last_error(msg);
   return -1;
 }
+bool pdl_enabled() {
+  static const bool on = [] {
+    const char* v = std::getenv("FORGESERVE_PDL");
+    return !(v && v[0] == '0');
+  }();
+  return on;
+}
+
 int check_launch(const char* what) {
   const cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return fail(std::string(what) + ": " + cudaGetErrorString(e));

@@ -71,6 +71,8 @@ __global__ void __launch_bounds__(THREADS)
     attn_decode_kernel(const T* __restrict__ q, int64_t ldq, KVCache kv, int64_t n_slots,
                        const int64_t* __restrict__ positions, T* __restrict__ out, int64_t ldo, int nh, int rep,
                        int splits, float scale, float* __restrict__ ws, unsigned* err) {
+  pdl_trigger();
+  pdl_wait();   // launched with PDL: everything below reads or writes other kernels' data
   using S = Smem<T, HD>;
   constexpr int VEC = 16 / static_cast<int>(sizeof(T));   // elements per 16-byte chunk
   constexpr int CPR = HD / VEC;                           // chunks per row
@@ -201,6 +203,8 @@ template <typename T, int HD>
 __global__ void __launch_bounds__(THREADS)
     attn_combine_kernel(const float* __restrict__ ws, int B, int nh, int splits, const int64_t* __restrict__ positions,
                         int64_t n_slots, T* __restrict__ out, int64_t ldo) {
+  pdl_trigger();
+  pdl_wait();   // launched with PDL: everything below reads or writes other kernels' data
   const int r = blockIdx.x, h = blockIdx.y, d = threadIdx.x;
   const int64_t base = (static_cast<int64_t>(r) * nh + h) * splits;
   const float* ml = ws + static_cast<int64_t>(B) * nh * splits * HD;
@@ -298,6 +302,8 @@ __device__ __forceinline__ uint32_t tile_addr(uint32_t base, int row, int chunk)
 template <int HD>
 __global__ void __launch_bounds__(THREADS_TC)
     attn_decode_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV, Params p) {
+  pdl_trigger();
+  pdl_wait();   // launched with PDL: everything below reads or writes other kernels' data
   using G = Geo<HD>;
   extern __shared__ uint8_t smem_raw[];
   __shared__ int abort_flag;
@@ -551,7 +557,7 @@ int launch_t(const void* q, int64_t ldq, const KVCache& kv, int64_t n_slots, con
     attr[dev] = true;
   }
   dim3 grid(static_cast<unsigned>(splits), static_cast<unsigned>(nkv), static_cast<unsigned>(B));
-  attn_decode_tc_kernel<HD><<<grid, THREADS_TC, G::SMEM, st>>>(mk, mv, p);
+  launch_pdl_async(attn_decode_tc_kernel<HD>, grid, THREADS_TC, G::SMEM, st, mk, mv, p);
   return check_launch("attn_decode_tc_kernel");
 }
 
@@ -572,7 +578,7 @@ int launch_t(const void* q, int64_t ldq, const KVCache& kv, int64_t n_slots, con
     attr[dev] = true;
   }
   dim3 grid(static_cast<unsigned>(splits), static_cast<unsigned>(nkv), static_cast<unsigned>(B));
-  attn_decode_kernel<T, HD><<<grid, THREADS, S::BYTES, st>>>(
+  launch_pdl_async(attn_decode_kernel<T, HD>, grid, THREADS, S::BYTES, st,
       static_cast<const T*>(q), ldq, kv, n_slots, positions, static_cast<T*>(out), ldo, static_cast<int>(nh),
       static_cast<int>(nh / nkv), splits, scale, ws, err);
   return check_launch("attn_decode_kernel");
@@ -581,7 +587,7 @@ int launch_t(const void* q, int64_t ldq, const KVCache& kv, int64_t n_slots, con
 template <typename T, int HD>
 int combine_t(float* ws, int64_t B, int64_t nh, int splits, const int64_t* positions, int64_t n_slots, void* out,
               int64_t ldo, cudaStream_t st) {
-  attn_combine_kernel<T, HD><<<dim3(static_cast<unsigned>(B), static_cast<unsigned>(nh)), THREADS, 0, st>>>(
+  launch_pdl_async(attn_combine_kernel<T, HD>, dim3(static_cast<unsigned>(B), static_cast<unsigned>(nh)), THREADS, 0, st,
       ws, static_cast<int>(B), static_cast<int>(nh), splits, positions, n_slots, static_cast<T*>(out), ldo);
   return check_launch("attn_combine_kernel");
 }

@@ -16,6 +16,7 @@
 
 #include <cstdio>
 #include <string>
+#include <utility>
 
 namespace fs {
 
@@ -35,6 +36,55 @@ unsigned* error_word();
 void set_last_error(const std::string& msg);
 int fail(const std::string& msg);                     // set_last_error + return -1
 int check_launch(const char* what);                   // cudaGetLastError -> status
+
+// Programmatic dependent launch (PDL). A kernel launched with launch_pdl() may start while the kernel before it on
+// the stream is still running: it must call pdl_wait() before its first access to any memory another kernel
+// writes (every read or write of activations, caches, counters, workspaces; only weights may be read before), and
+// it calls pdl_trigger() to let the kernel after it start early in turn. Launched without PDL, both are no-ops.
+// A kernel that allocates TMEM triggers only after its allocation, so that a dependent never holds TMEM that a
+// kernel it waits for still needs.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+bool pdl_enabled();   // FORGESERVE_PDL=0 turns programmatic launches off (for comparisons)
+
+// Launches `kernel` on `st`, with programmatic stream serialization when pdl_enabled(); the kernel must follow the
+// pdl_wait() rule above.
+template <typename... KArgs, typename... Args>
+int launch_pdl(const char* what, void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+               Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl_enabled() ? 1 : 0;
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+  if (e != cudaSuccess) return fail(std::string(what) + " launch: " + cudaGetErrorString(e));
+  return check_launch(what);
+}
+
+// The same launch where the caller checks it afterwards with check_launch() (a failed launch leaves its error for
+// cudaGetLastError, as a <<<>>> launch does).
+template <typename... KArgs, typename... Args>
+void launch_pdl_async(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl_enabled() ? 1 : 0;
+  (void)cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
+
 
 template <typename T> struct TypeOf;
 template <> struct TypeOf<float> { static constexpr int value = F32; };

@@ -26,6 +26,8 @@ template <typename T, int THREADS>
 __global__ void __launch_bounds__(THREADS)
     rmsnorm_kernel(const T* __restrict__ x, int64_t xs, const T* __restrict__ w, T* __restrict__ y, int64_t ys,
                    int dim, float eps) {
+  pdl_trigger();
+  pdl_wait();   // launched with PDL: everything below reads or writes other kernels' data
   const int64_t row = blockIdx.x;
   const T* xr = x + row * xs;
   T* yr = y + row * ys;
@@ -89,6 +91,8 @@ __global__ void rope_kv_kernel(T* __restrict__ qkv, int64_t ld, const float* __r
                                const float* __restrict__ sin_t, int rope_rows, const int64_t* __restrict__ positions,
                                KVCache kv, int T_new, int nh, int nkv, int hd, int64_t slot_base, int slot_from_pos,
                                int apply_rope, unsigned* err) {
+  pdl_trigger();
+  pdl_wait();   // launched with PDL: everything below reads or writes other kernels' data
   const int64_t tok = blockIdx.x;
   const int r = static_cast<int>(tok / T_new), j = static_cast<int>(tok % T_new);
   const int64_t pos = positions[tok];
@@ -146,6 +150,8 @@ __global__ void __launch_bounds__(128)
                        const float* __restrict__ sin_t, int rope_rows, const int64_t* __restrict__ positions,
                        KVCache kv, int T_new, int nh, int nkv, int hd, int64_t slot_base, int slot_from_pos,
                        unsigned* err) {
+  pdl_trigger();
+  pdl_wait();   // launched with PDL: everything below reads or writes other kernels' data
   using bf = __nv_bfloat16;
   const int64_t tok = blockIdx.x;
   const int r = static_cast<int>(tok / T_new), j = static_cast<int>(tok % T_new);
@@ -211,6 +217,8 @@ __global__ void __launch_bounds__(128)
 template <typename T>
 __global__ void kv_store_kernel(const T* __restrict__ k, const T* __restrict__ v, const int64_t* __restrict__ positions,
                                 KVCache kv, int T_new, int nkv, int hd, unsigned* err) {
+  pdl_trigger();
+  pdl_wait();   // launched with PDL: everything below reads or writes other kernels' data
   const int64_t tok = blockIdx.x;
   const int r = static_cast<int>(tok / T_new), j = static_cast<int>(tok % T_new);
   const int64_t slot = positions[tok];
@@ -236,6 +244,8 @@ __global__ void kv_store_kernel(const T* __restrict__ k, const T* __restrict__ v
 template <typename T>
 __global__ void paged_gather_kernel(const T* __restrict__ pool, const int64_t* __restrict__ table, int64_t nb,
                                     int64_t num_blocks, int nkv, int bs, int hd, T* __restrict__ out, unsigned* err) {
+  pdl_trigger();
+  pdl_wait();   // launched with PDL: everything below reads or writes other kernels' data
   // grid: (B * nb * nkv); each block copies one (row, table entry, head) = bs * hd values
   const int64_t id = blockIdx.x;
   const int g = static_cast<int>(id % nkv);
@@ -254,6 +264,8 @@ __global__ void paged_gather_kernel(const T* __restrict__ pool, const int64_t* _
 template <typename T>
 __global__ void embed_kernel(const int64_t* __restrict__ ids, const T* __restrict__ table, int64_t vocab, int dim,
                              T* __restrict__ out, unsigned* err) {
+  pdl_trigger();
+  pdl_wait();   // launched with PDL: everything below reads or writes other kernels' data
   const int64_t i = blockIdx.x;
   const int64_t id = ids[i];
   T* dst = out + i * dim;
@@ -284,6 +296,8 @@ __device__ __forceinline__ bool better(float a, int64_t ia, float b, int64_t ib)
 
 template <typename T>
 __global__ void argmax_kernel(const T* __restrict__ x, int64_t row_stride, int64_t n, int64_t* __restrict__ out) {
+  pdl_trigger();
+  pdl_wait();   // launched with PDL: everything below reads or writes other kernels' data
   const T* xr = x + static_cast<int64_t>(blockIdx.x) * row_stride;
   float best = -INFINITY;
   int64_t bi = INT64_MAX;
@@ -323,6 +337,8 @@ template <int VPL>
 __global__ void __launch_bounds__(256)
     rmsnorm_warp_kernel(const __nv_bfloat16* __restrict__ x, int64_t xs, const __nv_bfloat16* __restrict__ w,
                         __nv_bfloat16* __restrict__ y, int64_t ys, int64_t rows, float eps) {
+  pdl_trigger();
+  pdl_wait();   // launched with PDL: everything below reads or writes other kernels' data
   using bf = __nv_bfloat16;
   const int64_t row = static_cast<int64_t>(blockIdx.x) * 8 + (threadIdx.x >> 5);
   if (row >= rows) return;
@@ -360,7 +376,7 @@ __global__ void __launch_bounds__(256)
 template <int VPL>
 static void launch_rmsnorm_warp(const void* x, int64_t xs, const void* w, void* y, int64_t ys, int64_t rows, float eps,
                                 cudaStream_t st) {
-  rmsnorm_warp_kernel<VPL><<<static_cast<unsigned>((rows + 7) / 8), 256, 0, st>>>(
+  launch_pdl_async(rmsnorm_warp_kernel<VPL>, static_cast<unsigned>((rows + 7) / 8), 256, 0, st,
       static_cast<const __nv_bfloat16*>(x), xs, static_cast<const __nv_bfloat16*>(w), static_cast<__nv_bfloat16*>(y),
       ys, rows, eps);
 }
@@ -389,10 +405,10 @@ int rmsnorm(int dtype, const void* x, int64_t xs, const void* w, void* y, int64_
     }
   }
   if (dtype == F32)
-    rmsnorm_kernel<float, TH><<<static_cast<unsigned>(rows), TH, 0, st>>>(
+    launch_pdl_async(rmsnorm_kernel<float, TH>, static_cast<unsigned>(rows), TH, 0, st,
         static_cast<const float*>(x), xs, static_cast<const float*>(w), static_cast<float*>(y), ys, static_cast<int>(dim), eps);
   else if (dtype == BF16)
-    rmsnorm_kernel<__nv_bfloat16, TH><<<static_cast<unsigned>(rows), TH, 0, st>>>(
+    launch_pdl_async(rmsnorm_kernel<__nv_bfloat16, TH>, static_cast<unsigned>(rows), TH, 0, st,
         static_cast<const __nv_bfloat16*>(x), xs, static_cast<const __nv_bfloat16*>(w), static_cast<__nv_bfloat16*>(y), ys,
         static_cast<int>(dim), eps);
   else
@@ -413,18 +429,18 @@ int rope_kv_write(int dtype, void* qkv, int64_t ld, const float* cos_t, const fl
                    ((reinterpret_cast<uintptr_t>(qkv) | reinterpret_cast<uintptr_t>(kv.k) |
                      reinterpret_cast<uintptr_t>(kv.v)) & 15) == 0;
   if (vec) {
-    rope_kv_vec_kernel<<<static_cast<unsigned>(tokens), 128, 0, st>>>(
+    launch_pdl_async(rope_kv_vec_kernel, static_cast<unsigned>(tokens), 128, 0, st,
         static_cast<__nv_bfloat16*>(qkv), ld, cos_t, sin_t, static_cast<int>(rope_rows), positions, kv,
         static_cast<int>(T_new), static_cast<int>(nh), static_cast<int>(nkv), static_cast<int>(hd), slot_base,
         slot_from_pos, error_word());
     return check_launch("rope_kv_vec_kernel");
   }
   if (dtype == F32)
-    rope_kv_kernel<float><<<static_cast<unsigned>(tokens), th, 0, st>>>(
+    launch_pdl_async(rope_kv_kernel<float>, static_cast<unsigned>(tokens), th, 0, st,
         static_cast<float*>(qkv), ld, cos_t, sin_t, static_cast<int>(rope_rows), positions, kv, static_cast<int>(T_new),
         static_cast<int>(nh), static_cast<int>(nkv), static_cast<int>(hd), slot_base, slot_from_pos, apply_rope, error_word());
   else if (dtype == BF16)
-    rope_kv_kernel<__nv_bfloat16><<<static_cast<unsigned>(tokens), th, 0, st>>>(
+    launch_pdl_async(rope_kv_kernel<__nv_bfloat16>, static_cast<unsigned>(tokens), th, 0, st,
         static_cast<__nv_bfloat16*>(qkv), ld, cos_t, sin_t, static_cast<int>(rope_rows), positions, kv,
         static_cast<int>(T_new), static_cast<int>(nh), static_cast<int>(nkv), static_cast<int>(hd), slot_base,
         slot_from_pos, apply_rope, error_word());
@@ -439,11 +455,11 @@ int kv_store(int dtype, const void* k, const void* v, const int64_t* positions, 
   if (tokens <= 0) return 0;
   if (tokens > INT32_MAX) return fail("kv_store: too many tokens");
   if (dtype == F32)
-    kv_store_kernel<float><<<static_cast<unsigned>(tokens), 128, 0, st>>>(
+    launch_pdl_async(kv_store_kernel<float>, static_cast<unsigned>(tokens), 128, 0, st,
         static_cast<const float*>(k), static_cast<const float*>(v), positions, kv, static_cast<int>(T_new),
         static_cast<int>(nkv), static_cast<int>(hd), error_word());
   else if (dtype == BF16)
-    kv_store_kernel<__nv_bfloat16><<<static_cast<unsigned>(tokens), 128, 0, st>>>(
+    launch_pdl_async(kv_store_kernel<__nv_bfloat16>, static_cast<unsigned>(tokens), 128, 0, st,
         static_cast<const __nv_bfloat16*>(k), static_cast<const __nv_bfloat16*>(v), positions, kv,
         static_cast<int>(T_new), static_cast<int>(nkv), static_cast<int>(hd), error_word());
   else
@@ -457,11 +473,11 @@ int paged_gather(int dtype, const void* pool, const int64_t* table, int64_t B, i
   if (n <= 0) return 0;
   if (n > INT32_MAX) return fail("paged_gather: too large");
   if (dtype == F32)
-    paged_gather_kernel<float><<<static_cast<unsigned>(n), 128, 0, st>>>(
+    launch_pdl_async(paged_gather_kernel<float>, static_cast<unsigned>(n), 128, 0, st,
         static_cast<const float*>(pool), table, nb, num_blocks, static_cast<int>(nkv), static_cast<int>(bs),
         static_cast<int>(hd), static_cast<float*>(out), error_word());
   else if (dtype == BF16)
-    paged_gather_kernel<__nv_bfloat16><<<static_cast<unsigned>(n), 128, 0, st>>>(
+    launch_pdl_async(paged_gather_kernel<__nv_bfloat16>, static_cast<unsigned>(n), 128, 0, st,
         static_cast<const __nv_bfloat16*>(pool), table, nb, num_blocks, static_cast<int>(nkv), static_cast<int>(bs),
         static_cast<int>(hd), static_cast<__nv_bfloat16*>(out), error_word());
   else
@@ -474,10 +490,10 @@ int embed(int dtype, const int64_t* ids, int64_t n, const void* table, int64_t v
   if (n <= 0) return 0;
   if (n > INT32_MAX) return fail("embed: too many ids");
   if (dtype == F32)
-    embed_kernel<float><<<static_cast<unsigned>(n), 128, 0, st>>>(ids, static_cast<const float*>(table), vocab,
+    launch_pdl_async(embed_kernel<float>, static_cast<unsigned>(n), 128, 0, st, ids, static_cast<const float*>(table), vocab,
                                                                    static_cast<int>(dim), static_cast<float*>(out), error_word());
   else if (dtype == BF16)
-    embed_kernel<__nv_bfloat16><<<static_cast<unsigned>(n), 128, 0, st>>>(
+    launch_pdl_async(embed_kernel<__nv_bfloat16>, static_cast<unsigned>(n), 128, 0, st,
         ids, static_cast<const __nv_bfloat16*>(table), vocab, static_cast<int>(dim), static_cast<__nv_bfloat16*>(out),
         error_word());
   else
@@ -490,9 +506,9 @@ int argmax(int dtype, const void* x, int64_t rows, int64_t n, int64_t row_stride
   if (n <= 0) return fail("argmax: empty rows");
   if (rows > INT32_MAX) return fail("argmax: too many rows");
   if (dtype == F32)
-    argmax_kernel<float><<<static_cast<unsigned>(rows), 1024, 0, st>>>(static_cast<const float*>(x), row_stride, n, out);
+    launch_pdl_async(argmax_kernel<float>, static_cast<unsigned>(rows), 1024, 0, st, static_cast<const float*>(x), row_stride, n, out);
   else if (dtype == BF16)
-    argmax_kernel<__nv_bfloat16><<<static_cast<unsigned>(rows), 1024, 0, st>>>(static_cast<const __nv_bfloat16*>(x),
+    launch_pdl_async(argmax_kernel<__nv_bfloat16>, static_cast<unsigned>(rows), 1024, 0, st, static_cast<const __nv_bfloat16*>(x),
                                                                                row_stride, n, out);
   else
     return fail("argmax: unsupported dtype");

@@ -18,6 +18,7 @@
 //   warps 4-7   epilogue: tcgen05.ld 32 lanes x 32 columns, fused epilogue, vector stores to global memory
 // The two TMEM accumulators let the epilogue of one tile overlap the main loop of the next.
 // No TMA multicast is used anywhere (the kernel also runs in multi-GPU jobs).
+#include <cstdlib>
 #include <map>
 #include <mutex>
 #include <utility>
@@ -58,10 +59,11 @@ struct Params {
   int num_m_blocks, num_tiles, k_blocks;
   int sys_fence;   // C may be another GPU's memory: end every epilogue thread with a system-scope fence
   unsigned* sched; // 1-SM kernel: [next tile, CTAs finished], zero at launch; the last CTA to finish re-zeroes it
-  // Split K (1-SM kernel, one m-block): work unit u = (tile u / k_split, K chunk u % k_split of kb_per k-blocks);
-  // each unit stores its fp32 partial of the B rows it covers to ws[(chunk * M + row) * ldw + B row], and
-  // splitk_reduce_kernel applies the epilogue to the sums. k_split = 1: whole K, fused epilogue.
-  int k_split, kb_per;
+  // Split K (1-SM kernel, one m-block): work unit u = (tile u / k_split, K chunk c = u % k_split), chunk c covering
+  // k-blocks [c * k_blocks / k_split, (c + 1) * k_blocks / k_split) (sizes differ by one at most); each unit stores
+  // its fp32 partial of the B rows it covers to ws[(chunk * M + row) * ldw + B row], and splitk_reduce_kernel
+  // applies the epilogue to the sums. k_split = 1: whole K, fused epilogue.
+  int k_split;
   float* ws;
   int64_t ldw;
   unsigned* err;
@@ -232,6 +234,8 @@ template <int EPI>
 __global__ void __launch_bounds__(256)
     splitk_reduce_kernel(const float* __restrict__ ws, int64_t ldw, int k_split, int M, int n_out,
                          __nv_bfloat16* __restrict__ C, int64_t ldc, const __nv_bfloat16* __restrict__ R, int64_t ldr) {
+  pdl_trigger();
+  pdl_wait();
   const int64_t total = static_cast<int64_t>(M) * n_out;
   const int64_t plane = static_cast<int64_t>(M) * ldw;
   for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
@@ -262,6 +266,8 @@ template <int EPI>
 __global__ void __launch_bounds__(256)
     splitk_reduce_vec_kernel(const float* __restrict__ ws, int64_t ldw, int k_split, int M, int n_out,
                              __nv_bfloat16* C, int64_t ldc, const __nv_bfloat16* R, int64_t ldr) {
+  pdl_trigger();
+  pdl_wait();
   const int row = blockIdx.y;
   const int j = (blockIdx.x * 256 + threadIdx.x) * 4;
   if (j >= n_out) return;
@@ -354,11 +360,13 @@ __global__ void __launch_bounds__(THREADS, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  pdl_trigger();   // TMEM is held: the next kernel on the stream may start its own set-up
 
-  // Tiles are claimed at run time from a counter shared by the grid, in increasing order (M fastest), so a CTA
-  // slowed down by other work on its SM (a resident NCCL kernel) takes fewer tiles instead of holding the whole
-  // GEMM back. The producer claims; the tile queue hands each claim (or -1: no tiles left) to the MMA thread and
-  // the epilogue warps.
+  // The first unit of every CTA is its own index, so that (launched with PDL) its weight loads can start while the
+  // kernel before it still runs; everything else waits for that kernel (pdl_wait). Later units are claimed at run
+  // time from a counter shared by the grid, in increasing order (M fastest), so a CTA slowed down by other work on
+  // its SM (a resident NCCL kernel) takes fewer units instead of holding the whole GEMM back. The producer claims;
+  // the tile queue hands each unit (or -1: none left) to the MMA thread and the epilogue warps.
   if (warp == 0) {
     // ------------------------------------------------------------------ TMA producer
     if (lane == 0) {
@@ -368,6 +376,44 @@ __global__ void __launch_bounds__(THREADS, 1)
       uint32_t last_ph[STAGES];
 #pragma unroll
       for (int i = 0; i < STAGES; ++i) issued[i] = false, last_ph[i] = 0;
+      const int total = p.num_tiles * p.k_split;
+      const int first = static_cast<int>(blockIdx.x) < total ? static_cast<int>(blockIdx.x) : -1;
+      auto unit_coords = [&](int unit, int& kb0, int& kb1, int& m_blk, int& b_row0, int& b_row1) {
+        const int tile = unit / p.k_split, chunk = unit % p.k_split;
+        kb0 = chunk * p.k_blocks / p.k_split;
+        kb1 = (chunk + 1) * p.k_blocks / p.k_split;
+        int n_blk;
+        tile_coords(tile, p.num_m_blocks, p.num_tiles / p.num_m_blocks, m_blk, n_blk);
+        b_row0 = EPI == EPI_SWIGLU ? n_blk * (BN / 2) : n_blk * BN;
+        b_row1 = EPI == EPI_SWIGLU ? p.n_out + n_blk * (BN / 2) : n_blk * BN + BN / 2;
+      };
+      // Weights of the first unit's first k-blocks (the ring is fresh: stage i, phase 0), before the wait.
+      int pre = 0;
+      if (first >= 0) {
+        int kb0, kb1, m_blk, b_row0, b_row1;
+        unit_coords(first, kb0, kb1, m_blk, b_row0, b_row1);
+        for (int kb = kb0; kb < kb1 && pre < STAGES; ++kb, ++pre) {
+          mbar_arrive_expect_tx(&full[pre], STAGE_BYTES);
+#pragma unroll
+          for (int pk = 0; pk < KP1; ++pk) {
+            const int kx = (kb * KP1 + pk) * BK;
+            uint8_t* st = tiles + pre * STAGE_BYTES;
+            tma_load_2d(st + KP1 * A_BYTES + pk * B_BYTES, &tmB, &full[pre], kx, b_row0);
+            tma_load_2d(st + KP1 * A_BYTES + pk * B_BYTES + BH_BYTES, &tmB, &full[pre], kx, b_row1);
+          }
+          issued[pre] = true;
+        }
+      }
+      pdl_wait();
+      if (pre > 0) {   // ... and then the activations of those k-blocks, so that no stage is ever left half-issued
+        int kb0, kb1, m_blk, b_row0, b_row1;
+        unit_coords(first, kb0, kb1, m_blk, b_row0, b_row1);
+        for (int j = 0; j < pre; ++j)
+#pragma unroll
+          for (int pk = 0; pk < KP1; ++pk)
+            tma_load_2d(tiles + j * STAGE_BYTES + pk * A_BYTES, &tmA, &full[j], ((kb0 + j) * KP1 + pk) * BK,
+                        m_blk * BM);
+      }
       bool ok = true;
       for (int i = 0; ok; ++i) {
         const int slot = i & (TQ - 1);
@@ -375,30 +421,31 @@ __global__ void __launch_bounds__(THREADS, 1)
           ok = false;
           break;
         }
-        int unit = static_cast<int>(atomicAdd(p.sched, 1u));
-        if (unit >= p.num_tiles * p.k_split) unit = -1;
+        int unit = first;
+        if (i > 0) {
+          unit = static_cast<int>(gridDim.x + atomicAdd(p.sched, 1u));
+          if (unit >= total) unit = -1;
+        }
         tq[slot] = unit;
         mbar_arrive(&tq_full[slot]);
         if (unit < 0) break;
-        const int tile = unit / p.k_split, kb0 = (unit % p.k_split) * p.kb_per;
-        const int kb1 = kb0 + p.kb_per < p.k_blocks ? kb0 + p.kb_per : p.k_blocks;
-        int m_blk, n_blk;
-        tile_coords(tile, p.num_m_blocks, p.num_tiles / p.num_m_blocks, m_blk, n_blk);
-        const int b_row0 = EPI == EPI_SWIGLU ? n_blk * (BN / 2) : n_blk * BN;
-        const int b_row1 = EPI == EPI_SWIGLU ? p.n_out + n_blk * (BN / 2) : n_blk * BN + BN / 2;
+        int kb0, kb1, m_blk, b_row0, b_row1;
+        unit_coords(unit, kb0, kb1, m_blk, b_row0, b_row1);
         for (int kb = kb0; kb < kb1; ++kb) {
-          if (!mbar_wait(&empty[s], ph ^ 1u, p.err) || *abort_flag) {
-            ok = false;
-            break;
-          }
-          mbar_arrive_expect_tx(&full[s], STAGE_BYTES);
+          if (!(i == 0 && kb - kb0 < pre)) {   // (the first `pre` k-blocks of the first unit are issued already)
+            if (!mbar_wait(&empty[s], ph ^ 1u, p.err) || *abort_flag) {
+              ok = false;
+              break;
+            }
+            mbar_arrive_expect_tx(&full[s], STAGE_BYTES);
 #pragma unroll
-          for (int pk = 0; pk < KP1; ++pk) {
-            const int kx = (kb * KP1 + pk) * BK;
-            uint8_t* st = tiles + s * STAGE_BYTES;
-            tma_load_2d(st + pk * A_BYTES, &tmA, &full[s], kx, m_blk * BM);
-            tma_load_2d(st + KP1 * A_BYTES + pk * B_BYTES, &tmB, &full[s], kx, b_row0);
-            tma_load_2d(st + KP1 * A_BYTES + pk * B_BYTES + BH_BYTES, &tmB, &full[s], kx, b_row1);
+            for (int pk = 0; pk < KP1; ++pk) {
+              const int kx = (kb * KP1 + pk) * BK;
+              uint8_t* st = tiles + s * STAGE_BYTES;
+              tma_load_2d(st + pk * A_BYTES, &tmA, &full[s], kx, m_blk * BM);
+              tma_load_2d(st + KP1 * A_BYTES + pk * B_BYTES, &tmB, &full[s], kx, b_row0);
+              tma_load_2d(st + KP1 * A_BYTES + pk * B_BYTES + BH_BYTES, &tmB, &full[s], kx, b_row1);
+            }
           }
           issued[s] = true;
           last_ph[s] = ph;
@@ -427,8 +474,8 @@ __global__ void __launch_bounds__(THREADS, 1)
         const int unit = tq[slot];
         mbar_arrive(&tq_empty[slot]);
         if (unit < 0) break;
-        const int kb0 = (unit % p.k_split) * p.kb_per;
-        const int kb1 = kb0 + p.kb_per < p.k_blocks ? kb0 + p.kb_per : p.k_blocks;
+        const int chunk = unit % p.k_split;
+        const int kb0 = chunk * p.k_blocks / p.k_split, kb1 = (chunk + 1) * p.k_blocks / p.k_split;
         if (!mbar_wait(&tempty[acc], acc_ph ^ 1u, p.err) || *abort_flag) {
           ok = false;
           break;
@@ -467,6 +514,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     const int q = warp - 4;  // this warp may read TMEM lanes 32q .. 32q+31
     const bool vec_ok = ((p.ldc & 7) == 0) && ((reinterpret_cast<uintptr_t>(p.C) & 15) == 0) &&
                         (EPI != EPI_RESIDUAL || (((p.ldr & 7) == 0) && ((reinterpret_cast<uintptr_t>(p.R) & 15) == 0)));
+    pdl_wait();   // C, R and the split-K workspace belong to the kernels before this one until they complete
     int acc = 0;
     uint32_t acc_ph = 0;
     for (int i = 0;; ++i) {
@@ -880,8 +928,7 @@ static int launch_t(const CUtensorMap& ma, const CUtensorMap& mb, const Params& 
       return check_launch("gemm_tc set smem");
     attr_set[dev] = true;
   }
-  gemm_tc_kernel<EPI><<<grid, THREADS, SMEM_BYTES, st>>>(ma, mb, p);
-  return check_launch("gemm_tc_kernel");
+  return launch_pdl("gemm_tc_kernel", gemm_tc_kernel<EPI>, dim3(grid), dim3(THREADS), SMEM_BYTES, st, ma, mb, p);
 }
 
 template <int EPI>
@@ -967,16 +1014,55 @@ static int launch_reduce_t(const Params& p, int64_t M, int64_t n_out, cudaStream
                    (EPI != EPI_RESIDUAL || (p.ldr % 4 == 0 && (reinterpret_cast<uintptr_t>(p.R) & 7) == 0));
   if (vec && M <= 65535) {
     const dim3 grid(static_cast<unsigned>((n_out / 4 + 255) / 256), static_cast<unsigned>(M));
-    splitk_reduce_vec_kernel<EPI><<<grid, 256, 0, st>>>(p.ws, p.ldw, p.k_split, static_cast<int>(M),
-                                                       static_cast<int>(n_out), p.C, p.ldc, p.R, p.ldr);
-    return check_launch("splitk_reduce_vec_kernel");
+    return launch_pdl("splitk_reduce_vec_kernel", splitk_reduce_vec_kernel<EPI>, grid, dim3(256), 0, st,
+                      static_cast<const float*>(p.ws), p.ldw, p.k_split, static_cast<int>(M), static_cast<int>(n_out),
+                      p.C, p.ldc, static_cast<const __nv_bfloat16*>(p.R), p.ldr);
   }
   const int64_t total = M * n_out;
   int64_t blocks = (total + 255) / 256;
   if (blocks > 4 * sm_count()) blocks = 4 * sm_count();
-  splitk_reduce_kernel<EPI><<<static_cast<unsigned>(blocks), 256, 0, st>>>(
-      p.ws, p.ldw, p.k_split, static_cast<int>(M), static_cast<int>(n_out), p.C, p.ldc, p.R, p.ldr);
-  return check_launch("splitk_reduce_kernel");
+  return launch_pdl("splitk_reduce_kernel", splitk_reduce_kernel<EPI>, dim3(static_cast<unsigned>(blocks)), dim3(256), 0,
+                    st, static_cast<const float*>(p.ws), p.ldw, p.k_split, static_cast<int>(M),
+                    static_cast<int>(n_out), p.C, p.ldc, static_cast<const __nv_bfloat16*>(p.R), p.ldr);
+}
+
+// K split of a GEMM with one m-block (M <= 128 rows: decode steps). Such a GEMM streams the weights once and is
+// HBM-bound, and one CTA streams well below its share of HBM bandwidth (a 4-stage ring of 48 KB), so the split keeps
+// every persistent CTA streaming: the smallest split whose units fill the waves of `sms` CTAs to at least 90 %
+// (units / (waves x sms)), else the one that fills them best. FORGESERVE_DECODE_SPLIT=wave instead takes the smallest
+// split that keeps 60 % of the CTAs busy in one wave (fewer fp32 partials; for comparisons). Chunks keep at least
+// KB_MIN k-blocks (64 of K each). The split depends on the weight shape and the SM budget only, not on M: rows get
+// the same sums whatever the batch (eager, graph-captured or micro-batched decode steps).
+static bool split_one_wave() {
+  static const bool w = [] {
+    const char* v = std::getenv("FORGESERVE_DECODE_SPLIT");
+    return v && std::string(v) == "wave";
+  }();
+  return w;
+}
+
+int choose_k_split(int tiles, int k_blocks, int sms) {
+  constexpr int KB_MIN = 6;
+  if (sms <= 0 || tiles >= sms || k_blocks < 2 * KB_MIN) return 1;
+  int best = 1;
+  if (split_one_wave()) {
+    for (int split = 1; split <= k_blocks / KB_MIN; ++split) {
+      const int units = tiles * split;
+      if (units > sms) break;
+      best = split;
+      if (units >= 0.6 * sms) break;
+    }
+    return best;
+  }
+  double best_fill = 0.0;
+  for (int split = 1; split <= k_blocks / KB_MIN; ++split) {
+    const int units = tiles * split;
+    const int waves = (units + sms - 1) / sms;
+    const double fill = static_cast<double>(units) / (static_cast<double>(waves) * sms);
+    if (fill >= 0.9) return split;
+    if (fill > best_fill + 1e-9) best = split, best_fill = fill;
+  }
+  return best;
 }
 
 static int g_pair_mode = 1;   // 1: use the 2-SM kernel for M > 128; 0: always the 1-SM kernel
@@ -1008,7 +1094,6 @@ int gemm_tc(const void* A, int64_t lda, const void* B, int64_t ldb, void* C, int
   p.sys_fence = sys_fence ? 1 : 0;
   p.sched = nullptr;
   p.k_split = 1;
-  p.kb_per = p.k_blocks;
   p.ws = nullptr;
   p.ldw = 0;
   p.err = error_word();
@@ -1030,24 +1115,15 @@ int gemm_tc(const void* A, int64_t lda, const void* B, int64_t ldb, void* C, int
   p.sched = sched_counter(stream);
   if (!p.sched) return -1;
   const int sms = sm_count();
-  // Few rows (a decode step): with one m-block there are fewer tiles than SMs, so fewer CTAs than SMs would
-  // stream the weights. Split K into chunks of at least KB_MIN k-blocks until there are ~2 units per CTA; the
-  // partial sums (M rows x the tile's columns, fp32) are small next to the weight bytes.
-  constexpr int KB_MIN = 8;
-  if (!sys_fence && p.num_m_blocks == 1 && p.num_tiles < sms && p.k_blocks >= 2 * KB_MIN) {
-    int split = (2 * sms + p.num_tiles - 1) / p.num_tiles;
-    if (split > p.k_blocks / KB_MIN) split = p.k_blocks / KB_MIN;
-    if (split >= 2) {
-      p.kb_per = (p.k_blocks + split - 1) / split;
-      split = (p.k_blocks + p.kb_per - 1) / p.kb_per;
-      const int64_t n_b = epi == EPI_SWIGLU ? 2 * n_out : n_out;
-      p.ldw = (n_b + 3) / 4 * 4;
-      p.ws = splitk_workspace(stream, static_cast<int64_t>(split) * M * p.ldw * static_cast<int64_t>(sizeof(float)));
-      if (!p.ws) return -1;
-      p.k_split = split;
-    } else {
-      p.kb_per = p.k_blocks;
-    }
+  // Few rows (a decode step): with one m-block there are few tiles, and the GEMM streams the weights; the time is
+  // set by how evenly the SMs share them. Split K so that the units fill whole waves of the persistent grid.
+  const int split = p.num_m_blocks == 1 && !sys_fence ? choose_k_split(p.num_tiles, p.k_blocks, sms) : 1;
+  if (split >= 2) {
+    const int64_t n_b = epi == EPI_SWIGLU ? 2 * n_out : n_out;
+    p.ldw = (n_b + 3) / 4 * 4;
+    p.ws = splitk_workspace(stream, static_cast<int64_t>(split) * M * p.ldw * static_cast<int64_t>(sizeof(float)));
+    if (!p.ws) return -1;
+    p.k_split = split;
   }
   const int units = p.num_tiles * p.k_split;
   const int grid = units < sms ? units : sms;

@@ -275,6 +275,12 @@ class _DecodeGraph:
         self.stream = torch.cuda.Stream(dev)
         self.graph: Optional[torch.cuda.CUDAGraph] = None
         self.tokens: Optional[torch.Tensor] = None
+        # decode windows: per step of a window, its positions and block table (pinned, one slot per step, so that no
+        # slot is rewritten while its copy may still be pending) and its tokens on the device
+        self.ring: Optional[torch.Tensor] = None
+        self.wtok: Optional[torch.Tensor] = None
+        self.wtok_host: Optional[torch.Tensor] = None
+        self._w = 0
 
     def _step(self) -> torch.Tensor:
         from .model import layer_forward_
@@ -284,6 +290,59 @@ class _DecodeGraph:
         for layer, view in zip(m.layers, self.pool.views(self.tab, self.pos)):
             layer_forward_(layer, x, self.pos, view, cos, sin)
         return ops.argmax(m.head(x)[:, -1])
+
+    def _capture(self) -> torch.Tensor:
+        """First step of this row count: run it eagerly on the graph's stream, then capture the same work."""
+        out = self._step()
+        self.stream.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=self.stream):
+            self.tokens = self._step()
+        self.graph = g
+        return out
+
+    # ---- decode windows: several steps in a row with no host synchronisation between them
+    def begin_window(self, idx0: torch.Tensor, w: int) -> None:
+        """Start a window of w steps; idx0 (rows,) are the first step's token ids. Each later step takes its ids
+        from the previous step's argmax on the device."""
+        r, dev = self.rows, self.model.device
+        if self.ring is None or self.ring.shape[0] < w:
+            n = max(w, Engine.MAX_WINDOW)
+            self.ring = torch.zeros(n, r * (1 + self.width), dtype=torch.int64).pin_memory()
+            self.wtok = torch.empty(n, r, dtype=torch.int64, device=dev)
+            self.wtok_host = torch.empty(n, r, dtype=torch.int64).pin_memory()
+        self._w = w
+        self.host[:r].copy_(idx0.reshape(-1))
+        self.stream.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(self.stream):
+            self.idx.copy_(self.host[:r].view(r, 1), non_blocking=True)
+
+    def window_step(self, t: int, positions: torch.Tensor, tables: torch.Tensor) -> None:
+        """Enqueue step t of the window (its positions and block tables planned on the host)."""
+        r = self.rows
+        slot = self.ring[t]
+        slot.zero_()
+        slot[:r].copy_(positions.reshape(-1))
+        slot[r:].view(r, self.width)[:, : tables.shape[1]].copy_(tables)
+        with torch.cuda.stream(self.stream):
+            self.inp[r:].copy_(slot, non_blocking=True)
+            if t > 0:
+                self.idx.copy_(self.wtok[t - 1].view(r, 1))
+            if self.graph is None:
+                out = self._capture()
+            else:
+                self.graph.replay()
+                out = self.tokens
+            self.wtok[t].copy_(out)
+
+    def end_window(self) -> List[List[int]]:
+        """Wait for the window's steps; their tokens, step by step."""
+        w = self._w
+        with torch.cuda.stream(self.stream):
+            self.wtok_host[:w].copy_(self.wtok[:w], non_blocking=True)
+        self.stream.synchronize()
+        torch.cuda.current_stream(self.model.device).wait_stream(self.stream)
+        return self.wtok_host[:w].tolist()
 
     def run(self, idx: torch.Tensor, positions: torch.Tensor, tables: torch.Tensor) -> List[int]:
         r = self.rows
@@ -296,12 +355,7 @@ class _DecodeGraph:
         with torch.cuda.stream(self.stream):
             self.inp.copy_(self.host, non_blocking=True)
             if self.graph is None:
-                out = self._step()
-                self.stream.synchronize()
-                g = torch.cuda.CUDAGraph()
-                with torch.cuda.graph(g, stream=self.stream):
-                    self.tokens = self._step()
-                self.graph = g
+                out = self._capture()
             else:
                 self.graph.replay()
                 out = self.tokens
@@ -315,14 +369,17 @@ class Engine(Scheduler):
     """Continuous batching of one model on one GPU (forgeserve/engine.py:36-45).
 
     cuda_graphs=True (extra): decode steps whose rows are all greedy replay a captured CUDA graph per row count
-    (_DecodeGraph) instead of launching every kernel from Python; the tokens are the same. A tensor-parallel model
-    (its all-reduces run through torch.distributed) always launches eagerly.
+    (_DecodeGraph) instead of launching every kernel from Python; the tokens are the same. run() then also takes
+    decode windows (_decode_window): runs of greedy steps that the scheduler can plan ahead go to the GPU back to
+    back, without a host synchronisation per step. A tensor-parallel model (its all-reduces run through
+    torch.distributed) always launches eagerly and steps one at a time.
 
     Under tensor parallelism every shard runs the same Engine over its own model shard (model.tp): the pool holds
     the shard's KV heads, the logits are replicated, so every shard samples the same tokens (engine.py:36-45 with
     the TP model of model.py:112)."""
 
     MAX_GRAPHS = 4
+    MAX_WINDOW = 64     # decode steps per window: bounds what the host enqueues ahead of the GPU
 
     def __init__(self, model, num_blocks: int, block_size: int = 16, max_batch: int = 8, seed: int = 0,
                  cuda_graphs: bool = True):
@@ -330,18 +387,44 @@ class Engine(Scheduler):
         self.pool = PagedKVPool(self.cfg, num_blocks, block_size, tp=model.tp, dtype=model.dtype, device=model.device)
         self.cuda_graphs = cuda_graphs
         self._graphs: Dict[int, _DecodeGraph] = {}
+        self.windows = 0    # decode windows run (see _decode_window)
         self._init_scheduler(max_batch, seed)
+
+    def _graph(self, rows: int) -> "_DecodeGraph":
+        g = self._graphs.pop(rows, None)
+        if g is None:
+            if len(self._graphs) >= self.MAX_GRAPHS:
+                self._graphs.pop(next(iter(self._graphs)))
+            g = _DecodeGraph(self.model, self.pool, rows)
+        self._graphs[rows] = g
+        return g
 
     def _forward_rows(self, reqs, idx, positions, tables):
         if (self.cuda_graphs and self.pool.device.type == "cuda" and idx.shape[1] == 1 and self.model.tp.size == 1
                 and all(r.temperature == 0 for r in reqs)
                 and tables.shape[1] * self.pool.block_size <= self.cfg.max_seq_len + self.pool.block_size):
-            g = self._graphs.pop(idx.shape[0], None)
-            if g is None:
-                if len(self._graphs) >= self.MAX_GRAPHS:
-                    self._graphs.pop(next(iter(self._graphs)))
-                g = _DecodeGraph(self.model, self.pool, idx.shape[0])
-            self._graphs[idx.shape[0]] = g
-            return g.run(idx, positions, tables)
+            return self._graph(idx.shape[0]).run(idx, positions, tables)
         logits = self.model(idx, positions, self.pool.views(tables, positions), last_only=True)
         return self._sample_rows(logits[:, -1], reqs)
+
+    # ---- decode windows (extra): greedy steps planned ahead and replayed back to back ---------------------------
+    def _windowed(self) -> bool:
+        return self.cuda_graphs and self.pool.device.type == "cuda" and self.model.tp.size == 1
+
+    def _window_steps(self) -> int:
+        return min(super()._window_steps(), self.MAX_WINDOW)
+
+    def _decode_window(self, w: int) -> None:
+        """w decode steps of the running rows (all greedy, no eos: the scheduler's window, Scheduler._window_steps)
+        with no host synchronisation between them: the host plans step t + 1 (block grants, tables, positions)
+        while the GPU runs step t, each step's token ids come from the previous step's argmax on the device, and
+        the window's tokens are read back once at its end. Same outputs, tables and counters as stepping."""
+        self.windows += 1
+        rows = list(self.running)
+        cached = [r.cached for r in rows]
+        g = self._graph(len(rows))
+        g.begin_window(torch.tensor([r.output[-1] for r in rows]), w)
+        for t in range(w):
+            tables, positions = self._window_step(rows, cached, t, t == w - 1)
+            g.window_step(t, positions, tables)
+        self._window_end(rows, g.end_window())

@@ -78,6 +78,34 @@ def test_engine_bf16_matches_own_generate():
         assert agree >= 10, (out[rid], want)       # bf16: paged/batched and contiguous paths may flip a near-tie
 
 
+@pytest.mark.parametrize("num_blocks", [200, 12])
+def test_engine_decode_windows_equal_stepping(num_blocks):
+    """Engine.run() with decode windows (greedy steps replayed back to back, tokens fed on the device) gives the
+    same outputs, block usage and counters as stepping one step at a time, with and without preemptions."""
+    cfg = ModelConfig(vocab_size=512, d_model=256, n_layers=2, n_heads=2, n_kv_heads=1, max_seq_len=256)
+    torch.manual_seed(0)
+    m = ForgeModel(cfg, device="cuda").to(torch.bfloat16).eval()
+    g = torch.Generator().manual_seed(5)
+    for prm in m.parameters():
+        if prm.ndim >= 2:
+            prm.data.copy_((torch.randn(prm.shape, generator=g) * 0.1).to(prm.device, prm.dtype))
+    reqs = [(torch.randint(0, 512, (n,), generator=g).tolist(), k) for n, k in ((9, 40), (70, 25), (33, 60), (5, 50))]
+
+    def run(windows):
+        eng = Engine(m, num_blocks=num_blocks, block_size=16, max_batch=4)
+        if not windows:
+            eng._windowed = lambda: False
+        ids = [eng.add_request(p, k) for p, k in reqs]
+        out = eng.run()
+        return ([out[i] for i in ids], eng.steps, eng.preemptions, eng.peak_running, eng.peak_blocks,
+                eng.pool.allocator.num_free, eng.windows)
+
+    win, step = run(True), run(False)
+    assert win[:6] == step[:6]
+    assert win[6] > 0 and step[6] == 0
+    assert all(len(o) == k for o, (_, k) in zip(win[0], reqs))
+
+
 def pipeline_engine_worker(rank, size, cfg_dict, full_sd, requests, num_blocks, max_batch, microbatches, dtype):
     from forgeserve_b200 import PipelineEngine, PipelineStage
     cfg = ModelConfig(**cfg_dict)
