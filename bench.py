@@ -776,6 +776,32 @@ def profile_case(name: str, reps: int, timed: bool = False):
                           "splits_workspace": L.load().fs_attention_decode_workspace(rows, nh, nkv, hd, W * bs)}))
         fn = lambda: ops.attention_decode(q, desc, W * bs, positions, out, rows, nh, nkv, hd)
         work = (kv_bytes + 2.0 * rows * nh * hd * 2, "B")  # K and V of every key, q in, o out
+    elif name == "decode_projections":  # a decode layer's four projections back to back, 64 rows, 8 layers per replay
+        rows, per_replay = 64, 8
+        wqkv, wo = rnd((nh + 2 * nkv) * hd, d, scale=0.02), rnd(d, nh * hd, scale=0.02)
+        wgu, wd = rnd(2 * F, d, scale=0.02), rnd(d, F, scale=0.02)
+        x, h, a = rnd(rows, d), rnd(rows, d), rnd(rows, nh * hd)
+
+        def projections():
+            for _ in range(per_replay):
+                ops.linear(h, wqkv)
+                ops.linear(a, wo, L.FS_EPI_RESIDUAL, residual=x, out=x)
+                gg = ops.linear(h, wgu, L.FS_EPI_SWIGLU)
+                ops.linear(gg, wd, L.FS_EPI_RESIDUAL, residual=x, out=x)
+
+        cap = torch.cuda.Stream(dev)
+        cap.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(cap):
+            projections()
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=cap):
+            projections()
+
+        def fn():
+            graph.replay()
+        wbytes = sum(t.numel() * 2 for t in (wqkv, wo, wgu, wd))
+        work = (per_replay * wbytes, "B")
     elif name == "decode_layer":       # one whole decode layer of the C4 batch (8 layers per CUDA graph replay)
         import random
         from forgeserve_b200 import ModelConfig

@@ -305,12 +305,14 @@ _POS_CACHE: Dict[Tuple, torch.Tensor] = {}
 
 
 def _positions(start: int, t: int, rows: int, device) -> torch.Tensor:
+    """Positions start .. start + t - 1 for every row, made on the device (a copy from pageable host memory would
+    make the host wait for the stream, once per new decode step)."""
     key = (str(device), start, t, rows)
     p = _POS_CACHE.get(key)
     if p is None:
         if len(_POS_CACHE) > 256:
             _POS_CACHE.clear()
-        p = (start + torch.arange(t, dtype=torch.int64))[None, :].expand(rows, t).contiguous().to(device)
+        p = torch.arange(start, start + t, dtype=torch.int64, device=device)[None, :].expand(rows, t).contiguous()
         _POS_CACHE[key] = p
     return p
 

@@ -48,6 +48,10 @@ class PipelineEngine(Scheduler):
         self.overlap = overlap
         self.prefill_chunks = max(1, prefill_chunks)
         self.windows = 0          # decode windows taken by run()
+        # decode windows: each step's block tables and positions go to the device in one copy from a pinned slot of
+        # its own (a copy from pageable memory would make the host wait for the stream at every group)
+        self._ring: Optional[torch.Tensor] = None
+        self._ring_dev: Optional[torch.Tensor] = None
         self._init_scheduler(max_batch, seed)
 
     def _forward_rows(self, reqs: List[Request], idx: torch.Tensor, positions: torch.Tensor,
@@ -107,6 +111,23 @@ class PipelineEngine(Scheduler):
     def _window_steps(self) -> int:
         return min(super()._window_steps(), self.MAX_WINDOW)
 
+    def _plan_on_device(self, t: int, tables: torch.Tensor, positions: torch.Tensor):
+        """Step t's tables (R, width) and positions (R, 1) on the stage's device, through pinned slot t."""
+        if self.stage.device.type != "cuda":
+            return tables, positions
+        R, width = tables.shape
+        cap = -(-self.cfg.max_seq_len // self.pool.block_size) + 1
+        n = R * (1 + cap)
+        if self._ring is None or self._ring.shape[1] < n:
+            self._ring = torch.zeros(self.MAX_WINDOW, n, dtype=torch.int64).pin_memory()
+            self._ring_dev = torch.zeros(self.MAX_WINDOW, n, dtype=torch.int64, device=self.stage.device)
+        slot = self._ring[t]
+        slot[:R].copy_(positions.reshape(-1))
+        slot[R : R + R * width].copy_(tables.reshape(-1))
+        dst = self._ring_dev[t]
+        dst[: R * (1 + width)].copy_(slot[: R * (1 + width)], non_blocking=True)
+        return dst[R : R + R * width].view(R, width), dst[:R].view(R, 1)
+
     @torch.no_grad()
     def _decode_window(self, w: int) -> None:
         """w decode steps of the running rows, in groups, over ring_program's order (item k = step k // m of
@@ -142,7 +163,7 @@ class PipelineEngine(Scheduler):
                 sends.append((tr.isend(act_out.pop(k), r + 1), None))
             else:
                 if t != plan_t:
-                    plan, plan_t = self._window_step(rows, cached, t, last=t == w - 1), t
+                    plan, plan_t = self._plan_on_device(t, *self._window_step(rows, cached, t, last=t == w - 1)), t
                 tables, positions = plan
                 views = self.pool.views(tables[grp], positions[grp])
                 pos = views[0].positions if views else positions[grp].to(dev)
