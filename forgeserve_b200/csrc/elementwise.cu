@@ -329,7 +329,8 @@ __global__ void argmax_kernel(const T* __restrict__ x, int64_t row_stride, int64
   }
 }
 
-// bf16 rows of dim = 256 * VPL: one warp per row (8 rows per CTA), lanes reading consecutive 16-byte vectors.
+// bf16 rows of dim = 256 * VPL: one warp per row (8 rows per CTA, or 1 for a few rows, so that a decode step's 64
+// rows spread over 64 SMs; the per-row arithmetic is the same either way), lanes reading consecutive 16-byte vectors.
 // Pass 1 accumulates the sum of squares (a shuffle reduction, no block barrier); pass 2 reads the row again (now
 // in L1/L2) with w and writes y. Few registers, so every warp slot of an SM can hold a row in flight. Same
 // rounding points as rmsnorm_kernel.
@@ -340,7 +341,7 @@ __global__ void __launch_bounds__(256)
   pdl_trigger();
   pdl_wait();   // launched with PDL: everything below reads or writes other kernels' data
   using bf = __nv_bfloat16;
-  const int64_t row = static_cast<int64_t>(blockIdx.x) * 8 + (threadIdx.x >> 5);
+  const int64_t row = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
   if (row >= rows) return;
   const int lane = threadIdx.x & 31;
   const uint4* xr = reinterpret_cast<const uint4*>(x + row * xs);
@@ -376,7 +377,8 @@ __global__ void __launch_bounds__(256)
 template <int VPL>
 static void launch_rmsnorm_warp(const void* x, int64_t xs, const void* w, void* y, int64_t ys, int64_t rows, float eps,
                                 cudaStream_t st) {
-  launch_pdl_async(rmsnorm_warp_kernel<VPL>, static_cast<unsigned>((rows + 7) / 8), 256, 0, st,
+  const int per_cta = rows >= 2048 ? 8 : 1;   // rows (warps) per CTA
+  launch_pdl_async(rmsnorm_warp_kernel<VPL>, static_cast<unsigned>((rows + per_cta - 1) / per_cta), 32 * per_cta, 0, st,
       static_cast<const __nv_bfloat16*>(x), xs, static_cast<const __nv_bfloat16*>(w), static_cast<__nv_bfloat16*>(y),
       ys, rows, eps);
 }
