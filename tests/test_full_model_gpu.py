@@ -14,8 +14,9 @@ after one layer and 0.42 after 32 (measured on a B200; the bf16 logits alone are
 4-8), so the 2e-2 bar of the bf16 mode cannot hold at this depth for any bf16 implementation; it is met on the
 smaller bf16 models (config 1's golden bf16 logits, smoke()). Here the bar is the reference's own spread:
   * max-abs(log_softmax(product) - log_softmax(r16)) <= 1.1 * max-abs(log_softmax(o16) - log_softmax(r16));
-  * max-abs against o32 <= 1.15 * r16's max-abs against o32 (the product is as close to the exact algebra as the
-    reference's own bf16 module).
+  * max-abs against o32 <= 1.25 * r16's max-abs against o32 (the product is about as close to the exact algebra as
+    the reference's own bf16 module; measured 1.04, and a variant of the attention kernel that only summed each
+    softmax row in two halves moved it to 1.16, so the figure is sensitive to the order of fp32 sums).
 
 * ForgeModel's forward over 2 x 512 tokens (forgeserve/model.py:140-159), against all three.
 * Greedy generation of 16 tokens per row (forgeserve/sampling.py:24-35): the product's logits at every step (the
@@ -63,7 +64,7 @@ def lsm_err(a: torch.Tensor, b: torch.Tensor) -> float:
 
 
 SPREAD = 1.1           # the product may differ from r16 by 1.1x what o16 does
-EXACT_SPREAD = 1.15    # ... and from o32 by 1.15x what r16 does
+EXACT_SPREAD = 1.25    # ... and from o32 by 1.25x what r16 does
 
 
 def test_8b_full_model_logits_match_the_oracle(model8b):
