@@ -776,6 +776,31 @@ def profile_case(name: str, reps: int, timed: bool = False):
                           "splits_workspace": L.load().fs_attention_decode_workspace(rows, nh, nkv, hd, W * bs)}))
         fn = lambda: ops.attention_decode(q, desc, W * bs, positions, out, rows, nh, nkv, hd)
         work = (kv_bytes + 2.0 * rows * nh * hd * 2, "B")  # K and V of every key, q in, o out
+    elif name in ("prefill_paged", "prefill_contiguous"):   # one config-4 prefill step: 1 prompt of 2300 tokens
+        from forgeserve_b200 import ForgeModel, ModelConfig
+        from forgeserve_b200.kv import new_contiguous_cache
+        from forgeserve_b200.paged import PagedKVPool
+        from forgeserve_b200.weights import init_model_
+        import random
+        cfg = ModelConfig(**CFG)
+        model = ForgeModel(cfg, device=dev, dtype=torch.bfloat16).eval()
+        init_model_(model, seed=1234, std=0.02)
+        T = 2300
+        idx = torch.randint(0, cfg.vocab_size, (1, T), generator=torch.Generator().manual_seed(3)).to(dev)
+        pos = torch.arange(T, device=dev)[None]
+        if name == "prefill_paged":
+            bs = 16
+            nblk = -(-T // bs)
+            pool = PagedKVPool(cfg, 4 * nblk, bs, dtype=torch.bfloat16, device=dev)
+            blocks = list(range(4 * nblk))
+            random.Random(5).shuffle(blocks)
+            table = torch.tensor([blocks[:nblk]], device=dev)
+            fn = lambda: model(idx, pos, pool.views(table, pos), last_only=True)
+        else:
+            fn = lambda: model(idx, kv=new_contiguous_cache(cfg.n_layers, cfg.max_seq_len), last_only=True)
+        flops = T * (2 * (d * (nh + 2 * nkv) * hd + nh * hd * d + 3 * d * F) * cfg.n_layers + 2 * d * V / T) \
+            + 2 * nh * T * T * hd * cfg.n_layers
+        work = (float(flops), "FLOP")
     elif name == "decode_projections":  # a decode layer's four projections back to back, 64 rows, 8 layers per replay
         rows, per_replay = 64, 8
         wqkv, wo = rnd((nh + 2 * nkv) * hd, d, scale=0.02), rnd(d, nh * hd, scale=0.02)
