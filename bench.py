@@ -909,13 +909,11 @@ def profile_case(name: str, reps: int, timed: bool = False):
 
 def auto_seq_chunks(workload: str, gpus: int) -> int:
     """Sequence pieces per micro-batch for the prefill workloads by default: pieces cut the pipeline's fill and drain
-    from (p - 1) / (m + p - 1) to (p - 1) / (m s + p - 1), but every piece's GEMMs have s times fewer rows and the
-    stages in the middle, which receive and send every piece, lose GEMM throughput to the extra NCCL traffic.
-    Measured on config 3: at 2 GPUs 4 pieces gave 132.4k tokens/s against 137.9k whole, at 4 GPUs 238.7k against
-    242.5k (bubble 0.106 against 0.169, but the middle stages' busy time +14 %); the fill-and-drain saving grows with
-    the stage count (0.30 of a forward at 8 stages), so pieces only from 8 stages on, and only while a piece keeps
-    >= 2048 GEMM rows."""
-    if workload not in PREFILL or gpus < 8:
+    from (p - 1) / (m + p - 1) to (p - 1) / (m s + p - 1), but every piece's GEMMs have s times fewer rows. Measured on
+    config 3: at 2 GPUs 4 pieces gave 132.4k tokens/s against 137.9k whole; at 4 GPUs 248.6k against 242.5k (with one
+    NCCL channel per stage pair; with two, the middle stages lost 12 % of their GEMM rate and pieces gave 238.7k); at
+    8 GPUs 445.0k against 406.4k (two channels). So pieces from 4 stages on, while a piece keeps >= 2048 GEMM rows."""
+    if workload not in PREFILL or gpus < 4:
         return 1
     spec = PREFILL[workload]
     rows = spec["rows"] * spec["seq"]
@@ -933,7 +931,7 @@ def main():
     ap.add_argument("--seq-chunks", type=int, default=0,
                     help="c3, c2, c5: pieces per micro-batch along the sequence in the prompt's forward; c4 with "
                          "N > 1: pieces per prefill (pipeline_forward's seq_chunks, PipelineEngine's "
-                         "prefill_chunks). 0 (default): auto_seq_chunks (4 for c3 and 2 for c2 from 8 GPUs on, else 1)")
+                         "prefill_chunks). 0 (default): auto_seq_chunks (4 for c3 and 2 for c2 from 4 GPUs on, else 1)")
     ap.add_argument("--workload", choices=["c3", "c2", "c4", "c5"], default="c3",
                     help="c3: 8B-shape pipeline prefill (the headline metric); c2: 1B-shape pipeline prefill; "
                          "c4: continuous-batching decode; c5: 70B-shape generation, micro-batch sweep")

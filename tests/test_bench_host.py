@@ -63,8 +63,8 @@ def test_reference_arm_step_time_is_the_measured_sample():
 
 
 def test_sequence_pieces_default_to_the_stage_counts_where_they_pay():
-    assert [bench.auto_seq_chunks("c3", n) for n in (1, 2, 4, 8)] == [1, 1, 1, 4]
-    assert [bench.auto_seq_chunks("c2", n) for n in (1, 2, 4, 8)] == [1, 1, 1, 2]
+    assert [bench.auto_seq_chunks("c3", n) for n in (1, 2, 4, 8)] == [1, 1, 4, 4]
+    assert [bench.auto_seq_chunks("c2", n) for n in (1, 2, 4, 8)] == [1, 1, 2, 2]
     assert bench.auto_seq_chunks("c4", 8) == 1 and bench.auto_seq_chunks("c5", 8) == 1
     from forgeserve_b200.pipeline import seq_pieces
     for w in ("c3", "c2"):          # every default piece keeps >= 2048 GEMM rows
