@@ -716,18 +716,26 @@ def profile_case(name: str, reps: int, timed: bool = False):
         out = torch.empty(M, V, device=dev, dtype=torch.bfloat16)
         fn = lambda: ops.linear(a, w, out=out)
         work = (2.0 * M * V * d, "FLOP")
-    elif name.startswith("gemm_decode_"):   # a C4 decode step's projections (gemm_decode_<proj>[@rows], 64 rows)
-        proj, _, r = name[len("gemm_decode_"):].partition("@")
+    elif name.startswith(("gemm_decode_", "cublas_decode_")) and not name.endswith("_projections"):
+        # a C4 decode step's projections (gemm_decode_<proj>[@rows], 64 rows); gateup4k: gate/up with 4x the K (a
+        # longer weight stream, to separate the per-launch cost from the streaming rate); cublas_decode_<proj>:
+        # the same product by torch's cuBLAS matmul, store only, for comparison
+        lib = name.startswith("cublas_")
+        proj, _, r = name[len("cublas_decode_" if lib else "gemm_decode_"):].partition("@")
         rows = int(r) if r else 64
-        n_k = {"qkv": ((nh + 2 * nkv) * hd, d), "o": (d, nh * hd), "gateup": (2 * F, d), "down": (d, F)}
+        n_k = {"qkv": ((nh + 2 * nkv) * hd, d), "o": (d, nh * hd), "gateup": (2 * F, d), "down": (d, F),
+               "gateup4k": (2 * F, 4 * d)}
         if proj not in n_k:
             raise SystemExit(f"unknown profile case {name}")
         n, k = n_k[proj]
         a, w = rnd(rows, k), rnd(n, k, scale=0.02)
-        if proj in ("o", "down"):
+        if lib:
+            out = torch.empty(rows, n, device=dev, dtype=torch.bfloat16)
+            fn = lambda: torch.matmul(a, w.t(), out=out)
+        elif proj in ("o", "down"):
             x = rnd(rows, n)
             fn = lambda: ops.linear(a, w, L.FS_EPI_RESIDUAL, residual=x, out=x)
-        elif proj == "gateup":
+        elif proj.startswith("gateup"):
             fn = lambda: ops.linear(a, w, L.FS_EPI_SWIGLU)
         else:
             fn = lambda: ops.linear(a, w)
@@ -801,14 +809,24 @@ def profile_case(name: str, reps: int, timed: bool = False):
         flops = T * (2 * (d * (nh + 2 * nkv) * hd + nh * hd * d + 3 * d * F) * cfg.n_layers + 2 * d * V / T) \
             + 2 * nh * T * T * hd * cfg.n_layers
         work = (float(flops), "FLOP")
-    elif name == "decode_projections":  # a decode layer's four projections back to back, 64 rows, 8 layers per replay
+    elif name in ("decode_projections", "cublas_decode_projections"):
+        # a decode layer's four projections back to back, 64 rows, 8 layers per replay; the cublas_ form makes the
+        # same four products with torch's cuBLAS matmul, store only (no residual add, no SwiGLU), for comparison
         rows, per_replay = 64, 8
         wqkv, wo = rnd((nh + 2 * nkv) * hd, d, scale=0.02), rnd(d, nh * hd, scale=0.02)
         wgu, wd = rnd(2 * F, d, scale=0.02), rnd(d, F, scale=0.02)
         x, h, a = rnd(rows, d), rnd(rows, d), rnd(rows, nh * hd)
+        outs = [torch.empty(rows, n, device=dev, dtype=torch.bfloat16) for n in (wqkv.shape[0], d, 2 * F, d)]
+        gin = rnd(rows, F)
 
         def projections():
             for _ in range(per_replay):
+                if name.startswith("cublas_"):
+                    torch.matmul(h, wqkv.t(), out=outs[0])
+                    torch.matmul(a, wo.t(), out=outs[1])
+                    torch.matmul(h, wgu.t(), out=outs[2])
+                    torch.matmul(gin, wd.t(), out=outs[3])
+                    continue
                 ops.linear(h, wqkv)
                 ops.linear(a, wo, L.FS_EPI_RESIDUAL, residual=x, out=x)
                 gg = ops.linear(h, wgu, L.FS_EPI_SWIGLU)

@@ -334,6 +334,9 @@ __global__ void __launch_bounds__(THREADS_TC)
 
   uint8_t* ring = smem + warp * STAGES * G::STAGE_BYTES;
   uint64_t* wfull = full + warp * STAGES;
+  // Every cached key and value is read once per step: evict-first in L2, so that the split partials written
+  // meanwhile are still there for the combine.
+  const uint64_t kv_policy = l2_policy_evict_first();
   // Lane 0 of the warp fetches the warp's j-th tile (keys k0 .. k0+15, all in one cache block) into stage j % STAGES.
   auto issue = [&](int j) {
     const int64_t k0 = k_begin + static_cast<int64_t>(warp + WARPS * j) * TILE;
@@ -351,8 +354,8 @@ __global__ void __launch_bounds__(THREADS_TC)
     mbar_arrive_expect_tx(bar, G::STAGE_BYTES);
 #pragma unroll
     for (int b = 0; b < G::NB; ++b) {
-      tma_load_2d(st + b * BOX_BYTES, &tmK, bar, 64 * b, static_cast<int>(row));
-      tma_load_2d(st + G::KV_BYTES + b * BOX_BYTES, &tmV, bar, 64 * b, static_cast<int>(row));
+      tma_load_2d_hint(st + b * BOX_BYTES, &tmK, bar, 64 * b, static_cast<int>(row), kv_policy);
+      tma_load_2d_hint(st + G::KV_BYTES + b * BOX_BYTES, &tmV, bar, 64 * b, static_cast<int>(row), kv_policy);
     }
   };
 

@@ -49,6 +49,9 @@ constexpr int TMEM_COLS = NUM_ACC * BN;  // 512
 constexpr int THREADS = 256;
 constexpr int BAR_BYTES = 256;
 constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 + BAR_BYTES;
+constexpr int THIN_STAGES = 5;   // stages of the M <= 64 form (64-row A boxes)
+constexpr int THIN_SMEM_BYTES = THIN_STAGES * KP1 * (A_BYTES / 2 + B_BYTES) + 1024 + BAR_BYTES;
+static_assert(THIN_SMEM_BYTES <= 227 * 1024, "thin GEMM stages must fit in shared memory");
 constexpr uint32_t IDESC = idesc_bf16_f32(BM, BN);
 
 struct Params {
@@ -67,6 +70,7 @@ struct Params {
   float* ws;
   int64_t ldw;
   unsigned* err;
+  int b_once;   // 1-SM kernel, one m-block: every weight byte is read once, under the L2 evict-first policy
 };
 
 constexpr int TQ = 4;   // tile-queue entries (claimed tiles handed from the producer to the MMA and epilogue warps)
@@ -311,28 +315,34 @@ __global__ void __launch_bounds__(256)
   *reinterpret_cast<uint2*>(C + static_cast<int64_t>(row) * ldc + j) = out;
 }
 
-template <int EPI>
+template <int EPI, bool THIN>
 __global__ void __launch_bounds__(THREADS, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, Params p) {
+  // THIN (M <= 64: decode steps): the A box is the 64 live rows (8 KB; the MMA's rows 64-127 read whatever follows
+  // and land in accumulator rows that are never stored), which leaves room for a fifth stage of weights in flight.
+  constexpr int NST = THIN ? THIN_STAGES : STAGES;
+  constexpr int ABYTES = THIN ? A_BYTES / 2 : A_BYTES;
+  constexpr int SBYTES = KP1 * (ABYTES + B_BYTES);
+  static_assert((2 * NST + 2 * NUM_ACC + 1) * 8 + 8 <= 128, "stage barriers, TMEM slot and abort flag fill 128 bytes");
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* tiles = smem;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + NST * SBYTES);
   uint64_t* full = bars;
-  uint64_t* empty = bars + STAGES;
-  uint64_t* tfull = bars + 2 * STAGES;
-  uint64_t* tempty = bars + 2 * STAGES + NUM_ACC;
-  uint64_t* mma_done = bars + 2 * STAGES + 2 * NUM_ACC;
+  uint64_t* empty = bars + NST;
+  uint64_t* tfull = bars + 2 * NST;
+  uint64_t* tempty = bars + 2 * NST + NUM_ACC;
+  uint64_t* mma_done = bars + 2 * NST + 2 * NUM_ACC;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
-  uint64_t* tq_full = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES + 128);
+  uint64_t* tq_full = reinterpret_cast<uint64_t*>(smem + NST * SBYTES + 128);
   uint64_t* tq_empty = tq_full + TQ;
   volatile int* tq = reinterpret_cast<volatile int*>(tq_empty + TQ);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < STAGES; ++s) {
+    for (int s = 0; s < NST; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
@@ -372,10 +382,10 @@ __global__ void __launch_bounds__(THREADS, 1)
     if (lane == 0) {
       int s = 0;
       uint32_t ph = 0;
-      bool issued[STAGES];
-      uint32_t last_ph[STAGES];
+      bool issued[NST];
+      uint32_t last_ph[NST];
 #pragma unroll
-      for (int i = 0; i < STAGES; ++i) issued[i] = false, last_ph[i] = 0;
+      for (int i = 0; i < NST; ++i) issued[i] = false, last_ph[i] = 0;
       const int total = p.num_tiles * p.k_split;
       const int first = static_cast<int>(blockIdx.x) < total ? static_cast<int>(blockIdx.x) : -1;
       auto unit_coords = [&](int unit, int& kb0, int& kb1, int& m_blk, int& b_row0, int& b_row1) {
@@ -387,19 +397,26 @@ __global__ void __launch_bounds__(THREADS, 1)
         b_row0 = EPI == EPI_SWIGLU ? n_blk * (BN / 2) : n_blk * BN;
         b_row1 = EPI == EPI_SWIGLU ? p.n_out + n_blk * (BN / 2) : n_blk * BN + BN / 2;
       };
+      const uint64_t b_policy = p.b_once ? l2_policy_evict_first() : 0;
+      auto load_b = [&](void* dst, uint64_t* bar, int kx, int row) {
+        if (p.b_once)
+          tma_load_2d_hint(dst, &tmB, bar, kx, row, b_policy);
+        else
+          tma_load_2d(dst, &tmB, bar, kx, row);
+      };
       // Weights of the first unit's first k-blocks (the ring is fresh: stage i, phase 0), before the wait.
       int pre = 0;
       if (first >= 0) {
         int kb0, kb1, m_blk, b_row0, b_row1;
         unit_coords(first, kb0, kb1, m_blk, b_row0, b_row1);
-        for (int kb = kb0; kb < kb1 && pre < STAGES; ++kb, ++pre) {
-          mbar_arrive_expect_tx(&full[pre], STAGE_BYTES);
+        for (int kb = kb0; kb < kb1 && pre < NST; ++kb, ++pre) {
+          mbar_arrive_expect_tx(&full[pre], SBYTES);
 #pragma unroll
           for (int pk = 0; pk < KP1; ++pk) {
             const int kx = (kb * KP1 + pk) * BK;
-            uint8_t* st = tiles + pre * STAGE_BYTES;
-            tma_load_2d(st + KP1 * A_BYTES + pk * B_BYTES, &tmB, &full[pre], kx, b_row0);
-            tma_load_2d(st + KP1 * A_BYTES + pk * B_BYTES + BH_BYTES, &tmB, &full[pre], kx, b_row1);
+            uint8_t* st = tiles + pre * SBYTES;
+            load_b(st + KP1 * ABYTES + pk * B_BYTES, &full[pre], kx, b_row0);
+            load_b(st + KP1 * ABYTES + pk * B_BYTES + BH_BYTES, &full[pre], kx, b_row1);
           }
           issued[pre] = true;
         }
@@ -411,7 +428,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         for (int j = 0; j < pre; ++j)
 #pragma unroll
           for (int pk = 0; pk < KP1; ++pk)
-            tma_load_2d(tiles + j * STAGE_BYTES + pk * A_BYTES, &tmA, &full[j], ((kb0 + j) * KP1 + pk) * BK,
+            tma_load_2d(tiles + j * SBYTES + pk * ABYTES, &tmA, &full[j], ((kb0 + j) * KP1 + pk) * BK,
                         m_blk * BM);
       }
       bool ok = true;
@@ -437,25 +454,25 @@ __global__ void __launch_bounds__(THREADS, 1)
               ok = false;
               break;
             }
-            mbar_arrive_expect_tx(&full[s], STAGE_BYTES);
+            mbar_arrive_expect_tx(&full[s], SBYTES);
 #pragma unroll
             for (int pk = 0; pk < KP1; ++pk) {
               const int kx = (kb * KP1 + pk) * BK;
-              uint8_t* st = tiles + s * STAGE_BYTES;
-              tma_load_2d(st + pk * A_BYTES, &tmA, &full[s], kx, m_blk * BM);
-              tma_load_2d(st + KP1 * A_BYTES + pk * B_BYTES, &tmB, &full[s], kx, b_row0);
-              tma_load_2d(st + KP1 * A_BYTES + pk * B_BYTES + BH_BYTES, &tmB, &full[s], kx, b_row1);
+              uint8_t* st = tiles + s * SBYTES;
+              tma_load_2d(st + pk * ABYTES, &tmA, &full[s], kx, m_blk * BM);
+              load_b(st + KP1 * ABYTES + pk * B_BYTES, &full[s], kx, b_row0);
+              load_b(st + KP1 * ABYTES + pk * B_BYTES + BH_BYTES, &full[s], kx, b_row1);
             }
           }
           issued[s] = true;
           last_ph[s] = ph;
-          if (++s == STAGES) s = 0, ph ^= 1u;
+          if (++s == NST) s = 0, ph ^= 1u;
         }
       }
       if (!ok) {
         *abort_flag = 1;
         // Let every copy this thread started land before the CTA can exit (bounded).
-        for (int i = 0; i < STAGES; ++i)
+        for (int i = 0; i < NST; ++i)
           if (issued[i]) mbar_wait(&full[i], last_ph[i], p.err);
       }
     }
@@ -488,11 +505,11 @@ __global__ void __launch_bounds__(THREADS, 1)
             break;
           }
           tc_fence_after();
-          const uint32_t a_addr = smem_u32(tiles + s * STAGE_BYTES);
+          const uint32_t a_addr = smem_u32(tiles + s * SBYTES);
 #pragma unroll
           for (int pk = 0; pk < KP1; ++pk) {
-            const uint64_t adesc = sw128_kmajor_desc(a_addr + pk * A_BYTES);
-            const uint64_t bdesc = sw128_kmajor_desc(a_addr + KP1 * A_BYTES + pk * B_BYTES);
+            const uint64_t adesc = sw128_kmajor_desc(a_addr + pk * ABYTES);
+            const uint64_t bdesc = sw128_kmajor_desc(a_addr + KP1 * ABYTES + pk * B_BYTES);
 #pragma unroll
             for (int k = 0; k < BK / 16; ++k) {
               // +32 bytes along K inside the 128-byte swizzle row = +2 in the descriptor's address field
@@ -500,7 +517,7 @@ __global__ void __launch_bounds__(THREADS, 1)
             }
           }
           tc_commit(&empty[s]);  // the smem stage is free once these MMAs have read it
-          if (++s == STAGES) s = 0, ph ^= 1u;
+          if (++s == NST) s = 0, ph ^= 1u;
         }
         if (!ok) break;
         tc_commit(&tfull[acc]);  // accumulator complete
@@ -528,10 +545,13 @@ __global__ void __launch_bounds__(THREADS, 1)
       tc_fence_after();
       int m_blk, n_blk;
       tile_coords(unit / p.k_split, p.num_m_blocks, p.num_tiles / p.num_m_blocks, m_blk, n_blk);
-      if (p.k_split > 1)
+      if (THIN && q >= 2) {
+        // accumulator lanes 64-127 hold rows that do not exist
+      } else if (p.k_split > 1) {
         epilogue_partial<EPI>(p, tmem_base, acc, q, lane, m_blk * BM + q * 32 + lane, n_blk, unit % p.k_split);
-      else
+      } else {
         epilogue_tile<EPI>(p, tmem_base, acc, q, lane, m_blk * BM + q * 32 + lane, n_blk, vec_ok);
+      }
       tc_fence_before();
       mbar_arrive(&tempty[acc]);
       if (++acc == NUM_ACC) acc = 0, acc_ph ^= 1u;
@@ -917,18 +937,19 @@ bool supported(const void* A, int64_t lda, const void* B, int64_t ldb, int64_t K
          (lda % 8 == 0) && (ldb % 8 == 0) && K >= 8 && K % 8 == 0;
 }
 
-template <int EPI>
+template <int EPI, bool THIN>
 static int launch_t(const CUtensorMap& ma, const CUtensorMap& mb, const Params& p, int grid, cudaStream_t st) {
   static bool attr_set[64] = {false};
+  constexpr int smem = THIN ? THIN_SMEM_BYTES : SMEM_BYTES;
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev >= 0 && dev < 64 && !attr_set[dev]) {
-    if (cudaFuncSetAttribute(gemm_tc_kernel<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES) !=
+    if (cudaFuncSetAttribute(gemm_tc_kernel<EPI, THIN>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) !=
         cudaSuccess)
       return check_launch("gemm_tc set smem");
     attr_set[dev] = true;
   }
-  return launch_pdl("gemm_tc_kernel", gemm_tc_kernel<EPI>, dim3(grid), dim3(THREADS), SMEM_BYTES, st, ma, mb, p);
+  return launch_pdl("gemm_tc_kernel", gemm_tc_kernel<EPI, THIN>, dim3(grid), dim3(THREADS), smem, st, ma, mb, p);
 }
 
 template <int EPI>
@@ -1041,6 +1062,26 @@ static bool split_one_wave() {
   return w;
 }
 
+// M <= 64 runs the thin form of the 1-SM kernel (64-row A boxes, five stages) unless FORGESERVE_GEMM_THIN=0. Rows
+// get the same sums either way: each output row is the same K-ordered MMA chain over the same weights.
+// With one m-block every weight byte is read once: those loads carry the L2 evict-first policy (unless
+// FORGESERVE_GEMM_L2HINT=0), so that the split-K partials written meanwhile stay in L2 for the reduce.
+static bool l2_hint_enabled() {
+  static const bool t = [] {
+    const char* v = std::getenv("FORGESERVE_GEMM_L2HINT");
+    return !(v && std::string(v) == "0");
+  }();
+  return t;
+}
+
+static bool thin_enabled() {
+  static const bool t = [] {
+    const char* v = std::getenv("FORGESERVE_GEMM_THIN");
+    return !(v && std::string(v) == "0");
+  }();
+  return t;
+}
+
 int choose_k_split(int tiles, int k_blocks, int sms) {
   constexpr int KB_MIN = 6;
   if (sms <= 0 || tiles >= sms || k_blocks < 2 * KB_MIN) return 1;
@@ -1076,8 +1117,9 @@ int gemm_tc(const void* A, int64_t lda, const void* B, int64_t ldb, void* C, int
             int64_t ldr, int64_t M, int64_t N, int64_t K, int64_t n_out, int epi, bool sys_fence, cudaStream_t stream) {
   if (M <= 0 || N <= 0 || n_out <= 0) return 0;
   if (M > INT32_MAX / 2 || N > INT32_MAX / 2 || K > INT32_MAX / 2) return fail("gemm: dimension too large");
+  const bool thin = M <= BM / 2 && thin_enabled();
   CUtensorMap ma, mb;
-  if (make_kmajor_map(&ma, A, M, K, lda, BM)) return -1;
+  if (make_kmajor_map(&ma, A, M, K, lda, thin ? BM / 2 : BM)) return -1;
   if (make_kmajor_map(&mb, B, N, K, ldb, BN / 2)) return -1;
   Params p;
   p.C = static_cast<__nv_bfloat16*>(C);
@@ -1098,6 +1140,7 @@ int gemm_tc(const void* A, int64_t lda, const void* B, int64_t ldb, void* C, int
   p.ldw = 0;
   p.err = error_word();
   if (!p.err) return -1;
+  p.b_once = 0;
   if (g_pair_mode && M > BM) {
     p.k_blocks = static_cast<int>((K + BK * KP - 1) / (BK * KP));   // k-blocks of 64 * KP
     p.sched = sched_counter(stream);
@@ -1114,6 +1157,7 @@ int gemm_tc(const void* A, int64_t lda, const void* B, int64_t ldb, void* C, int
   }
   p.sched = sched_counter(stream);
   if (!p.sched) return -1;
+  p.b_once = p.num_m_blocks == 1 && l2_hint_enabled() ? 1 : 0;
   const int sms = sm_count();
   // Few rows (a decode step): with one m-block there are few tiles, and the GEMM streams the weights; the time is
   // set by how evenly the SMs share them. Split K so that the units fill whole waves of the persistent grid.
@@ -1128,10 +1172,13 @@ int gemm_tc(const void* A, int64_t lda, const void* B, int64_t ldb, void* C, int
   const int units = p.num_tiles * p.k_split;
   const int grid = units < sms ? units : sms;
   int rc;
-  switch (epi) {
-    case EPI_STORE: rc = launch_t<EPI_STORE>(ma, mb, p, grid, stream); break;
-    case EPI_RESIDUAL: rc = launch_t<EPI_RESIDUAL>(ma, mb, p, grid, stream); break;
-    case EPI_SWIGLU: rc = launch_t<EPI_SWIGLU>(ma, mb, p, grid, stream); break;
+  switch (epi * 2 + (thin ? 1 : 0)) {
+    case EPI_STORE * 2: rc = launch_t<EPI_STORE, false>(ma, mb, p, grid, stream); break;
+    case EPI_RESIDUAL * 2: rc = launch_t<EPI_RESIDUAL, false>(ma, mb, p, grid, stream); break;
+    case EPI_SWIGLU * 2: rc = launch_t<EPI_SWIGLU, false>(ma, mb, p, grid, stream); break;
+    case EPI_STORE * 2 + 1: rc = launch_t<EPI_STORE, true>(ma, mb, p, grid, stream); break;
+    case EPI_RESIDUAL * 2 + 1: rc = launch_t<EPI_RESIDUAL, true>(ma, mb, p, grid, stream); break;
+    case EPI_SWIGLU * 2 + 1: rc = launch_t<EPI_SWIGLU, true>(ma, mb, p, grid, stream); break;
     default: return fail("gemm: unknown epilogue");
   }
   if (rc || p.k_split == 1) return rc;

@@ -111,6 +111,22 @@ def test_split_k_reduce_paths_agree_bitwise(epi):
     assert L.device_error(clear=True) == 0
 
 
+@pytest.mark.parametrize("epi", [L.FS_EPI_STORE, L.FS_EPI_RESIDUAL, L.FS_EPI_SWIGLU])
+@pytest.mark.parametrize("M,N,K", [(64, 2048, 4096), (17, 1002, 4096), (1, 512, 256), (50, 768, 320)])
+def test_gemm_thin_rows_match_full_tile_bitwise(epi, M, N, K):
+    """Up to 64 rows run the thin form (64-row A boxes, five stages); the same rows inside a 100-row product run
+    the full 128-row form. Each row is the same MMA chain over the same weights and the same split of K, so the
+    two give the same bits, with and without split K."""
+    a = torch.randn(100, K, device=DEV).bfloat16()
+    w = (torch.randn(N, K, device=DEV) / math.sqrt(K)).bfloat16()
+    n_out = N // 2 if epi == L.FS_EPI_SWIGLU else N
+    r = torch.randn(100, n_out, device=DEV).bfloat16() if epi == L.FS_EPI_RESIDUAL else None
+    full = ops.linear(a, w, epi, residual=r)
+    thin = ops.linear(a[:M], w, epi, residual=None if r is None else r[:M])
+    assert torch.equal(thin, full[:M])
+    assert L.device_error(clear=True) == 0
+
+
 def test_gemm_tcgen05_strided_rows():
     """A operand that is a column slice of a wider buffer (row stride > K), as the q part of a qkv buffer."""
     buf = torch.randn(200, 384, device=DEV).bfloat16()
