@@ -196,7 +196,11 @@ def rope_ref(x, cos, sin, positions):
 
 
 @pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
-@pytest.mark.parametrize("nh,nkv,hd", [(8, 4, 8), (32, 8, 128)])
+@pytest.mark.parametrize("nh,nkv,hd", [(8, 4, 8), (32, 8, 128),
+                                       # bf16 vector path: fewer heads than one group of threads (hd 16: one chunk
+                                       # per half head; hd 64), more heads than four groups (70B shape), v wider
+                                       # than the block, and hd 48 (chunks do not divide the block: generic path)
+                                       (4, 2, 16), (4, 2, 64), (64, 8, 128), (16, 16, 128), (6, 2, 48)])
 def test_rope_kv_write_contiguous(dtype, nh, nkv, hd):
     B, T, start, cap = 3, 5, 4, 16
     cos, sin = rope_tables(hd, 64, 10000.0)
@@ -240,6 +244,41 @@ def test_rope_kv_write_paged_slots():
             p = int(positions[r, j])
             blk = int(table[r, p // bs])
             torch.testing.assert_close(pool_v[blk, :, p % bs], v_src[r, j])
+
+
+@pytest.mark.parametrize("hd", [16, 128])
+def test_rope_kv_write_bad_slot_and_position_bf16(hd):
+    """bf16 vector path, paged: a token whose block-table entry is -1 still has its q rotated, stores no k or v,
+    and raises FS_ERR_BAD_SLOT; a position past the RoPE table raises FS_ERR_BAD_POSITION and writes nothing."""
+    nh, nkv, bs = 8, 2, 16
+    cos, sin = rope_tables(hd, 64, 10000.0)
+    cos, sin = cos.to(DEV), sin.to(DEV)
+    pool_k = torch.zeros(4, nkv, bs, hd, device=DEV, dtype=torch.bfloat16)
+    pool_v = torch.zeros_like(pool_k)
+    table = torch.tensor([[1, -1]], device=DEV)
+    positions = torch.tensor([[3, 20]], device=DEV)             # block 1, then the missing block
+    qkv = torch.randn(2, (nh + 2 * nkv) * hd, device=DEV).bfloat16()
+    orig = qkv.clone()
+    ops.rope_kv_write(qkv, cos, sin, positions, ops.paged_desc(pool_k, pool_v, table), 1, 2, nh, nkv, hd,
+                      slot_base=0, slot_from_pos=True)
+    assert L.device_error(clear=True) & L.FS_ERR_BAD_SLOT
+    q0 = orig[:, : nh * hd].view(1, 2, nh, hd).transpose(1, 2).cpu()
+    q_want = rope_ref(q0, cos.cpu(), sin.cpu(), positions.cpu())
+    torch.testing.assert_close(qkv[:, : nh * hd].view(1, 2, nh, hd).transpose(1, 2).cpu(), q_want, atol=0, rtol=0)
+    v_src = orig[:, (nh + nkv) * hd :].view(2, nkv, hd)
+    torch.testing.assert_close(pool_v[1, :, 3], v_src[0], atol=0, rtol=0)
+    assert pool_k[[0, 2, 3]].abs().sum() == 0 and pool_v[[0, 2, 3]].abs().sum() == 0
+    assert int((pool_v[1].abs().sum(-1) != 0).sum()) == nkv      # only slot 3 of block 1 was written
+
+    bad = torch.tensor([[3, 64]], device=DEV)                    # 64 = the table's length: out of range
+    qkv2 = orig.clone()
+    pool_k.zero_()
+    pool_v.zero_()
+    ops.rope_kv_write(qkv2, cos, sin, bad, ops.paged_desc(pool_k, pool_v, torch.tensor([[1, 2, 3, 0, 0]], device=DEV)),
+                      1, 2, nh, nkv, hd, slot_base=0, slot_from_pos=True)
+    assert L.device_error(clear=True) & L.FS_ERR_BAD_POSITION
+    assert torch.equal(qkv2[1], orig[1])                          # the bad token is left as it was
+    assert int((pool_v.abs().sum(-1) != 0).sum()) == nkv          # only the good token's v was stored
 
 
 # ------------------------------------------------------------------------------------------ attention
