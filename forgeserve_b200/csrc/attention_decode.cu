@@ -337,11 +337,18 @@ __global__ void __launch_bounds__(THREADS_TC)
   // Every cached key and value is read once per step: evict-first in L2, so that the split partials written
   // meanwhile are still there for the combine.
   const uint64_t kv_policy = l2_policy_evict_first();
-  // Lane 0 of the warp fetches the warp's j-th tile (keys k0 .. k0+15, all in one cache block) into stage j % STAGES.
-  auto issue = [&](int j) {
+  // Cache block of the warp's j-th tile (keys k0 .. k0+15, all in one block); -1 past the table.
+  auto tile_block = [&](int j) -> int64_t {
     const int64_t k0 = k_begin + static_cast<int64_t>(warp + WARPS * j) * TILE;
     const int64_t bi = k0 / p.block_size;
-    const int64_t blk = bi < p.table_cols ? p.table[static_cast<int64_t>(r) * p.table_stride + bi] : -1;
+    return bi < p.table_cols ? p.table[static_cast<int64_t>(r) * p.table_stride + bi] : -1;
+  };
+  // Lane l holds the block of tile base + l of this warp, loaded 32 tiles at a time by the whole warp, so that a
+  // TMA issue does not wait on a table load of its own.
+  int64_t lane_blk = lane < my_n ? tile_block(lane) : -1;
+  // Lane 0 of the warp fetches the warp's j-th tile (block blk) into stage j % STAGES.
+  auto issue = [&](int j, int64_t blk) {
+    const int64_t k0 = k_begin + static_cast<int64_t>(warp + WARPS * j) * TILE;
     int64_t row;
     if (blk < 0 || blk >= p.num_blocks) {
       flag_error(p.err, ERR_BAD_SLOT);
@@ -378,8 +385,10 @@ __global__ void __launch_bounds__(THREADS_TC)
 #pragma unroll
   for (int mt = 0; mt < HD / 16; ++mt) acc[mt][0] = acc[mt][1] = acc[mt][2] = acc[mt][3] = 0.f;
 
-  if (lane == 0)
-    for (int j = 0; j < my_n && j < STAGES; ++j) issue(j);
+  for (int j = 0; j < STAGES; ++j) {
+    const int64_t b = __shfl_sync(0xffffffffu, lane_blk, j);
+    if (lane == 0 && j < my_n) issue(j, b);
+  }
   int j = 0;
   bool timed_out = false;
   for (; j < my_n; ++j) {
@@ -447,9 +456,14 @@ __global__ void __launch_bounds__(THREADS_TC)
       }
     }
     __syncwarp();   // every lane's reads of this stage are done before it is refilled
-    if (lane == 0 && j + STAGES < my_n) {
-      fence_proxy_async_smem();
-      issue(j + STAGES);
+    {
+      const int jn = j + STAGES;   // the tile that goes into the stage just freed
+      if ((jn & 31) == 0 && jn < my_n) lane_blk = jn + lane < my_n ? tile_block(jn + lane) : -1;   // next 32
+      const int64_t b = __shfl_sync(0xffffffffu, lane_blk, jn & 31);
+      if (lane == 0 && jn < my_n) {
+        fence_proxy_async_smem();
+        issue(jn, b);
+      }
     }
   }
   if (timed_out) {   // let the copies still in flight land (bounded) before the CTA gives its shared memory back

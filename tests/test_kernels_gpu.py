@@ -527,6 +527,35 @@ def test_attention_decode_paged(dtype, hd, nh, nkv, lengths, bs):
     assert (got - want).abs().max().item() < tol
 
 
+def test_attention_decode_long_rows_reload_block_ids():
+    """Rows past 64 splits x 512 keys: a split then covers more than 32 of a warp's 16-key tiles, and the warp
+    reloads its lanes' block ids every 32 tiles. A sharper softmax (q x 2) makes a wrong block show as an error of
+    the order of the output itself."""
+    dtype, hd, nh, nkv, bs = torch.bfloat16, 128, 2, 1, 16
+    lengths = [140000, 40000]
+    B = len(lengths)
+    widths = [-(-(n + 1) // bs) for n in lengths]
+    nblk = sum(widths) + 3
+    blocks = list(range(nblk))
+    random.Random(7).shuffle(blocks)
+    it = iter(blocks)
+    W = max(widths)
+    table = torch.tensor([[next(it) for _ in range(w)] + [0] * (W - w) for w in widths], device=DEV)
+    pool_k = torch.randn(nblk, nkv, bs, hd, device=DEV).to(dtype)
+    pool_v = torch.randn(nblk, nkv, bs, hd, device=DEV).to(dtype)
+    positions = torch.tensor([[n] for n in lengths], device=DEV)
+    q = (torch.randn(B, nh * hd, device=DEV) * 2).to(dtype)
+    out = torch.empty_like(q)
+    assert L.load().fs_attention_decode_workspace(B, nh, nkv, hd, W * bs) > 0
+    ops.attention_decode(q, ops.paged_desc(pool_k, pool_v, table), W * bs, positions, out, B, nh, nkv, hd)
+    k_all = pool_k[table].permute(0, 2, 1, 3, 4).reshape(B, nkv, -1, hd)
+    v_all = pool_v[table].permute(0, 2, 1, 3, 4).reshape(B, nkv, -1, hd)
+    want = attention_ref(q.view(B, 1, nh, hd).transpose(1, 2), k_all, v_all, positions, nh // nkv)
+    got = out.view(B, 1, nh, hd).transpose(1, 2).double()
+    err, scale = (got - want).abs().max().item(), want.abs().max().item()
+    assert err <= 3e-2 * scale, f"max err {err} vs output scale {scale}"
+
+
 def test_attention_decode_ignores_stale_slots():
     """Slots past each row's position (in the last block, and whole unused blocks) hold NaN: they must not leak."""
     B, nh, nkv, hd, bs = 3, 32, 8, 128, 16
