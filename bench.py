@@ -382,7 +382,7 @@ def run_c4(args):
         init_stage_(stage, seed=1234, std=0.02)
         engine = PipelineEngine(stage, C4["num_blocks"], C4["block_size"], max_batch=C4["requests"], seed=0,
                                 microbatches=args.microbatches or world, overlap=False if args.no_windows else None,
-                                prefill_chunks=args.seq_chunks)
+                                prefill_chunks=args.seq_chunks, cuda_graphs=not args.no_graphs)
         weight_bytes = sum(p.numel() * p.element_size() for p in stage.parameters())
     rng = random.Random(11)
     lengths = [rng.randint(C4["prompt_lo"], C4["prompt_hi"]) for _ in range(C4["requests"])]
@@ -458,7 +458,7 @@ def run_c4(args):
             "data": "synthetic: seeded prompt lengths and token ids, seeded N(0, 0.02) weights",
             "config": {"workload": C4_WORKLOAD, "stages": world, "parallelism": f"pp{world}",
                        "microbatches": 1 if world == 1 else (args.microbatches or world),
-                       "decode_cuda_graphs": world == 1 and not args.no_graphs,
+                       "decode_cuda_graphs": (not args.no_graphs) and (world == 1 or not args.no_windows),
                        "prefill_pieces": args.seq_chunks if world > 1 else 1,
                        "decode_windows": getattr(engine, "windows", 0)},
             "decode": {"tokens_per_s": round(dec_tokens / (dec_ms / 1e3), 1), "steps": steps_dec,

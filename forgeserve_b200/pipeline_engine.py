@@ -18,15 +18,69 @@ on step t's group j while the first stage already runs step t+1's earlier groups
 stages no stage waits for a token. The tokens reach every stage with one broadcast at the end of the window.
 """
 
-from typing import List, Optional
+from typing import Dict, List, Optional
 
 import torch
 import torch.distributed as dist
 
+from . import ops
 from .engine import Request, Scheduler
 from .paged import PagedKVPool
 from .pipeline import microbatch_sizes, ring_program, seq_pieces
 from .transport import DistTransport, ring_group
+
+
+class _StageDecodeGraph:
+    """One decode step of one row group on this stage, captured as a CUDA graph: the embedding (first stage), the
+    stage's layers, and the final norm, head of the last position and argmax (last stage), over static device
+    buffers for the input (token ids or activations), positions and block tables (tables padded with block 0 to
+    max_seq_len / block_size columns, which leaves the decode kernels' sums unchanged). The transfers between stages
+    stay outside the graph. The first step of a row count runs eagerly on the graph's own stream (it also sets up
+    that stream's GEMM tile counter, split-K and decode workspaces), then the same work is captured; replays run on
+    the caller's stream, in order with its transfers."""
+
+    def __init__(self, stage, pool, rows: int):
+        self.stage, self.pool, self.rows = stage, pool, rows
+        dev = stage.device
+        self.width = -(-stage.cfg.max_seq_len // pool.block_size)
+        self.pos = torch.zeros(rows, 1, dtype=torch.int64, device=dev)
+        self.tab = torch.zeros(rows, self.width, dtype=torch.int64, device=dev)
+        if stage.is_first:
+            self.inp = torch.zeros(rows, 1, dtype=torch.int64, device=dev)
+        else:
+            self.inp = torch.zeros(rows, 1, stage.cfg.d_model, dtype=stage.dtype, device=dev)
+        self.stream = torch.cuda.Stream(dev)
+        self.graph: Optional[torch.cuda.CUDAGraph] = None
+        self.out: Optional[torch.Tensor] = None
+
+    def _step(self) -> torch.Tensor:
+        st = self.stage
+        x = st.embed(self.inp) if st.is_first else self.inp
+        st.run_layers_(x, self.pos, self.pool.views(self.tab, self.pos))
+        return ops.argmax(st.head(x[:, -1:])[:, -1]) if st.is_last else x
+
+    def run(self, positions: torch.Tensor, tables: torch.Tensor, inp: torch.Tensor) -> torch.Tensor:
+        """The group's step on the current stream: its tokens (last stage) or output activations, in a new
+        tensor."""
+        self.pos.copy_(positions)
+        self.tab.zero_()
+        self.tab[:, : tables.shape[1]].copy_(tables)
+        self.inp.copy_(inp.view(self.inp.shape))
+        if self.graph is not None:
+            self.graph.replay()
+            return self.out.clone()
+        cur = torch.cuda.current_stream(self.stage.device)
+        self.stream.wait_stream(cur)
+        with torch.cuda.stream(self.stream):
+            out = self._step().clone()
+        self.stream.synchronize()
+        g = torch.cuda.CUDAGraph()
+        # thread-local capture: the process group's watchdog thread keeps polling its events meanwhile
+        with torch.cuda.graph(g, stream=self.stream, capture_error_mode="thread_local"):
+            self.out = self._step()
+        self.graph = g
+        cur.wait_stream(self.stream)
+        return out
 
 
 class PipelineEngine(Scheduler):
@@ -35,12 +89,18 @@ class PipelineEngine(Scheduler):
 
     prefill_chunks (extra): a prefill step pushes the prompt through the stages in up to this many pieces along the
     sequence (pipeline.seq_pieces), so the stages work on different pieces at once instead of taking turns; a
-    piece's keys and values of earlier positions are in the pool by the time it reaches a stage. Same tokens."""
+    piece's keys and values of earlier positions are in the pool by the time it reaches a stage. Same tokens.
+
+    cuda_graphs (extra, CUDA stages without tensor parallelism): inside decode windows each row group's step on a
+    stage replays a captured CUDA graph (_StageDecodeGraph, one per group size) instead of launching every kernel
+    from Python; the same kernels, so the same tokens."""
 
     MAX_WINDOW = 64     # decode steps per window: bounds what the host enqueues ahead of the GPUs
+    MAX_GRAPHS = 4
 
     def __init__(self, stage, num_blocks: int, block_size: int = 16, max_batch: int = 8, seed: int = 0,
-                 microbatches: int = 1, overlap: Optional[bool] = None, prefill_chunks: int = 1):
+                 microbatches: int = 1, overlap: Optional[bool] = None, prefill_chunks: int = 1,
+                 cuda_graphs: bool = True):
         self.stage, self.cfg = stage, stage.cfg
         self.pool = PagedKVPool(self.cfg, num_blocks, block_size, tp=stage.tp, dtype=stage.dtype,
                                 device=stage.device, n_layers=len(stage.layers))
@@ -48,6 +108,8 @@ class PipelineEngine(Scheduler):
         self.overlap = overlap
         self.prefill_chunks = max(1, prefill_chunks)
         self.windows = 0          # decode windows taken by run()
+        self.cuda_graphs = cuda_graphs
+        self._graphs: Dict[int, _StageDecodeGraph] = {}
         # decode windows: each step's block tables and positions go to the device in one copy from a pinned slot of
         # its own (a copy from pageable memory would make the host wait for the stream at every group)
         self._ring: Optional[torch.Tensor] = None
@@ -111,6 +173,19 @@ class PipelineEngine(Scheduler):
     def _window_steps(self) -> int:
         return min(super()._window_steps(), self.MAX_WINDOW)
 
+    def _stage_graph(self, rows: int, tables: torch.Tensor) -> Optional[_StageDecodeGraph]:
+        st = self.stage
+        if not (self.cuda_graphs and st.device.type == "cuda" and st.tp.size == 1
+                and tables.shape[1] * self.pool.block_size <= self.cfg.max_seq_len + self.pool.block_size):
+            return None
+        g = self._graphs.pop(rows, None)
+        if g is None:
+            if len(self._graphs) >= self.MAX_GRAPHS:
+                self._graphs.pop(next(iter(self._graphs)))
+            g = _StageDecodeGraph(st, self.pool, rows)
+        self._graphs[rows] = g
+        return g
+
     def _plan_on_device(self, t: int, tables: torch.Tensor, positions: torch.Tensor):
         """Step t's tables (R, width) and positions (R, 1) on the stage's device, through pinned slot t."""
         if self.stage.device.type != "cuda":
@@ -165,20 +240,21 @@ class PipelineEngine(Scheduler):
                 if t != plan_t:
                     plan, plan_t = self._plan_on_device(t, *self._window_step(rows, cached, t, last=t == w - 1)), t
                 tables, positions = plan
-                views = self.pool.views(tables[grp], positions[grp])
-                pos = views[0].positions if views else positions[grp].to(dev)
-                if st.is_first:
-                    work, tb = tok_in.pop(k)
-                    work.wait()
-                    x = st.embed(tb.view(-1, 1))
+                work, inp = (tok_in if st.is_first else act_in).pop(k)
+                work.wait()
+                g = self._stage_graph(sizes[j], tables)
+                if g is not None:
+                    out = g.run(positions[grp], tables[grp], inp)
                 else:
-                    work, x = act_in.pop(k)
-                    work.wait()
-                st.run_layers_(x, pos, views)
+                    views = self.pool.views(tables[grp], positions[grp])
+                    pos = views[0].positions if views else positions[grp].to(dev)
+                    x = st.embed(inp.view(-1, 1)) if st.is_first else inp
+                    st.run_layers_(x, pos, views)
+                    out = self._argmax(st.head(x[:, -1:])[:, -1]) if st.is_last else x
                 if st.is_last:
-                    toks[t + 1, grp].copy_(self._argmax(st.head(x[:, -1:])[:, -1]))
+                    toks[t + 1, grp].copy_(out)
                 else:
-                    act_out[k] = x
+                    act_out[k] = out
         for work, _ in sends:
             work.wait()
         tr.broadcast(toks, src=p - 1)

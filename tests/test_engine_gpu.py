@@ -183,16 +183,16 @@ def engine_windows_worker(rank, size, cfg_dict, sd, requests, num_blocks, max_ba
     from forgeserve_b200 import PipelineEngine, PipelineStage, _lib
     cfg = ModelConfig(**cfg_dict)
     res = []
-    for overlap in (False, None):
+    for overlap, graphs in ((False, True), (None, True), (None, False)):
         stage = PipelineStage(cfg, rank, size)
         stage.load_from_full(sd)
         stage = stage.to(torch.bfloat16).eval()
         eng = PipelineEngine(stage, num_blocks=num_blocks, block_size=16, max_batch=max_batch,
-                             microbatches=microbatches, overlap=overlap)
+                             microbatches=microbatches, overlap=overlap, cuda_graphs=graphs)
         ids = [eng.add_request(p, n) for p, n in requests]
         out = eng.run()
         res.append(([out[i] for i in ids], eng.steps, eng.preemptions, eng.peak_running, eng.peak_blocks,
-                    eng.pool.allocator.num_free, eng.windows))
+                    eng.pool.allocator.num_free, eng.windows, len(eng._graphs)))
     return res, _lib.device_error(clear=True)
 
 
@@ -201,8 +201,9 @@ def engine_windows_worker(rank, size, cfg_dict, sd, requests, num_blocks, max_ba
 def test_nccl_pipeline_engine_decode_windows_match_stepping(microbatches):
     """PipelineEngine over NCCL ranks: decode windows (the token ring, no pipeline drain per step) give exactly the
     tokens, step and preemption counts and peaks of stepping one by one (bf16, head_dim 128: split-KV decode
-    attention and split-K GEMMs; the same row groups per step either way, so the logits are the same bits). The
-    20-block pool makes the scheduler preempt (twice), so windows also end before a grant that finds the pool empty."""
+    attention and split-K GEMMs; the same row groups per step either way, so the logits are the same bits), with
+    each group's step replayed from a CUDA graph and with every kernel launched from Python. The 20-block pool
+    makes the scheduler preempt (twice), so windows also end before a grant that finds the pool empty."""
     cfg = ModelConfig(vocab_size=512, d_model=512, n_layers=4, n_heads=4, n_kv_heads=2, max_seq_len=512)
     sd = O.test_model_weights(O.Cfg(**cfg.to_dict()), seed=11, scale=0.05)
     gen = torch.Generator().manual_seed(6)
@@ -210,10 +211,11 @@ def test_nccl_pipeline_engine_decode_windows_match_stepping(microbatches):
                 for n, k in ((9, 30), (130, 24), (40, 33), (75, 12), (20, 28), (61, 20))]
     res = run_distributed(engine_windows_worker, 2, cfg.to_dict(), sd, requests, 20, 5, microbatches,
                           backend="nccl", timeout=300)
-    for (stepwise, windowed), err in res:
+    for (stepwise, windowed, eager), err in res:
         assert err == 0
-        assert stepwise[6] == 0 and windowed[6] > 0
-        assert windowed[:6] == stepwise[:6]
+        assert stepwise[6] == 0 and windowed[6] > 0 and eager[6] > 0
+        assert windowed[:6] == stepwise[:6] and eager[:6] == stepwise[:6]
+        assert windowed[7] > 0 and eager[7] == 0                      # graphs replayed only where enabled
         assert stepwise[2] > 0
     assert res[0][0][0][0] == res[1][0][0][0]
     assert len({t for out in res[0][0][0][0] for t in out}) > 5           # tokens vary
