@@ -501,6 +501,7 @@ int rope_kv_write(int dtype, void* qkv, int64_t ld, const float* cos_t, const fl
                   int64_t hd, int64_t slot_base, int slot_from_pos, int apply_rope, cudaStream_t st) {
   const int64_t tokens = B * T_new;
   if (tokens <= 0) return 0;
+  if (hd <= 0 || nh <= 0 || nkv <= 0) return fail("rope: head_dim and the head counts must be positive");
   if (hd % 2) return fail("rope: head_dim must be even");
   if (tokens > INT32_MAX) return fail("rope: too many tokens");
   const int th = 128;

@@ -83,3 +83,16 @@ def test_static_decode_refuses_a_call_beyond_its_fixed_scratch_on_the_host(lib):
                                         L.FS_BF16, None)
     assert rc == -1
     assert f"needs {need} bytes of scratch".encode() in lib.fs_last_error()
+
+
+def test_rope_refuses_non_positive_head_shapes_on_the_host(lib):
+    """A zero head_dim or head count is refused with a message before any device work (the vectorised path's
+    chunk arithmetic divides by head_dim / 16); the pointers below are never dereferenced."""
+    p = 4096
+    desc = L.KVCacheDesc(k=p, v=p, table=p, table_stride=4, table_cols=4, block_size=16, block_stride=2 * 16 * 128,
+                         head_stride=16 * 128, num_blocks=4)
+    for nh, nkv, hd in ((4, 2, 0), (0, 2, 128), (4, 0, 128)):
+        rc = lib.fs_rope_kv_write(ctypes.c_void_p(p), 1024, ctypes.c_void_p(p), ctypes.c_void_p(p), 64,
+                                  ctypes.c_void_p(p), ctypes.byref(desc), 1, 1, nh, nkv, hd, 0, 1, 1, L.FS_BF16, None)
+        assert rc == -1
+        assert b"must be positive" in lib.fs_last_error()
